@@ -1,0 +1,447 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 paged-KV write + paged attention path.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl nvllm|reference]
+                    [--workload decode|mixed|longctx]
+
+One step = one pass of the hot path over one batch: nvllm_reshape_and_cache of
+the step's new K/V rows, then nvllm_paged_attention (plan, split-K decode and
+merge kernels; the causal prefill kernel too for multi-row sequences). The
+default workload is the decode microbenchmark: 64 sequences, contexts
+U[512, 4096], 32 heads x head_dim 128, block size 16, 65536-block arena, fp32.
+
+Under torchrun each rank runs its own batch on its own GPU (sequence
+partitioning: no collective on the data path, weak scaling); the timed region
+is bracketed by a barrier and torch.cuda.synchronize(), timed with CUDA events
+on the launching stream, and the maximum over ranks is reported.
+
+``--impl reference`` times the reference's own CPU implementation of the path
+(TransformerModel::forward_batch's KV write + paged attention on its
+ThreadPool, built from the reference sources into oracle/_ref) on the host
+cores, for the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "nano-vllm-cpp26_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged-attn tokens/s + HBM GB/s (% peak) at 1/2/4/8 B200 vs host-CPU ref"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+KERNELS_PER_STEP = 4  # reshape_and_cache, plan, decode (+prefill if any), merge
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {}
+
+
+def profile_traffic(workload: str):
+    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / f"decode_attention_{workload}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.lines: list[str] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return self
+
+        def reader():
+            for line in self.proc.stdout:
+                self.lines.append(line.strip())
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        return self
+
+    def stop(self) -> dict:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() in ("active", "1"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# the reference CPU path
+
+
+def reference_time(spec, steps: int, warmup: int, budget_s: float | None = None,
+                   max_seqs: int | None = None) -> dict:
+    """Times the reference's forward_batch (KV write + paged attention; its
+    matmuls are answered by the harness) over a batch with the workload's
+    shape. The arena holds only the blocks the batch uses (its contents do not
+    change the work); tables keep a random permutation."""
+    from oracle.oracle import KVLayout, RefPath
+    ref = RefPath()
+    S = spec.num_seqs if max_seqs is None else min(spec.num_seqs, max_seqs)
+    ctx = spec.ctx_lens[:S]
+    ql = spec.q_lens[:S]
+    B = spec.block_size
+    nbs = (ctx + B - 1) // B
+    used = int(nbs.sum())
+    rng = np.random.Generator(np.random.PCG64(1234))
+    perm = rng.permutation(used)
+    bt = np.zeros((S, int(nbs.max())), np.int64)
+    off = 0
+    for s in range(S):
+        bt[s, :nbs[s]] = perm[off:off + nbs[s]]
+        off += int(nbs[s])
+    threads = os.cpu_count() or 1
+    lay = KVLayout(used, 1, B, spec.num_heads, spec.head_dim)
+    cache = ref.cache_create(lay)
+    eng = ref.engine_create(1, spec.num_heads, spec.head_dim, threads)
+    n = int(ql.sum())
+    D = spec.hidden
+    g = np.random.Generator(np.random.PCG64(7))
+    q = g.standard_normal((1, n, D), dtype=np.float32)
+    k = g.standard_normal((1, n, D), dtype=np.float32)
+    v = g.standard_normal((1, n, D), dtype=np.float32)
+    out = np.zeros((1, n, D), np.float32)
+    for _ in range(max(warmup, 0)):
+        ref.forward_attention(eng, cache, ql, ctx, bt, q, k, v, out)
+    times = []
+    t_start = time.perf_counter()
+    for i in range(steps):
+        t0 = time.perf_counter()
+        ref.forward_attention(eng, cache, ql, ctx, bt, q, k, v, out)
+        times.append(time.perf_counter() - t0)
+        if budget_s is not None and time.perf_counter() - t_start > budget_s and i >= 1:
+            break
+    ref.cache_destroy(cache)
+    avg = sum(times) / len(times)
+    kv = int(ctx.astype(np.int64).sum()) * D * 8
+    return {"seconds_per_step": avg, "steps": len(times), "tokens_per_step": n,
+            "tokens_per_s": n / avg, "kv_gbs": kv / avg / 1e9, "threads": threads,
+            "num_seqs": S, "arena_blocks": used}
+
+
+def reference_main(args, spec):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle.oracle import reference_available
+    if not reference_available():
+        print(json.dumps({"impl": "reference", "metric": METRIC,
+                          "unavailable": "oracle/_ref (the reference's C++ built from its sources) "
+                                         "is not present on this machine"}))
+        return 0
+    # Each step is the full batch unless that would exceed the time budget.
+    probe = reference_time(spec, steps=1, warmup=0)
+    per = probe["seconds_per_step"]
+    max_seqs = None
+    budget = 150.0
+    if per * (args.steps + args.warmup) > budget:
+        frac = budget / (per * (args.steps + args.warmup))
+        max_seqs = max(1, int(spec.num_seqs * frac))
+    r = reference_time(spec, steps=args.steps, warmup=args.warmup, max_seqs=max_seqs)
+    sample = (f"{r['num_seqs']} of {spec.num_seqs} sequences per step, full contexts, "
+              f"{r['steps']} timed steps; arena of the {r['arena_blocks']} blocks the batch uses")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": r["tokens_per_s"], "unit": UNIT,
+        "n_gpus": args.gpus, "steps": r["steps"], "warmup": args.warmup,
+        "ms_per_step": r["seconds_per_step"] * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": workload_config(spec),
+        "cpu_baseline": {"value": r["tokens_per_s"], "unit": UNIT, "cores": r["threads"],
+                         "kind": "reference", "sample": sample, "kv_gbs": r["kv_gbs"]},
+        "e2e": {"value": r["tokens_per_s"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def workload_config(spec) -> dict:
+    return {"workload": {"decode": "decode paged attention (64 seqs, ctx U[512,4096])",
+                         "mixed": "mixed prefill+decode super-batch (8 prefills U[512,2048] "
+                                  "+ 120 decodes ctx U[256,8192])",
+                         "longctx": "long-context decode (4 seqs x 32768 ctx)"}[spec.name],
+            "num_seqs": spec.num_seqs, "num_heads": spec.num_heads, "head_dim": spec.head_dim,
+            "block_size": spec.block_size, "arena_blocks": spec.num_blocks,
+            "new_tokens_per_step": spec.n_tokens,
+            "mean_context": float(spec.ctx_lens.mean()),
+            "kv_bytes_per_step": spec.kv_bytes(),
+            "l2": "inputs larger than L2 (KV read per step >> 126 MB), no flush"}
+
+
+# ---------------------------------------------------------------------------
+# the nvllm path
+
+
+def nvllm_main(args, spec):
+    import torch
+    import nvllm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    nvllm.lib()  # fails loudly when the CUDA library is missing
+
+    # per-rank batch: sequence partitioning gives every GPU its own sequences
+    if rank != 0:
+        from nvllm.workload import make_batch
+        spec = make_batch(args.workload, seed=args.seed + rank)
+    lay = nvllm.KVLayout(spec.num_blocks, 1, spec.block_size, spec.num_heads, spec.head_dim)
+    D = spec.hidden
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    ka = torch.empty(lay.arena_shape(), dtype=torch.float32, device=dev).normal_(generator=gen)
+    va = torch.empty_like(ka).normal_(generator=gen)
+    n = spec.n_tokens
+    q = torch.randn((n, D), generator=gen, device=dev)
+    k = torch.randn((n, D), generator=gen, device=dev)
+    v = torch.randn((n, D), generator=gen, device=dev)
+    out = torch.empty_like(q)
+    bt = torch.from_numpy(spec.block_tables).to(dev)
+    cu = torch.from_numpy(spec.cu_seqlens_q).to(dev)
+    ctx = torch.from_numpy(spec.ctx_lens).to(dev)
+    slots = torch.from_numpy(spec.slot_mapping()).to(dev)
+    max_q = int(spec.q_lens.max())
+    max_ctx = int(spec.ctx_lens.max())
+    ws = nvllm.alloc_workspace(spec.num_seqs, max_q, max_ctx, lay, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        nvllm.reshape_and_cache(k, v, ka, va, slots, 0, lay, stream=stream)
+        nvllm.paged_attention(out, q, ka, va, bt, cu, ctx, max_q, max_ctx, 0, lay,
+                              workspace=ws, stream=stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(local).start()
+
+    # ---- device-resident throughput --------------------------------------
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    if nvllm.get_last_error(stream) != nvllm.OK:
+        raise RuntimeError("device status after warm-up is not OK")
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    # per-step attention timing (events bracket the attention call only)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    e0.record(stream)
+    for i in range(args.steps):
+        nvllm.reshape_and_cache(k, v, ka, va, slots, 0, lay, stream=stream)
+        ev[i][0].record(stream)
+        nvllm.paged_attention(out, q, ka, va, bt, cu, ctx, max_q, max_ctx, 0, lay,
+                              workspace=ws, stream=stream)
+        ev[i][1].record(stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    attn_s = sum(a.elapsed_time(b) for a, b in ev) / 1e3 / args.steps
+    elapsed_max = max_over_ranks(elapsed)
+    attn_max = max_over_ranks(attn_s)
+
+    # ---- end to end through the C ABI with host buffers -----------------
+    h_q = torch.empty((n, D), dtype=torch.float32, pin_memory=True).copy_(q)
+    h_k = torch.empty_like(h_q, pin_memory=True).copy_(k)
+    h_v = torch.empty_like(h_q, pin_memory=True).copy_(v)
+    h_out = torch.empty_like(h_q, pin_memory=True)
+    h_meta = [torch.from_numpy(x).pin_memory() for x in
+              (spec.block_tables, spec.cu_seqlens_q, spec.ctx_lens, spec.slot_mapping())]
+    d_meta = [bt, cu, ctx, slots]
+    h2d = sum(t.numel() * t.element_size() for t in [h_q, h_k, h_v, *h_meta])
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        q.copy_(h_q, non_blocking=True)
+        k.copy_(h_k, non_blocking=True)
+        v.copy_(h_v, non_blocking=True)
+        for d_, h_ in zip(d_meta, h_meta):
+            d_.copy_(h_, non_blocking=True)
+        step()
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_elapsed = max_over_ranks(f0.elapsed_time(f1) / 1e3)
+    clocks = sampler.stop()
+    status = nvllm.get_last_error(stream)
+    if status != nvllm.OK:
+        raise RuntimeError(f"device status {nvllm.status_string(status)}")
+
+    tokens = n * args.steps * world
+    value = tokens / elapsed_max
+    e2e_value = tokens / e2e_elapsed
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs")
+    peak_src = "measured" if peak else "fallback"
+    if not peak:
+        peak = FALLBACK_HBM_GBS
+    alg_bytes = spec.decode_algorithmic_bytes()
+    achieved = alg_bytes / attn_max / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic", "config": {**workload_config(spec),
+                                        "parallelism": f"sequence-partitioned x{world}"},
+        "hbm_gbs": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_src,
+                     "kernel": "nvllm_paged_attention (plan + split-K decode + merge)",
+                     "algorithmic_bytes_per_launch": alg_bytes,
+                     "ms_per_launch": attn_max * 1e3,
+                     "traffic": profile_traffic(spec.name)},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": KERNELS_PER_STEP * args.steps * 2 + (args.steps if max_q > 1 else 0) * 2,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.oracle import reference_available
+        try:
+            if reference_available():
+                r = reference_time(spec, steps=50, warmup=1, budget_s=12.0)
+                kind = "reference"
+            else:
+                r = None
+                kind = None
+            if r is not None:
+                line["cpu_baseline"] = {
+                    "value": r["tokens_per_s"], "unit": UNIT, "cores": r["threads"],
+                    "kind": kind,
+                    "sample": f"{r['steps']} calls of the full {r['num_seqs']}-sequence batch "
+                              f"(~12 s of CPU work); KV {r['kv_gbs']:.1f} GB/s"}
+            else:
+                line["cpu_baseline"] = None
+        except Exception as exc:  # reported, never fatal
+            line["cpu_baseline"] = {"error": str(exc)}
+    if rank == 0:
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["nvllm", "reference"], default="nvllm")
+    ap.add_argument("--workload", choices=["decode", "mixed", "longctx"], default="decode")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warm-up raised to 3 steps")
+        args.warmup = 3
+    from nvllm.workload import make_batch
+    spec = make_batch(args.workload, seed=args.seed)
+    if args.impl == "reference":
+        return reference_main(args, spec)
+    return nvllm_main(args, spec)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,108 @@
+/*
+ * nvllm — B200 (sm_100a) paged-KV write + paged attention for nano-vllm-cpp26.
+ *
+ * C ABI of libnvllm.so. All tensors are fp32 device pointers owned by the
+ * caller; every call is asynchronous on the caller's CUDA stream (passed as
+ * void*, i.e. a cudaStream_t; NULL = legacy default stream) and allocates
+ * nothing. Return value: NVLLM_OK or one of the NVLLM_ERR_* codes below.
+ *
+ * Geometry follows the reference's PagedKVCache: one K and one V arena of
+ * [num_blocks, num_layers, block_size, num_heads * head_dim] floats
+ * (include/nano_vllm/kv_cache.hpp:30-33), i.e. row (block, layer, slot) holds
+ * all heads of one token, head h at columns [h * head_dim, (h + 1) * head_dim).
+ *
+ * Flattened batch: the query/key/value rows of one step are the uncomputed
+ * tokens of every scheduled sequence, sequence-major (src/model.cpp:138-159).
+ * Sequence s owns rows [cu_seqlens_q[s], cu_seqlens_q[s+1]) and, after this
+ * step's cache write, context_lens[s] cached positions; its query row i is at
+ * position context_lens[s] - q_len + i and attends causally to positions
+ * 0..pos through row s of block_tables ([num_seqs, max_blocks_per_seq] int32
+ * physical block ids, the reference's SequenceState::block_table).
+ */
+#ifndef NVLLM_H
+#define NVLLM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum nvllm_status {
+    NVLLM_OK = 0,
+    NVLLM_ERR_INVALID = 1,     /* bad argument, geometry or metadata */
+    NVLLM_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed */
+    NVLLM_ERR_TIMEOUT = 3,     /* a bounded device wait gave up */
+    NVLLM_ERR_BOUNDS = 4,      /* a block id / slot outside the arena was skipped */
+    NVLLM_ERR_WORKSPACE = 5,   /* workspace missing or smaller than required */
+    NVLLM_ERR_UNSUPPORTED = 6  /* head_dim or precision not built */
+};
+
+enum nvllm_precision {
+    NVLLM_PRECISION_FP32 = 0,  /* fp32 FFMA everywhere (max-abs 2e-5 vs the reference) */
+    NVLLM_PRECISION_TF32 = 1   /* prefill QK^T / PV tiles on tcgen05 kind::tf32 (1e-3) */
+};
+
+typedef struct nvllm_kv_layout {
+    int64_t num_blocks;
+    int32_t num_layers;
+    int32_t block_size;
+    int32_t num_heads;
+    int32_t head_dim;  /* 32, 64, 128 or 256 */
+} nvllm_kv_layout;
+
+/*
+ * KV write of one layer for a batch. Replaces the per-token loop of
+ * PagedKVCache::write_kv calls at src/model.cpp:188-202 (write_kv itself:
+ * src/kv_cache.cpp:57-68). Row t of key/value ([num_tokens, H*hd]) is copied
+ * bit-exactly to arena row (slot_mapping[t] / B, layer, slot_mapping[t] % B);
+ * slot_mapping[t] = block_table[pos / B] * B + pos % B (src/model.cpp:192-194).
+ * A negative slot skips the token. A slot beyond the arena is skipped and
+ * raises NVLLM_ERR_BOUNDS in nvllm_get_last_error().
+ */
+int nvllm_reshape_and_cache(const float* key, const float* value, float* k_arena,
+                            float* v_arena, const int32_t* slot_mapping,
+                            int64_t num_tokens, int32_t layer,
+                            const nvllm_kv_layout* layout, void* stream);
+
+/* Bytes of device workspace nvllm_paged_attention needs for a batch of at
+ * most num_seqs sequences, max_query_len query rows and max_context_len
+ * cached positions per sequence. */
+size_t nvllm_paged_attention_workspace_size(int32_t num_seqs, int32_t max_query_len,
+                                            int32_t max_context_len,
+                                            const nvllm_kv_layout* layout);
+
+/*
+ * Causal paged attention with online softmax over one layer of the arena.
+ * Replaces step 3d of TransformerModel::forward_batch (src/model.cpp:204-260),
+ * including read_head_kv (src/kv_cache.cpp:70-81). query/out are
+ * [cu_seqlens_q[num_seqs], H*hd]. Sequences with one query row go to the
+ * split-K decode kernel, longer ones to the causal prefill kernel; both run
+ * in fp32 (precision selects the prefill tile arithmetic). max_query_len and
+ * max_context_len bound the per-sequence values (the kernels check them).
+ * scale is the softmax scale (the reference uses 1/sqrt(head_dim),
+ * src/model.cpp:205).
+ */
+int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
+                          const float* v_arena, const int32_t* block_tables,
+                          int32_t max_blocks_per_seq, const int32_t* cu_seqlens_q,
+                          const int32_t* context_lens, int32_t num_seqs,
+                          int32_t max_query_len, int32_t max_context_len, int32_t layer,
+                          float scale, int32_t precision, void* workspace,
+                          size_t workspace_bytes, const nvllm_kv_layout* layout,
+                          void* stream);
+
+/* Synchronizes the stream, then returns (and clears) the device status word
+ * of the current device that the kernels set on skipped out-of-range accesses,
+ * inconsistent metadata or bounded waits that gave up. The reference has
+ * assert()s for these (src/kv_cache.cpp:50-51, :63-64). */
+int nvllm_get_last_error(void* stream);
+
+/* Static string for a status code. */
+const char* nvllm_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NVLLM_H */

@@ -1,0 +1,462 @@
+// K0 plan + K2 split-K paged decode attention + merge (sm_100a).
+//
+// Replaces step 3d of TransformerModel::forward_batch (src/model.cpp:204-260)
+// for sequences with one query row. For token t of sequence s at position
+// p = ctx - 1 and head h the reference walks the block table
+// (:225-253): score = (q . k) * scale, online max / sum rescaling, V
+// accumulation, then out /= max(sum, 1e-12) (:255-258).
+//
+// B200 design (HBM-bound, ~0.25 FLOP/byte):
+//  * The context of each (sequence, head) is cut into items of P positions
+//    (decode_split_tokens); a persistent grid of warps pulls
+//    (item, head) pairs from a global cursor, so every SM streams until the
+//    whole batch is done and ragged contexts balance themselves.
+//  * Each warp owns a ring of NS shared-memory stages. A stage holds one chunk
+//    of T = 2048 / hd consecutive positions: its K rows and V rows arrive by
+//    bulk asynchronous copies (TMA engine, cp.async.bulk, one row of hd floats
+//    each -- a row is contiguous in the arena) completing on the stage's
+//    mbarrier. Rows are padded by 16 bytes in shared memory so both the
+//    row-per-lane QK^T reads and the column-per-lane PV reads are free of bank
+//    conflicts.
+//  * QK^T: each lane computes full 64-dim partial dots of one row (two lanes
+//    per row for hd 128), one shuffle completes the dot. Softmax runs in the
+//    log2 domain (scores pre-multiplied by scale*log2 e, exp2f). PV: each lane
+//    owns 4 (or 8) output columns.
+//  * An item that covers the whole context writes the normalised output; other
+//    items write (m, l, acc) partials that the merge kernel combines with the
+//    usual max-rescaled sum.
+#include <cfloat>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace nvllm {
+
+__device__ uint32_t g_status = 0;
+
+namespace {
+
+template <int HD>
+struct DecodeShape {
+    static constexpr int T = 2048 / HD;                      // positions per chunk
+    static constexpr int ROW = HD + 4;                       // padded smem row (floats)
+    static constexpr int PPR = HD >= 128 ? HD / 64 : 1;      // QK lanes per row
+    static constexpr int RLANES = 32 / PPR;                  // rows covered per pass
+    static constexpr int RPL = T / RLANES;                   // rows per lane (QK)
+    static constexpr int DPP = HD / PPR;                     // dims per lane per row
+    static constexpr int G = HD >= 128 ? 32 : HD / 4;        // PV lanes per row
+    static constexpr int RG = 32 / G;                        // PV row groups
+    static constexpr int CPL = HD >= 256 ? HD / 128 : 1;     // float4 columns per lane
+    static constexpr int RPG = T / RG;                       // rows per PV group
+    static constexpr int COPY_FLOATS = HD < 128 ? HD : 128;  // one bulk copy
+    static constexpr int COPY_BYTES = COPY_FLOATS * 4;
+    static constexpr int CPR = HD / COPY_FLOATS;             // copies per row
+    static constexpr int NCOPIES = 2 * T * CPR;              // K + V copies per chunk
+    static constexpr int COPIES_PER_LANE = NCOPIES / 32;
+    static constexpr int STAGE_FLOATS = 2 * T * ROW + T;     // K, V, P
+    static_assert(NCOPIES % 32 == 0, "copy count must fill the warp");
+    static_assert(RPG % 4 == 0, "P reads are float4");
+    static_assert((STAGE_FLOATS * 4) % 16 == 0, "stage alignment");
+};
+
+constexpr int kBarBytes = 1024;  // mbarriers live in the first KiB of shared memory
+
+template <int HD, int NW, int NS>
+constexpr size_t decode_smem_bytes() {
+    return kBarBytes + size_t(NW) * NS * DecodeShape<HD>::STAGE_FLOATS * sizeof(float);
+}
+
+template <int HD, int NW, int NS>
+__global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const AttnParams p) {
+    using S = DecodeShape<HD>;
+    static_assert(NW * NS * 8 <= kBarBytes, "barrier area");
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw) + warp * NS;
+    float* wbuf = reinterpret_cast<float*>(smem_raw + kBarBytes) +
+                  size_t(warp) * NS * S::STAGE_FLOATS;
+
+    // Zero this warp's stages once: rows past the end of a chunk then always
+    // hold finite data (zeros or an earlier chunk), so their zero softmax
+    // weight cancels them exactly in PV.
+    for (int i = lane * 4; i < NS * S::STAGE_FLOATS; i += 128) {
+        *reinterpret_cast<float4*>(wbuf + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (lane == 0) {
+        for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
+    }
+    fence_barrier_init();
+    __syncwarp();
+
+    const uint64_t pol = l2_evict_first();
+    const ArenaGeom& g = p.g;
+    const int H = g.num_heads;
+    const int total = p.counters->decode_items * H;
+    const int part = lane / S::RLANES;
+    const int rl = lane % S::RLANES;
+    const int rg = lane / S::G;
+    const int cg = lane % S::G;
+    uint32_t chunk_seq = 0;  // chunks consumed by this warp so far (ring position)
+
+    for (;;) {
+        int it = 0;
+        if (lane == 0) it = atomicAdd(&p.counters->decode_next, 1);
+        it = __shfl_sync(0xffffffffu, it, 0);
+        if (it >= total) break;
+        const WorkItem wi = p.decode_items[it / H];
+        const int h = it % H;
+        const int s = wi.seq;
+        const int ctx = p.context_lens[s];
+        const int pos0 = wi.part * p.split_tokens;
+        const int pos1 = min(pos0 + p.split_tokens, ctx);
+        const int nchunks = (pos1 - pos0 + S::T - 1) / S::T;
+        const int tok = p.cu_seqlens_q[s];
+        const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
+        const int64_t head_off = int64_t(p.layer) * g.layer_stride + int64_t(h) * HD;
+
+        float4 qv[S::DPP / 4];
+        {
+            const float4* qp = reinterpret_cast<const float4*>(p.q + int64_t(tok) * g.row +
+                                                               int64_t(h) * HD + part * S::DPP);
+#pragma unroll
+            for (int i = 0; i < S::DPP / 4; ++i) qv[i] = __ldg(qp + i);
+        }
+
+        auto issue = [&](int c, int stage) {
+            float* sK = wbuf + stage * S::STAGE_FLOATS;
+            float* sV = sK + S::T * S::ROW;
+            const int cpos = pos0 + c * S::T;
+            const int nvalid = min(S::T, pos1 - cpos);
+            const float* src[S::COPIES_PER_LANE];
+            float* dst[S::COPIES_PER_LANE];
+            bool ok[S::COPIES_PER_LANE];
+            uint32_t bytes = 0;
+#pragma unroll
+            for (int k = 0; k < S::COPIES_PER_LANE; ++k) {
+                const int ci = lane + 32 * k;
+                const int tensor = ci / (S::T * S::CPR);
+                const int rem = ci % (S::T * S::CPR);
+                const int row = rem / S::CPR;
+                const int piece = rem % S::CPR;
+                const int pos = cpos + row;
+                ok[k] = row < nvalid;
+                int64_t blk = 0;
+                if (ok[k]) {
+                    blk = table[pos / g.block_size];
+                    if (blk < 0 || blk >= g.num_blocks) {
+                        ok[k] = false;
+                        raise_status(kStatusBounds);
+                    }
+                }
+                const int64_t off = blk * g.block_stride + head_off +
+                                    int64_t(pos % g.block_size) * g.row + piece * S::COPY_FLOATS;
+                src[k] = (tensor ? p.v_arena : p.k_arena) + off;
+                dst[k] = (tensor ? sV : sK) + row * S::ROW + piece * S::COPY_FLOATS;
+                bytes += ok[k] ? S::COPY_BYTES : 0u;
+            }
+            bytes = __reduce_add_sync(0xffffffffu, bytes);
+            if (lane == 0) mbar_arrive_expect_tx(&bars[stage], bytes);
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < S::COPIES_PER_LANE; ++k) {
+                if (ok[k]) bulk_copy_g2s(dst[k], src[k], S::COPY_BYTES, &bars[stage], pol);
+            }
+        };
+
+        const int prologue = min(NS, nchunks);
+        for (int c = 0; c < prologue; ++c) issue(c, int((chunk_seq + c) % NS));
+
+        float m_run = -INFINITY;
+        float l_run = 0.f;
+        float4 acc[S::CPL];
+#pragma unroll
+        for (int c = 0; c < S::CPL; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+        bool timed_out = false;
+        int c = 0;
+        for (; c < nchunks; ++c) {
+            const uint32_t n = chunk_seq + c;
+            const int stage = int(n % NS);
+            if (!mbar_wait(&bars[stage], (n / NS) & 1u)) {
+                timed_out = true;
+                break;
+            }
+            const float* sK = wbuf + stage * S::STAGE_FLOATS;
+            const float* sV = sK + S::T * S::ROW;
+            float* sP = const_cast<float*>(sV) + S::T * S::ROW;
+            const int nvalid = min(S::T, pos1 - (pos0 + c * S::T));
+
+            // scores of this chunk (log2 domain)
+            float sc[S::RPL];
+#pragma unroll
+            for (int k = 0; k < S::RPL; ++k) {
+                const int r = rl + k * S::RLANES;
+                const float* kr = sK + r * S::ROW + part * S::DPP;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+                for (int i = 0; i < S::DPP / 4; ++i) {
+                    const float4 kv = ld_shared4(kr + 4 * i);
+                    a0 = fmaf(qv[i].x, kv.x, a0);
+                    a1 = fmaf(qv[i].y, kv.y, a1);
+                    a2 = fmaf(qv[i].z, kv.z, a2);
+                    a3 = fmaf(qv[i].w, kv.w, a3);
+                }
+                float d = (a0 + a1) + (a2 + a3);
+#pragma unroll
+                for (int o = S::RLANES; o < 32; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                sc[k] = r < nvalid ? d * p.qk_scale_log2 : -INFINITY;
+            }
+            float cm = sc[0];
+#pragma unroll
+            for (int k = 1; k < S::RPL; ++k) cm = fmaxf(cm, sc[k]);
+            cm = warp_max_xor(cm, S::RLANES);
+            const float m_new = fmaxf(m_run, cm);
+            const float alpha = exp2f(m_run - m_new);
+            float psum = 0.f;
+#pragma unroll
+            for (int k = 0; k < S::RPL; ++k) {
+                const float pk = exp2f(sc[k] - m_new);
+                psum += pk;
+                if (part == 0) {
+                    const int r = rl + k * S::RLANES;
+                    sP[(r % S::RG) * S::RPG + r / S::RG] = pk;
+                }
+            }
+            l_run = fmaf(l_run, alpha, psum);
+            __syncwarp();
+#pragma unroll
+            for (int cc = 0; cc < S::CPL; ++cc) {
+                acc[cc].x *= alpha;
+                acc[cc].y *= alpha;
+                acc[cc].z *= alpha;
+                acc[cc].w *= alpha;
+            }
+#pragma unroll
+            for (int i4 = 0; i4 < S::RPG / 4; ++i4) {
+                const float4 pp = ld_shared4(sP + rg * S::RPG + 4 * i4);
+                const float pj[4] = {pp.x, pp.y, pp.z, pp.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int r = rg + S::RG * (4 * i4 + j);
+#pragma unroll
+                    for (int cc = 0; cc < S::CPL; ++cc) {
+                        const float4 vv = ld_shared4(sV + r * S::ROW + (cg + 32 * cc) * 4);
+                        acc[cc].x = fmaf(pj[j], vv.x, acc[cc].x);
+                        acc[cc].y = fmaf(pj[j], vv.y, acc[cc].y);
+                        acc[cc].z = fmaf(pj[j], vv.z, acc[cc].z);
+                        acc[cc].w = fmaf(pj[j], vv.w, acc[cc].w);
+                    }
+                }
+            }
+            m_run = m_new;
+            __syncwarp();
+            if (c + NS < nchunks) issue(c + NS, stage);
+        }
+        if (timed_out) {
+            // Let the copies this warp still has in flight land (bounded), then stop.
+            const int last = min(nchunks, c + NS);
+            for (int cc = c + 1; cc < last; ++cc) {
+                const uint32_t n = chunk_seq + cc;
+                mbar_wait(&bars[n % NS], (n / NS) & 1u);
+            }
+            return;
+        }
+        chunk_seq += nchunks;
+
+        // epilogue
+        const float l_tot = warp_sum_xor(l_run, S::RLANES);
+#pragma unroll
+        for (int o = S::G; o < 32; o <<= 1) {
+#pragma unroll
+            for (int cc = 0; cc < S::CPL; ++cc) {
+                acc[cc].x += __shfl_xor_sync(0xffffffffu, acc[cc].x, o);
+                acc[cc].y += __shfl_xor_sync(0xffffffffu, acc[cc].y, o);
+                acc[cc].z += __shfl_xor_sync(0xffffffffu, acc[cc].z, o);
+                acc[cc].w += __shfl_xor_sync(0xffffffffu, acc[cc].w, o);
+            }
+        }
+        const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+        if (rg == 0) {
+            if (nsplit == 1) {
+                const float inv = 1.0f / fmaxf(l_tot, 1e-12f);
+                float* op = p.out + int64_t(tok) * g.row + int64_t(h) * HD;
+#pragma unroll
+                for (int cc = 0; cc < S::CPL; ++cc) {
+                    const float4 v = make_float4(acc[cc].x * inv, acc[cc].y * inv,
+                                                 acc[cc].z * inv, acc[cc].w * inv);
+                    reinterpret_cast<float4*>(op)[cg + 32 * cc] = v;
+                }
+            } else {
+                const int64_t pi = (int64_t(s) * H + h) * p.max_splits + wi.part;
+                float* ap = p.part_acc + pi * HD;
+#pragma unroll
+                for (int cc = 0; cc < S::CPL; ++cc) reinterpret_cast<float4*>(ap)[cg + 32 * cc] = acc[cc];
+                if (lane == 0) p.part_ml[pi] = make_float2(m_run, l_tot);
+            }
+        }
+    }
+}
+
+// Combines the split partials of each (decode sequence, head):
+// M = max m_j, L = sum l_j 2^(m_j - M), out = sum acc_j 2^(m_j - M) / L.
+template <int HD>
+__global__ void __launch_bounds__(256) merge_kernel(const AttnParams p) {
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int H = p.g.num_heads;
+    if (gw >= p.num_seqs * H) return;
+    const int s = gw / H;
+    const int h = gw % H;
+    const int q0 = p.cu_seqlens_q[s];
+    if (p.cu_seqlens_q[s + 1] - q0 != 1) return;
+    const int ctx = p.context_lens[s];
+    if (ctx < 1 || ctx > p.max_context_len) return;
+    const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+    if (nsplit <= 1) return;
+    const int64_t pbase = (int64_t(s) * H + h) * p.max_splits;
+    float M = -INFINITY;
+    for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, p.part_ml[pbase + j].x);
+    M = warp_max_xor(M, 32);
+    float L = 0.f;
+    for (int j = lane; j < nsplit; j += 32) {
+        const float2 ml = p.part_ml[pbase + j];
+        L += ml.y * exp2f(ml.x - M);
+    }
+    L = warp_sum_xor(L, 32);
+    const float inv = 1.0f / fmaxf(L, 1e-12f);
+    constexpr int PER_LANE = HD / 32;
+    float o[PER_LANE];
+#pragma unroll
+    for (int k = 0; k < PER_LANE; ++k) o[k] = 0.f;
+    for (int j = 0; j < nsplit; ++j) {
+        const float w = exp2f(p.part_ml[pbase + j].x - M);
+        const float* ap = p.part_acc + (pbase + j) * HD;
+#pragma unroll
+        for (int k = 0; k < PER_LANE; ++k) o[k] = fmaf(w, ap[lane + 32 * k], o[k]);
+    }
+    float* op = p.out + int64_t(q0) * p.g.row + int64_t(h) * HD;
+#pragma unroll
+    for (int k = 0; k < PER_LANE; ++k) op[lane + 32 * k] = o[k] * inv;
+}
+
+// Builds the decode and prefill work lists from the batch metadata (one CTA).
+constexpr int kPlanThreads = 1024;
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int& total) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < (kPlanThreads / 32) ? warp_tot[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        warp_tot[lane] = w;  // inclusive warp prefix
+    }
+    __syncthreads();
+    const int before = (warp > 0 ? warp_tot[warp - 1] : 0) + x - v;
+    total = warp_tot[kPlanThreads / 32 - 1];
+    __syncthreads();
+    return before;
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const AttnParams p) {
+    __shared__ int warp_tot[32];
+    int run_d = 0, run_p = 0;
+    const int B = p.g.block_size;
+    for (int base = 0; base < p.num_seqs; base += kPlanThreads) {
+        const int s = base + threadIdx.x;
+        int nd = 0, np = 0;
+        if (s < p.num_seqs) {
+            const int q0 = p.cu_seqlens_q[s];
+            const int qlen = p.cu_seqlens_q[s + 1] - q0;
+            const int ctx = p.context_lens[s];
+            const bool ok = q0 >= 0 && qlen >= 0 && qlen <= ctx && qlen <= p.max_query_len &&
+                            ctx <= p.max_context_len &&
+                            int64_t(ctx) <= int64_t(p.max_blocks) * B;
+            if (!ok) {
+                raise_status(kStatusMetadata);
+            } else if (qlen == 1) {
+                nd = (ctx + p.split_tokens - 1) / p.split_tokens;
+            } else if (qlen > 1) {
+                np = (qlen + p.prefill_tile - 1) / p.prefill_tile;
+            }
+        }
+        int tot_d = 0, tot_p = 0;
+        const int off_d = block_exclusive_scan(nd, warp_tot, tot_d);
+        const int off_p = block_exclusive_scan(np, warp_tot, tot_p);
+        for (int j = 0; j < nd; ++j) p.decode_items[run_d + off_d + j] = WorkItem{s, j};
+        // Prefill tiles of a sequence go out last-tile first (they see the most keys).
+        for (int j = 0; j < np; ++j) p.prefill_items[run_p + off_p + j] = WorkItem{s, np - 1 - j};
+        run_d += tot_d;
+        run_p += tot_p;
+    }
+    if (threadIdx.x == 0) {
+        p.counters->decode_next = 0;
+        p.counters->decode_items = run_d;
+        p.counters->prefill_next = 0;
+        p.counters->prefill_items = run_p;
+    }
+}
+
+template <int HD, int NW, int NS>
+cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream) {
+    constexpr size_t smem = decode_smem_bytes<HD, NW, NS>();
+    static int grid_per_device[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (grid_per_device[dev] == 0) {
+        e = cudaFuncSetAttribute(decode_kernel<HD, NW, NS>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        int sms = 0, per_sm = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel<HD, NW, NS>,
+                                                          NW * 32, smem);
+        if (e != cudaSuccess) return e;
+        grid_per_device[dev] = sms * (per_sm > 0 ? per_sm : 1);
+    }
+    decode_kernel<HD, NW, NS><<<grid_per_device[dev], NW * 32, smem, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int warps = p.num_seqs * p.g.num_heads;
+    merge_kernel<HD><<<(warps + 7) / 8, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int32_t decode_split_tokens(int32_t head_dim) {
+    // 16 chunks of 2048/hd positions: 256 KiB of K+V per item at any head_dim.
+    return 16 * (2048 / head_dim);
+}
+
+cudaError_t launch_plan(const AttnParams& p, cudaStream_t stream) {
+    plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream) {
+    switch (p.g.head_dim) {
+        case 32: return launch_decode_t<32, 4, 3>(p, stream);
+        case 64: return launch_decode_t<64, 4, 3>(p, stream);
+        case 128: return launch_decode_t<128, 4, 3>(p, stream);
+        case 256: return launch_decode_t<256, 4, 3>(p, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace nvllm
