@@ -8,20 +8,27 @@
 //
 // B200 design (HBM-bound, ~0.25 FLOP/byte):
 //  * The context of each (sequence, head) is cut into items of P positions
-//    (decode_split_tokens); a persistent grid of warps pulls
-//    (item, head) pairs from a global cursor, so every SM streams until the
-//    whole batch is done and ragged contexts balance themselves.
-//  * Each warp owns a ring of NS shared-memory stages. A stage holds one chunk
-//    of T = 2048 / hd consecutive positions: its K rows and V rows arrive by
-//    bulk asynchronous copies (TMA engine, cp.async.bulk, one row of hd floats
-//    each -- a row is contiguous in the arena) completing on the stage's
-//    mbarrier. Rows are padded by 16 bytes in shared memory so both the
-//    row-per-lane QK^T reads and the column-per-lane PV reads are free of bank
-//    conflicts.
-//  * QK^T: each lane computes full 64-dim partial dots of one row (two lanes
-//    per row for hd 128), one shuffle completes the dot. Softmax runs in the
-//    log2 domain (scores pre-multiplied by scale*log2 e, exp2f). PV: each lane
-//    owns 4 (or 8) output columns.
+//    (decode_split_tokens); a persistent grid of warps pulls (item, head)
+//    pairs from a global cursor, so every SM streams until the whole batch is
+//    done and ragged contexts balance themselves.
+//  * Each warp owns a ring of NS shared-memory stages and streams chunks of
+//    T = 2048 / hd consecutive positions through it without a bubble between
+//    items: while it computes item i it already fetches item i + 1's index and
+//    metadata and issues its first chunks. A chunk's K rows and V rows arrive
+//    by bulk asynchronous copies (TMA engine, cp.async.bulk, one arena row of
+//    hd floats each) completing on the stage's mbarrier; an item's Q row rides
+//    on its first chunk's barrier. With block size 16 at hd 128 a chunk is one
+//    physical block, so one block-table entry per chunk is held in a lane
+//    register for the whole item.
+//  * Rows are padded by 16 bytes in shared memory so both the row-per-lane
+//    QK^T reads and the column-per-lane PV reads are free of bank conflicts.
+//  * QK^T: each lane computes 64-dim partial dots of its rows (two lanes per
+//    row at hd 128), shuffles complete them. Softmax runs in the log2 domain
+//    (scores times scale*log2 e, exp2f). PV: each lane owns 4 (or 8) output
+//    columns.
+//  * Latency, not bandwidth, bounds a single warp (one chunk's dependent
+//    shuffle / exp / FMA chain), so a CTA holds several warps with shallow
+//    rings (NVLLM_DECODE_NW x NVLLM_DECODE_NS) rather than one deep ring.
 //  * An item that covers the whole context writes the normalised output; other
 //    items write (m, l, acc) partials that the merge kernel combines with the
 //    usual max-rescaled sum.
@@ -61,21 +68,64 @@ struct DecodeShape {
 
 constexpr int kBarBytes = 1024;  // mbarriers live in the first KiB of shared memory
 
-template <int HD, int NW, int NS>
-constexpr size_t decode_smem_bytes() {
-    return kBarBytes + size_t(NW) * NS * DecodeShape<HD>::STAGE_FLOATS * sizeof(float);
+// Per-warp shared memory: NS stages plus two Q rows (current / next item).
+template <int HD, int NS>
+constexpr size_t decode_warp_floats() {
+    return size_t(NS) * DecodeShape<HD>::STAGE_FLOATS + 2 * HD;
 }
 
 template <int HD, int NW, int NS>
+constexpr size_t decode_smem_bytes() {
+    return kBarBytes + size_t(NW) * decode_warp_floats<HD, NS>() * sizeof(float);
+}
+
+// One decode work item: positions [pos0, pos1) of head h of sequence s.
+struct DecodeItem {
+    int s;  // < 0: none
+    int h;
+    int part;
+    int pos0;
+    int pos1;
+    int nchunks;
+    int tok;
+    bool whole;  // covers the whole context: write the normalised output
+};
+
+template <int HD>
+__device__ __forceinline__ DecodeItem load_decode_item(const AttnParams& p, int it, int total) {
+    using S = DecodeShape<HD>;
+    DecodeItem d;
+    d.s = -1;
+    if (it >= total) return d;
+    const int H = p.g.num_heads;
+    const WorkItem wi = p.decode_items[it / H];
+    d.s = wi.seq;
+    d.h = it % H;
+    d.part = wi.part;
+    const int ctx = p.context_lens[d.s];
+    d.pos0 = wi.part * p.split_tokens;
+    d.pos1 = min(d.pos0 + p.split_tokens, ctx);
+    d.nchunks = (d.pos1 - d.pos0 + S::T - 1) / S::T;
+    d.tok = p.cu_seqlens_q[d.s];
+    d.whole = d.pos0 == 0 && d.pos1 == ctx;
+    return d;
+}
+
+// kB16: the arena's block size is 16 and equals the chunk (hd 128), so a chunk
+// is one physical block: one table entry per chunk, held in a lane register
+// for the whole item. Otherwise every row looks its block up.
+template <int HD, int NW, int NS, bool kB16>
 __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const AttnParams p) {
     using S = DecodeShape<HD>;
     static_assert(NW * NS * 8 <= kBarBytes, "barrier area");
+    static_assert(!kB16 || S::T == 16, "block-16 path needs 16-position chunks");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw) + warp * NS;
     float* wbuf = reinterpret_cast<float*>(smem_raw + kBarBytes) +
-                  size_t(warp) * NS * S::STAGE_FLOATS;
+                  size_t(warp) * decode_warp_floats<HD, NS>();
+    float* qbuf = wbuf + NS * S::STAGE_FLOATS;  // two Q rows
 
     // Zero this warp's stages once: rows past the end of a chunk then always
     // hold finite data (zeros or an earlier chunk), so their zero softmax
@@ -97,37 +147,52 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const AttnParams p) 
     const int rl = lane % S::RLANES;
     const int rg = lane / S::G;
     const int cg = lane % S::G;
-    uint32_t chunk_seq = 0;  // chunks consumed by this warp so far (ring position)
 
-    for (;;) {
-        int it = 0;
-        if (lane == 0) it = atomicAdd(&p.counters->decode_next, 1);
-        it = __shfl_sync(0xffffffffu, it, 0);
-        if (it >= total) break;
-        const WorkItem wi = p.decode_items[it / H];
-        const int h = it % H;
-        const int s = wi.seq;
-        const int ctx = p.context_lens[s];
-        const int pos0 = wi.part * p.split_tokens;
-        const int pos1 = min(pos0 + p.split_tokens, ctx);
-        const int nchunks = (pos1 - pos0 + S::T - 1) / S::T;
-        const int tok = p.cu_seqlens_q[s];
-        const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
-        const int64_t head_off = int64_t(p.layer) * g.layer_stride + int64_t(h) * HD;
+    auto fetch_index = [&]() {
+        int v = 0;
+        if (lane == 0) v = atomicAdd(&p.counters->decode_next, 1);
+        return __shfl_sync(0xffffffffu, v, 0);
+    };
+    auto table_of = [&](const DecodeItem& d) -> const int32_t* {
+        return p.block_tables + int64_t(d.s) * p.max_blocks;
+    };
+    // lane l holds the block id of chunk l of the item (block-16 path)
+    auto load_lane_block = [&](const DecodeItem& d) -> int {
+        if (!kB16 || lane >= d.nchunks) return 0;
+        return table_of(d)[d.pos0 / 16 + lane];
+    };
 
-        float4 qv[S::DPP / 4];
-        {
-            const float4* qp = reinterpret_cast<const float4*>(p.q + int64_t(tok) * g.row +
-                                                               int64_t(h) * HD + part * S::DPP);
-#pragma unroll
-            for (int i = 0; i < S::DPP / 4; ++i) qv[i] = __ldg(qp + i);
-        }
-
-        auto issue = [&](int c, int stage) {
-            float* sK = wbuf + stage * S::STAGE_FLOATS;
-            float* sV = sK + S::T * S::ROW;
-            const int cpos = pos0 + c * S::T;
-            const int nvalid = min(S::T, pos1 - cpos);
+    // Issue chunk c of item d into stage `stage`; the item's Q row rides on
+    // the first chunk's barrier.
+    auto issue = [&](const DecodeItem& d, int c, int stage, int lane_blk, int qslot) {
+        float* sK = wbuf + stage * S::STAGE_FLOATS;
+        float* sV = sK + S::T * S::ROW;
+        const int cpos = d.pos0 + c * S::T;
+        const int nvalid = min(S::T, d.pos1 - cpos);
+        const int64_t head_off = int64_t(p.layer) * g.layer_stride + int64_t(d.h) * HD;
+        const bool first = c == 0;
+        if constexpr (kB16) {
+            const int64_t blk = __shfl_sync(0xffffffffu, lane_blk, c);
+            const bool blk_ok = blk >= 0 && blk < g.num_blocks;
+            if (!blk_ok && lane == 0) raise_status(kStatusBounds);
+            const uint32_t bytes = (blk_ok ? uint32_t(nvalid) * HD * 4u * 2u : 0u) +
+                                   (first ? HD * 4u : 0u);
+            if (lane == 0) mbar_arrive_expect_tx(&bars[stage], bytes);
+            __syncwarp();
+            if (first && lane == 0) {
+                bulk_copy_g2s(qbuf + qslot * HD, p.q + int64_t(d.tok) * g.row + int64_t(d.h) * HD,
+                              HD * 4, &bars[stage], pol);
+            }
+            // lanes 0..15: K rows, lanes 16..31: V rows
+            const int tensor = lane / S::T;
+            const int row = lane % S::T;
+            if (blk_ok && row < nvalid) {
+                const int64_t off = blk * g.block_stride + head_off + int64_t(row) * g.row;
+                bulk_copy_g2s((tensor ? sV : sK) + row * S::ROW, (tensor ? p.v_arena : p.k_arena) + off,
+                              HD * 4, &bars[stage], pol);
+            }
+        } else {
+            const int32_t* table = table_of(d);
             const float* src[S::COPIES_PER_LANE];
             float* dst[S::COPIES_PER_LANE];
             bool ok[S::COPIES_PER_LANE];
@@ -155,145 +220,195 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const AttnParams p) 
                 dst[k] = (tensor ? sV : sK) + row * S::ROW + piece * S::COPY_FLOATS;
                 bytes += ok[k] ? S::COPY_BYTES : 0u;
             }
-            bytes = __reduce_add_sync(0xffffffffu, bytes);
+            bytes = __reduce_add_sync(0xffffffffu, bytes) + (first ? HD * 4u : 0u);
             if (lane == 0) mbar_arrive_expect_tx(&bars[stage], bytes);
             __syncwarp();
+            if (first && lane == 0) {
+                bulk_copy_g2s(qbuf + qslot * HD, p.q + int64_t(d.tok) * g.row + int64_t(d.h) * HD,
+                              HD * 4, &bars[stage], pol);
+            }
 #pragma unroll
             for (int k = 0; k < S::COPIES_PER_LANE; ++k) {
                 if (ok[k]) bulk_copy_g2s(dst[k], src[k], S::COPY_BYTES, &bars[stage], pol);
             }
-        };
-
-        const int prologue = min(NS, nchunks);
-        for (int c = 0; c < prologue; ++c) issue(c, int((chunk_seq + c) % NS));
-
-        float m_run = -INFINITY;
-        float l_run = 0.f;
-        float4 acc[S::CPL];
-#pragma unroll
-        for (int c = 0; c < S::CPL; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-
-        bool timed_out = false;
-        int c = 0;
-        for (; c < nchunks; ++c) {
-            const uint32_t n = chunk_seq + c;
-            const int stage = int(n % NS);
-            if (!mbar_wait(&bars[stage], (n / NS) & 1u)) {
-                timed_out = true;
-                break;
-            }
-            const float* sK = wbuf + stage * S::STAGE_FLOATS;
-            const float* sV = sK + S::T * S::ROW;
-            float* sP = const_cast<float*>(sV) + S::T * S::ROW;
-            const int nvalid = min(S::T, pos1 - (pos0 + c * S::T));
-
-            // scores of this chunk (log2 domain)
-            float sc[S::RPL];
-#pragma unroll
-            for (int k = 0; k < S::RPL; ++k) {
-                const int r = rl + k * S::RLANES;
-                const float* kr = sK + r * S::ROW + part * S::DPP;
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-                for (int i = 0; i < S::DPP / 4; ++i) {
-                    const float4 kv = ld_shared4(kr + 4 * i);
-                    a0 = fmaf(qv[i].x, kv.x, a0);
-                    a1 = fmaf(qv[i].y, kv.y, a1);
-                    a2 = fmaf(qv[i].z, kv.z, a2);
-                    a3 = fmaf(qv[i].w, kv.w, a3);
-                }
-                float d = (a0 + a1) + (a2 + a3);
-#pragma unroll
-                for (int o = S::RLANES; o < 32; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                sc[k] = r < nvalid ? d * p.qk_scale_log2 : -INFINITY;
-            }
-            float cm = sc[0];
-#pragma unroll
-            for (int k = 1; k < S::RPL; ++k) cm = fmaxf(cm, sc[k]);
-            cm = warp_max_xor(cm, S::RLANES);
-            const float m_new = fmaxf(m_run, cm);
-            const float alpha = exp2f(m_run - m_new);
-            float psum = 0.f;
-#pragma unroll
-            for (int k = 0; k < S::RPL; ++k) {
-                const float pk = exp2f(sc[k] - m_new);
-                psum += pk;
-                if (part == 0) {
-                    const int r = rl + k * S::RLANES;
-                    sP[(r % S::RG) * S::RPG + r / S::RG] = pk;
-                }
-            }
-            l_run = fmaf(l_run, alpha, psum);
-            __syncwarp();
-#pragma unroll
-            for (int cc = 0; cc < S::CPL; ++cc) {
-                acc[cc].x *= alpha;
-                acc[cc].y *= alpha;
-                acc[cc].z *= alpha;
-                acc[cc].w *= alpha;
-            }
-#pragma unroll
-            for (int i4 = 0; i4 < S::RPG / 4; ++i4) {
-                const float4 pp = ld_shared4(sP + rg * S::RPG + 4 * i4);
-                const float pj[4] = {pp.x, pp.y, pp.z, pp.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int r = rg + S::RG * (4 * i4 + j);
-#pragma unroll
-                    for (int cc = 0; cc < S::CPL; ++cc) {
-                        const float4 vv = ld_shared4(sV + r * S::ROW + (cg + 32 * cc) * 4);
-                        acc[cc].x = fmaf(pj[j], vv.x, acc[cc].x);
-                        acc[cc].y = fmaf(pj[j], vv.y, acc[cc].y);
-                        acc[cc].z = fmaf(pj[j], vv.z, acc[cc].z);
-                        acc[cc].w = fmaf(pj[j], vv.w, acc[cc].w);
-                    }
-                }
-            }
-            m_run = m_new;
-            __syncwarp();
-            if (c + NS < nchunks) issue(c + NS, stage);
         }
-        if (timed_out) {
-            // Let the copies this warp still has in flight land (bounded), then stop.
-            const int last = min(nchunks, c + NS);
-            for (int cc = c + 1; cc < last; ++cc) {
-                const uint32_t n = chunk_seq + cc;
-                mbar_wait(&bars[n % NS], (n / NS) & 1u);
+    };
+
+    // ---- streaming state ---------------------------------------------------
+    int next_it = fetch_index();
+    DecodeItem L = load_decode_item<HD>(p, next_it, total);  // item being issued
+    if (L.s < 0) return;
+    next_it = fetch_index();
+    int lane_blk = load_lane_block(L);
+    DecodeItem C = L;          // item being computed
+    bool c_live = true;        // C still has chunks to compute
+    bool ahead = false;        // L is the item after C
+    bool exhausted = false;    // no further items
+    int lc = 0;                // next chunk of L to issue
+    int cc = 0;                // next chunk of C to compute
+    uint32_t issued = 0, consumed = 0;
+    uint32_t l_index = 0, c_index = 0;  // items fetched / computed (Q slot parity)
+
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    float4 acc[S::CPL];
+#pragma unroll
+    for (int c = 0; c < S::CPL; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 qv[S::DPP / 4];
+
+    for (;;) {
+        // keep the ring full, running at most one item ahead of the compute
+        while (issued - consumed < uint32_t(NS)) {
+            if (lc == L.nchunks) {
+                if (ahead || exhausted) break;
+                const DecodeItem nx = load_decode_item<HD>(p, next_it, total);
+                if (nx.s < 0) {
+                    exhausted = true;
+                    break;
+                }
+                next_it = fetch_index();
+                L = nx;
+                lane_blk = load_lane_block(L);
+                lc = 0;
+                ++l_index;
+                if (c_live) {
+                    ahead = true;
+                } else {
+                    C = L;
+                    c_live = true;
+                }
             }
+            issue(L, lc, int(issued % NS), lane_blk, int(l_index & 1u));
+            ++lc;
+            ++issued;
+        }
+        if (consumed == issued) break;
+
+        const int stage = int(consumed % NS);
+        if (!mbar_wait(&bars[stage], (consumed / NS) & 1u)) {
+            // let this warp's other copies land (bounded), then stop
+            for (uint32_t n = consumed + 1; n < issued; ++n) mbar_wait(&bars[n % NS], (n / NS) & 1u);
             return;
         }
-        chunk_seq += nchunks;
+        if (cc == 0) {
+            const float4* qs = reinterpret_cast<const float4*>(qbuf + (c_index & 1u) * HD + part * S::DPP);
+#pragma unroll
+            for (int i = 0; i < S::DPP / 4; ++i) qv[i] = qs[i];
+        }
+        const float* sK = wbuf + stage * S::STAGE_FLOATS;
+        const float* sV = sK + S::T * S::ROW;
+        float* sP = const_cast<float*>(sV) + S::T * S::ROW;
+        const int nvalid = min(S::T, C.pos1 - (C.pos0 + cc * S::T));
 
-        // epilogue
+        // scores of this chunk (log2 domain)
+        float sc[S::RPL];
+#pragma unroll
+        for (int k = 0; k < S::RPL; ++k) {
+            const int r = rl + k * S::RLANES;
+            const float* kr = sK + r * S::ROW + part * S::DPP;
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+            for (int i = 0; i < S::DPP / 4; ++i) {
+                const float4 kv = ld_shared4(kr + 4 * i);
+                a0 = fmaf(qv[i].x, kv.x, a0);
+                a1 = fmaf(qv[i].y, kv.y, a1);
+                a2 = fmaf(qv[i].z, kv.z, a2);
+                a3 = fmaf(qv[i].w, kv.w, a3);
+            }
+            float d = (a0 + a1) + (a2 + a3);
+#pragma unroll
+            for (int o = S::RLANES; o < 32; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            sc[k] = r < nvalid ? d * p.qk_scale_log2 : -INFINITY;
+        }
+        float cm = sc[0];
+#pragma unroll
+        for (int k = 1; k < S::RPL; ++k) cm = fmaxf(cm, sc[k]);
+        cm = warp_max_xor(cm, S::RLANES);
+        const float m_new = fmaxf(m_run, cm);
+        const float alpha = exp2f(m_run - m_new);
+        float psum = 0.f;
+#pragma unroll
+        for (int k = 0; k < S::RPL; ++k) {
+            const float pk = exp2f(sc[k] - m_new);
+            psum += pk;
+            if (part == 0) {
+                const int r = rl + k * S::RLANES;
+                sP[(r % S::RG) * S::RPG + r / S::RG] = pk;
+            }
+        }
+        l_run = fmaf(l_run, alpha, psum);
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < S::CPL; ++c) {
+            acc[c].x *= alpha;
+            acc[c].y *= alpha;
+            acc[c].z *= alpha;
+            acc[c].w *= alpha;
+        }
+#pragma unroll
+        for (int i4 = 0; i4 < S::RPG / 4; ++i4) {
+            const float4 pp = ld_shared4(sP + rg * S::RPG + 4 * i4);
+            const float pj[4] = {pp.x, pp.y, pp.z, pp.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int r = rg + S::RG * (4 * i4 + j);
+#pragma unroll
+                for (int c = 0; c < S::CPL; ++c) {
+                    const float4 vv = ld_shared4(sV + r * S::ROW + (cg + 32 * c) * 4);
+                    acc[c].x = fmaf(pj[j], vv.x, acc[c].x);
+                    acc[c].y = fmaf(pj[j], vv.y, acc[c].y);
+                    acc[c].z = fmaf(pj[j], vv.z, acc[c].z);
+                    acc[c].w = fmaf(pj[j], vv.w, acc[c].w);
+                }
+            }
+        }
+        m_run = m_new;
+        __syncwarp();  // stage free for the next issue
+        ++consumed;
+        ++cc;
+        if (cc < C.nchunks) continue;
+
+        // ---- item epilogue ---------------------------------------------------
         const float l_tot = warp_sum_xor(l_run, S::RLANES);
 #pragma unroll
         for (int o = S::G; o < 32; o <<= 1) {
 #pragma unroll
-            for (int cc = 0; cc < S::CPL; ++cc) {
-                acc[cc].x += __shfl_xor_sync(0xffffffffu, acc[cc].x, o);
-                acc[cc].y += __shfl_xor_sync(0xffffffffu, acc[cc].y, o);
-                acc[cc].z += __shfl_xor_sync(0xffffffffu, acc[cc].z, o);
-                acc[cc].w += __shfl_xor_sync(0xffffffffu, acc[cc].w, o);
+            for (int c = 0; c < S::CPL; ++c) {
+                acc[c].x += __shfl_xor_sync(0xffffffffu, acc[c].x, o);
+                acc[c].y += __shfl_xor_sync(0xffffffffu, acc[c].y, o);
+                acc[c].z += __shfl_xor_sync(0xffffffffu, acc[c].z, o);
+                acc[c].w += __shfl_xor_sync(0xffffffffu, acc[c].w, o);
             }
         }
-        const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
         if (rg == 0) {
-            if (nsplit == 1) {
+            if (C.whole) {
                 const float inv = 1.0f / fmaxf(l_tot, 1e-12f);
-                float* op = p.out + int64_t(tok) * g.row + int64_t(h) * HD;
+                float* op = p.out + int64_t(C.tok) * g.row + int64_t(C.h) * HD;
 #pragma unroll
-                for (int cc = 0; cc < S::CPL; ++cc) {
-                    const float4 v = make_float4(acc[cc].x * inv, acc[cc].y * inv,
-                                                 acc[cc].z * inv, acc[cc].w * inv);
-                    reinterpret_cast<float4*>(op)[cg + 32 * cc] = v;
+                for (int c = 0; c < S::CPL; ++c) {
+                    const float4 v = make_float4(acc[c].x * inv, acc[c].y * inv, acc[c].z * inv,
+                                                 acc[c].w * inv);
+                    reinterpret_cast<float4*>(op)[cg + 32 * c] = v;
                 }
             } else {
-                const int64_t pi = (int64_t(s) * H + h) * p.max_splits + wi.part;
+                const int64_t pi = (int64_t(C.s) * H + C.h) * p.max_splits + C.part;
                 float* ap = p.part_acc + pi * HD;
 #pragma unroll
-                for (int cc = 0; cc < S::CPL; ++cc) reinterpret_cast<float4*>(ap)[cg + 32 * cc] = acc[cc];
+                for (int c = 0; c < S::CPL; ++c) reinterpret_cast<float4*>(ap)[cg + 32 * c] = acc[c];
                 if (lane == 0) p.part_ml[pi] = make_float2(m_run, l_tot);
             }
+        }
+        m_run = -INFINITY;
+        l_run = 0.f;
+#pragma unroll
+        for (int c = 0; c < S::CPL; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        cc = 0;
+        ++c_index;
+        if (ahead) {
+            C = L;
+            ahead = false;
+        } else {
+            c_live = false;
         }
     }
 }
@@ -409,7 +524,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const AttnParams p) 
     }
 }
 
-template <int HD, int NW, int NS>
+template <int HD, int NW, int NS, bool kB16>
 cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream) {
     constexpr size_t smem = decode_smem_bytes<HD, NW, NS>();
     static int grid_per_device[64] = {0};
@@ -418,18 +533,18 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (grid_per_device[dev] == 0) {
-        e = cudaFuncSetAttribute(decode_kernel<HD, NW, NS>,
+        e = cudaFuncSetAttribute(decode_kernel<HD, NW, NS, kB16>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
         int sms = 0, per_sm = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel<HD, NW, NS>,
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel<HD, NW, NS, kB16>,
                                                           NW * 32, smem);
         if (e != cudaSuccess) return e;
         grid_per_device[dev] = sms * (per_sm > 0 ? per_sm : 1);
     }
-    decode_kernel<HD, NW, NS><<<grid_per_device[dev], NW * 32, smem, stream>>>(p);
+    decode_kernel<HD, NW, NS, kB16><<<grid_per_device[dev], NW * 32, smem, stream>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const int warps = p.num_seqs * p.g.num_heads;
@@ -449,12 +564,24 @@ cudaError_t launch_plan(const AttnParams& p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+// Warps per CTA and stages per warp of the decode kernel (build-time tunables).
+#ifndef NVLLM_DECODE_NW
+#define NVLLM_DECODE_NW 6
+#endif
+#ifndef NVLLM_DECODE_NS
+#define NVLLM_DECODE_NS 2
+#endif
+
 cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream) {
+    constexpr int NW = NVLLM_DECODE_NW;
+    constexpr int NS = NVLLM_DECODE_NS;
     switch (p.g.head_dim) {
-        case 32: return launch_decode_t<32, 4, 3>(p, stream);
-        case 64: return launch_decode_t<64, 4, 3>(p, stream);
-        case 128: return launch_decode_t<128, 4, 3>(p, stream);
-        case 256: return launch_decode_t<256, 4, 3>(p, stream);
+        case 32: return launch_decode_t<32, NW, NS, false>(p, stream);
+        case 64: return launch_decode_t<64, NW, NS, false>(p, stream);
+        case 128:
+            return p.g.block_size == 16 ? launch_decode_t<128, NW, NS, true>(p, stream)
+                                        : launch_decode_t<128, NW, NS, false>(p, stream);
+        case 256: return launch_decode_t<256, NW, NS, false>(p, stream);
         default: return cudaErrorInvalidValue;
     }
 }
