@@ -1,0 +1,107 @@
+"""The C ABI without a GPU: libnvllm.so loads, exports every function that
+include/*.h declares, and its host-only paths (workspace sizing, status strings,
+argument validation that returns before any CUDA call) behave."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+DECL = re.compile(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(nvllm_\w+)\s*\(", re.M)
+
+
+def declared_functions() -> list[str]:
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += DECL.findall(text)
+    return sorted(set(names))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for must in ("nvllm_reshape_and_cache", "nvllm_paged_attention",
+                 "nvllm_paged_attention_workspace_size", "nvllm_get_last_error",
+                 "nvllm_status_string"):
+        assert must in names
+
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_library_exports_declared_symbol(nvlib, name):
+    assert hasattr(nvlib, name), f"libnvllm.so does not export {name}"
+
+
+@pytest.fixture(scope="module")
+def nvlib():
+    import nvllm
+    return nvllm.lib()
+
+
+@pytest.fixture(scope="module")
+def nvmod():
+    import nvllm
+    nvllm.lib()
+    return nvllm
+
+
+def test_status_strings(nvmod):
+    for code in range(7):
+        assert nvmod.status_string(code) not in ("", "unknown status")
+    assert nvmod.status_string(99) == "unknown status"
+
+
+def test_workspace_size_host_only(nvmod):
+    lay = nvmod.KVLayout(65536, 1, 16, 32, 128)
+    ws = nvmod.workspace_size(64, 1, 4096, lay)
+    # partials: 64 seqs x 32 heads x 16 splits x (128 floats + (m, l))
+    assert ws >= 64 * 32 * 16 * (128 * 4 + 8)
+    assert ws % 256 == 0
+    assert nvmod.workspace_size(64, 1, 4096, nvmod.KVLayout(65536, 1, 16, 32, 48)) == 0
+    assert nvmod.workspace_size(64, 1, 4096, nvmod.KVLayout(0, 1, 16, 32, 128)) == 0
+    assert nvmod.workspace_size(-1, 1, 4096, lay) == 0
+
+
+def test_validation_returns_before_any_launch(nvlib, nvmod):
+    """Invalid geometry is refused on the host (no device pointer is touched)."""
+    vp = ctypes.c_void_p
+    bad_hd = nvmod.KVLayout(16, 1, 16, 2, 48)
+    rc = nvlib.nvllm_reshape_and_cache(vp(16), vp(16), vp(16), vp(16), vp(16), 1, 0,
+                                       ctypes.byref(bad_hd), None)
+    assert rc == nvmod.ERR_UNSUPPORTED
+    zero_blocks = nvmod.KVLayout(0, 1, 16, 2, 64)
+    rc = nvlib.nvllm_reshape_and_cache(vp(16), vp(16), vp(16), vp(16), vp(16), 1, 0,
+                                       ctypes.byref(zero_blocks), None)
+    assert rc == nvmod.ERR_INVALID
+    lay = nvmod.KVLayout(16, 2, 16, 2, 64)
+    rc = nvlib.nvllm_reshape_and_cache(vp(16), vp(16), vp(16), vp(16), vp(16), 1, 2,
+                                       ctypes.byref(lay), None)  # layer out of range
+    assert rc == nvmod.ERR_INVALID
+    # empty batches are no-ops that need no device
+    assert nvlib.nvllm_reshape_and_cache(None, None, None, None, None, 0, 0, ctypes.byref(lay),
+                                         None) == nvmod.OK
+    rc = nvlib.nvllm_paged_attention(None, None, None, None, None, 1, None, None, 0, 1, 1, 0,
+                                     ctypes.c_float(0.1), 0, None, 0, ctypes.byref(lay), None)
+    assert rc == nvmod.OK
+    # bad precision / maxima / null pointers
+    args = [vp(256)] * 5
+    rc = nvlib.nvllm_paged_attention(*args, 4, vp(256), vp(256), 2, 1, 64, 0,
+                                     ctypes.c_float(0.1), 7, vp(256), 1 << 20,
+                                     ctypes.byref(lay), None)
+    assert rc == nvmod.ERR_INVALID
+    rc = nvlib.nvllm_paged_attention(*args, 4, vp(256), vp(256), 2, 1, 65, 0,
+                                     ctypes.c_float(0.1), 0, vp(256), 1 << 20,
+                                     ctypes.byref(lay), None)  # 65 > 4 blocks x 16
+    assert rc == nvmod.ERR_INVALID
+    rc = nvlib.nvllm_paged_attention(None, *args[1:], 4, vp(256), vp(256), 2, 1, 64, 0,
+                                     ctypes.c_float(0.1), 0, vp(256), 1 << 20,
+                                     ctypes.byref(lay), None)
+    assert rc == nvmod.ERR_INVALID
+    rc = nvlib.nvllm_paged_attention(*args, 4, vp(256), vp(256), 2, 1, 64, 0,
+                                     ctypes.c_float(0.1), 0, vp(256), 16, ctypes.byref(lay),
+                                     None)  # workspace too small
+    assert rc == nvmod.ERR_WORKSPACE
+    rc = nvlib.nvllm_paged_attention(*args, 4, vp(256), vp(256), 2, 1, 64, 0,
+                                     ctypes.c_float(0.1), 0, vp(8), 1 << 20, ctypes.byref(lay),
+                                     None)  # misaligned workspace
+    assert rc == nvmod.ERR_WORKSPACE
