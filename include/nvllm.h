@@ -93,6 +93,33 @@ int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
                           size_t workspace_bytes, const nvllm_kv_layout* layout,
                           void* stream);
 
+/*
+ * nvllm_paged_attention without a caller workspace, for callers that cannot
+ * allocate device memory: a host that reaches the GPU only through this C ABI
+ * and has no device allocator, or a serving loop whose memory pool forbids
+ * extra cudaMalloc / cudaFree (both synchronize the device mid-step). This
+ * entry point has no counterpart in the reference (whose attention runs on the
+ * CPU and needs no device memory at all).
+ *
+ * The workspace is owned by the library: a 64 MiB device array of which every
+ * GPU that loads libnvllm.so holds one copy until the process exits. A batch
+ * whose nvllm_paged_attention_workspace_size() exceeds 64 MiB is refused with
+ * NVLLM_ERR_WORKSPACE. The entry point itself allocates nothing. The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress,
+ * with that device current); make that first call before any stream capture.
+ * All calls share the one array, so calls that overlap on the GPU (different
+ * streams, or host threads, without ordering between them) race and corrupt
+ * each other's results: order them on one stream. Arguments and results are
+ * otherwise those of nvllm_paged_attention.
+ */
+int nvllm_paged_attention_static(float* out, const float* query, const float* k_arena,
+                                 const float* v_arena, const int32_t* block_tables,
+                                 int32_t max_blocks_per_seq, const int32_t* cu_seqlens_q,
+                                 const int32_t* context_lens, int32_t num_seqs,
+                                 int32_t max_query_len, int32_t max_context_len,
+                                 int32_t layer, float scale, int32_t precision,
+                                 const nvllm_kv_layout* layout, void* stream);
+
 /* Synchronizes the stream, then returns (and clears) the device status word
  * of the current device that the kernels set on skipped out-of-range accesses,
  * inconsistent metadata or bounded waits that gave up. The reference has
