@@ -284,10 +284,12 @@ def nvllm_main(args, spec):
     ws = nvllm.alloc_workspace(spec.num_seqs, max_q, max_ctx, lay, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    precision = nvllm.PRECISION_TF32 if args.precision == "tf32" else nvllm.PRECISION_FP32
+
     def step():
         nvllm.reshape_and_cache(k, v, ka, va, slots, 0, lay, stream=stream)
         nvllm.paged_attention(out, q, ka, va, bt, cu, ctx, max_q, max_ctx, 0, lay,
-                              workspace=ws, stream=stream)
+                              workspace=ws, stream=stream, precision=precision)
 
     def barrier():
         if dist is not None:
@@ -320,7 +322,7 @@ def nvllm_main(args, spec):
         nvllm.reshape_and_cache(k, v, ka, va, slots, 0, lay, stream=stream)
         ev[i][0].record(stream)
         nvllm.paged_attention(out, q, ka, va, bt, cu, ctx, max_q, max_ctx, 0, lay,
-                              workspace=ws, stream=stream)
+                              workspace=ws, stream=stream, precision=precision)
         ev[i][1].record(stream)
     e1.record(stream)
     torch.cuda.synchronize(dev)
@@ -384,7 +386,7 @@ def nvllm_main(args, spec):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic", "config": {**workload_config(spec),
+        "data": "synthetic", "config": {**workload_config(spec), "prefill_precision": args.precision,
                                         "parallelism": f"sequence-partitioned x{world}"},
         "hbm_gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -434,6 +436,8 @@ def main() -> int:
     ap.add_argument("--workload", choices=["decode", "mixed", "longctx", "decode_small"],
                     default="decode")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32",
+                    help="prefill tile arithmetic (decode is always fp32)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

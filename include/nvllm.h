@@ -41,7 +41,9 @@ enum nvllm_status {
 
 enum nvllm_precision {
     NVLLM_PRECISION_FP32 = 0,  /* fp32 FFMA everywhere (max-abs 2e-5 vs the reference) */
-    NVLLM_PRECISION_TF32 = 1   /* prefill QK^T / PV tiles on tcgen05 kind::tf32 (1e-3) */
+    NVLLM_PRECISION_TF32 = 1   /* prefill QK^T / PV tiles on tcgen05 kind::tf32 (1e-3) when
+                                  head_dim is 128 and block_size 16; other geometries keep
+                                  the fp32 prefill */
 };
 
 typedef struct nvllm_kv_layout {

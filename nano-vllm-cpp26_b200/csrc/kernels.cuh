@@ -68,6 +68,9 @@ cudaError_t launch_reshape_and_cache(const float* key, const float* value, float
 cudaError_t launch_plan(const AttnParams& p, cudaStream_t stream);
 cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream);
 cudaError_t launch_prefill_fp32(const AttnParams& p, cudaStream_t stream);
+cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream);
+bool prefill_tc_supported(const ArenaGeom& g);
+int32_t prefill_tc_tile_rows();
 
 int32_t decode_split_tokens(int32_t head_dim);
 int32_t prefill_tile_rows(int32_t head_dim);

@@ -131,7 +131,6 @@ int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
         return NVLLM_ERR_INVALID;
     }
     if (!(scale > 0.0f) || scale != scale) return NVLLM_ERR_INVALID;
-    if (precision == NVLLM_PRECISION_TF32 && max_query_len > 1) return NVLLM_ERR_UNSUPPORTED;
 
     const WorkspaceLayout w = workspace_layout(num_seqs, max_query_len, max_context_len,
                                                layout->num_heads, layout->head_dim);
@@ -165,9 +164,18 @@ int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
     p.split_tokens = w.split_tokens;
     p.prefill_tile = w.prefill_tile;
 
+    // TF32 prefill runs on the tensor cores where the kernel's geometry allows
+    // (hd 128, block size 16); elsewhere the fp32 FFMA kernel serves it, whose
+    // error is far inside the TF32 tolerance.
+    const bool tc_prefill =
+        precision == NVLLM_PRECISION_TF32 && max_query_len > 1 && prefill_tc_supported(p.g);
+    if (tc_prefill) p.prefill_tile = prefill_tc_tile_rows();
+
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = launch_plan(p, st);
-    if (e == cudaSuccess && max_query_len > 1) e = launch_prefill_fp32(p, st);
+    if (e == cudaSuccess && max_query_len > 1) {
+        e = tc_prefill ? launch_prefill_tc(p, st) : launch_prefill_fp32(p, st);
+    }
     if (e == cudaSuccess) e = launch_decode(p, st);
     return e == cudaSuccess ? NVLLM_OK : NVLLM_ERR_CUDA;
 }

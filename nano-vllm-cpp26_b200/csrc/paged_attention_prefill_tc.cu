@@ -1,0 +1,464 @@
+// K3 (TF32 tensor cores): causal paged prefill attention on tcgen05.
+//
+// Same mathematics as src/model.cpp:204-260 for sequences with more than one
+// query row, with the two dense products QK^T and PV on the 5th-generation
+// tensor cores (kind::tf32, fp32 accumulation in TMEM); softmax in fp32.
+// Geometry: head_dim 128, block size 16 (one TMA box = the 16 rows of one
+// physical block and 32 columns of one head).
+//
+// One CTA per SM (persistent), 5 warps:
+//   warps 0-3  softmax / epilogue: thread t owns query row t of a 128-row tile
+//              and TMEM lane t. Per key tile it reads its row of S from TMEM
+//              (tcgen05.ld), applies the causal mask, updates the online max
+//              and sum, writes P (tf32, 128B-swizzled, K-major) to shared
+//              memory, and folds the previous tile's P.V from TMEM into an
+//              fp32 register accumulator with the usual rescale.
+//   warp 4     producer: one thread issues the TMA gathers of the K and V tiles
+//              (64 keys = 4 physical blocks x 4 swizzle atoms per tensor, into a
+//              double-buffered ring) and all tcgen05.mma: S(t+1) = Q K(t+1)^T is
+//              issued while the softmax warps work on S(t); O(t) = P(t) V(t)
+//              after P(t) is in shared memory.
+// Operands: Q (rounded to tf32 on load), K, P are K-major and V MN-major, all in
+// the 128-byte swizzled layout TMA produces; TMEM holds S twice (2 x 64
+// columns) and O once (128 columns).
+// Every wait is bounded; on a timeout the CTA records NVLLM_ERR_TIMEOUT, lets
+// its outstanding copies and MMAs finish and frees its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tcgen05.cuh"
+
+namespace nvllm {
+
+namespace {
+
+constexpr int kQT = 128;  // query rows per tile (= TMEM lanes)
+constexpr int kKT = 64;   // keys per tile
+constexpr int kHD = 128;
+constexpr int kThreads = 160;
+constexpr uint32_t kTmemCols = 256;  // S[0] 0..63, S[1] 64..127, O 128..255
+
+constexpr uint32_t kQAtom = kQT * 128;         // 128 rows x 32 fp32
+constexpr uint32_t kQBytes = 4 * kQAtom;       // 64 KiB
+constexpr uint32_t kKVAtom = kKT * 128;        // 64 rows x 32 fp32
+constexpr uint32_t kKBytes = 4 * kKVAtom;      // 32 KiB
+constexpr uint32_t kStageBytes = 2 * kKBytes;  // K + V
+constexpr uint32_t kPAtom = kQT * 128;         // 128 rows x 32 keys
+constexpr uint32_t kPBytes = 2 * kPAtom;       // 32 KiB
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffKV = kOffQ + kQBytes;
+constexpr uint32_t kOffP = kOffKV + 2 * kStageBytes;
+constexpr uint32_t kOffBar = kOffP + kPBytes;
+constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + control block + alignment slack
+
+constexpr uint32_t kIdescS = tc::tf32_idesc(kQT, kKT, false, false);
+constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, true);
+
+struct Control {
+    uint64_t kv_full[2];
+    uint64_t pv_done[2];
+    uint64_t s_full[2];
+    uint64_t p_full;
+    uint64_t o_full;
+    uint64_t drain;
+    uint32_t tmem_base;
+    int32_t item;
+    int32_t abort;
+};
+static_assert(sizeof(Control) <= 256, "control block");
+
+// Bounded wait that also gives up once another role has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Control* ctl) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*reinterpret_cast<volatile int32_t*>(&ctl->abort)) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            raise_status(kStatusTimeout);
+            atomicExch(&ctl->abort, 1);
+            return false;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
+                  const __grid_constant__ CUtensorMap vmap) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* sQ = base + kOffQ;
+    unsigned char* sKV = base + kOffKV;
+    unsigned char* sP = base + kOffP;
+    Control* ctl = reinterpret_cast<Control*>(base + kOffBar);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+
+    // K/V stages start as zeros: rows past a sequence's end are never loaded
+    // and must be finite (their softmax weight is 0).
+    for (uint32_t i = tid * 16; i < 2 * kStageBytes; i += kThreads * 16) {
+        *reinterpret_cast<float4*>(sKV + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&ctl->kv_full[i], 1);
+            mbar_init(&ctl->pv_done[i], 1);
+            mbar_init(&ctl->s_full[i], 1);
+        }
+        mbar_init(&ctl->p_full, kQT);
+        mbar_init(&ctl->o_full, 1);
+        mbar_init(&ctl->drain, 1);
+        ctl->abort = 0;
+    }
+    fence_barrier_init();
+    if (warp == 4) {
+        tc::tmem_alloc(&ctl->tmem_base, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = ctl->tmem_base;
+    const uint32_t tS0 = tmem;
+    const uint32_t tO = tmem + 128;
+
+    const ArenaGeom& g = p.g;
+    const int H = g.num_heads;
+    const int total = p.counters->prefill_items * H;
+    uint32_t tile_seq = 0;   // key tiles processed by this CTA (ring position)
+    uint32_t next_load = 0;  // producer: ring index of the next K/V load to issue
+    uint32_t next_wait = 0;  // producer: ring index of the next K/V load to wait for
+    bool issued_mma = false;
+
+    for (;;) {
+        if (tid == 0) ctl->item = atomicAdd(&p.counters->prefill_next, 1);
+        __syncthreads();
+        const int it = ctl->item;
+        const bool stop = it >= total || *reinterpret_cast<volatile int32_t*>(&ctl->abort);
+        __syncthreads();
+        if (stop) break;
+
+        const WorkItem wi = p.prefill_items[it / H];
+        const int h = it % H;
+        const int s = wi.seq;
+        const int q0 = p.cu_seqlens_q[s];
+        const int qlen = p.cu_seqlens_q[s + 1] - q0;
+        const int first_pos = p.context_lens[s] - qlen;
+        const int r0 = wi.part * kQT;
+        const int nrows = min(kQT, qlen - r0);
+        const int nk = first_pos + r0 + nrows;  // keys 0..nk-1 visible to this tile
+        const int ntiles = (nk + kKT - 1) / kKT;
+        const uint32_t n0 = tile_seq;
+
+        if (warp < 4) {
+            // Q tile -> shared memory: tf32 (round to nearest), 128B-swizzled, K-major.
+            const int row = tid;
+            const float4* qrow = reinterpret_cast<const float4*>(
+                p.q + int64_t(q0 + r0 + row) * g.row + int64_t(h) * kHD);
+#pragma unroll 8
+            for (int c = 0; c < kHD / 4; ++c) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (row < nrows) v = __ldg(qrow + c);
+                v.x = tc::to_tf32(v.x);
+                v.y = tc::to_tf32(v.y);
+                v.z = tc::to_tf32(v.z);
+                v.w = tc::to_tf32(v.w);
+                const int atom = c >> 3;
+                const int pos = (c & 7) ^ (row & 7);
+                *reinterpret_cast<float4*>(sQ + atom * kQAtom + row * 128 + pos * 16) = v;
+            }
+            tc::fence_async_smem();
+        }
+        __syncthreads();
+
+        if (warp == 4) {
+            if (lane == 0) {
+                // ------------------------------------------------------------ producer
+                const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
+                bool ok = true;
+                auto load = [&](uint32_t n, int t) -> bool {
+                    const int st = int(n & 1u);
+                    if (n >= 2 && !wait_or_abort(&ctl->pv_done[st], ((n - 2) >> 1) & 1u, ctl)) {
+                        return false;
+                    }
+                    unsigned char* sK = sKV + st * kStageBytes;
+                    unsigned char* sV = sK + kKBytes;
+                    const int kbase = t * kKT;
+                    const int nvalid = min(kKT, nk - kbase);
+                    const int nblk = (nvalid + 15) / 16;
+                    uint32_t bytes = 0;
+                    for (int j = 0; j < nblk; ++j) {
+                        const int64_t blk = table[kbase / 16 + j];
+                        if (blk >= 0 && blk < g.num_blocks) bytes += 2u * 4u * 2048u;
+                    }
+                    mbar_arrive_expect_tx(&ctl->kv_full[st], bytes);
+                    for (int j = 0; j < nblk; ++j) {
+                        const int64_t blk = table[kbase / 16 + j];
+                        if (blk < 0 || blk >= g.num_blocks) {
+                            raise_status(kStatusBounds);
+                            continue;
+                        }
+                        const int y = int((blk * g.num_layers + p.layer) * 16);
+#pragma unroll
+                        for (int a = 0; a < 4; ++a) {
+                            const int x = h * kHD + a * 32;
+                            tc::tma_load_2d(sK + a * kKVAtom + j * 2048, &kmap, x, y, &ctl->kv_full[st]);
+                            tc::tma_load_2d(sV + a * kKVAtom + j * 2048, &vmap, x, y, &ctl->kv_full[st]);
+                        }
+                    }
+                    next_load = n + 1;
+                    return true;
+                };
+                auto issue_s = [&](uint32_t n) {
+                    const int st = int(n & 1u);
+                    const uint32_t qa = smem_addr(sQ);
+                    const uint32_t ka = smem_addr(sKV + st * kStageBytes);
+#pragma unroll
+                    for (int k = 0; k < kHD / 8; ++k) {
+                        const uint32_t off = (k & 3) * 32u;  // 8 tf32 = 32 B within the atom
+                        const uint64_t ad = tc::sw128_desc(qa + (k >> 2) * kQAtom + off, 16, 1024);
+                        const uint64_t bd = tc::sw128_desc(ka + (k >> 2) * kKVAtom + off, 16, 1024);
+                        tc::mma_tf32(tS0 + (n & 1u) * 64u, ad, bd, kIdescS, k > 0);
+                    }
+                    tc::commit(&ctl->s_full[n & 1u]);
+                    issued_mma = true;
+                };
+                auto issue_o = [&](uint32_t n) {
+                    const int st = int(n & 1u);
+                    const uint32_t pa = smem_addr(sP);
+                    const uint32_t va = smem_addr(sKV + st * kStageBytes + kKBytes);
+#pragma unroll
+                    for (int k = 0; k < kKT / 8; ++k) {
+                        const uint64_t ad = tc::sw128_desc(pa + (k >> 2) * kPAtom + (k & 3) * 32u, 16, 1024);
+                        const uint64_t bd = tc::sw128_desc(va + k * 1024u, kKVAtom, 1024);
+                        tc::mma_tf32(tO, ad, bd, kIdescO, k > 0);
+                    }
+                    tc::commit(&ctl->o_full);
+                    tc::commit(&ctl->pv_done[st]);
+                };
+
+                ok = load(n0, 0);
+                if (ok && ntiles > 1) ok = load(n0 + 1, 1);
+                if (ok) ok = wait_or_abort(&ctl->kv_full[n0 & 1u], (n0 >> 1) & 1u, ctl);
+                if (ok) {
+                    next_wait = n0 + 1;
+                    tc::fence_after_sync();
+                    issue_s(n0);
+                }
+                for (int t = 0; ok && t < ntiles; ++t) {
+                    const uint32_t n = n0 + t;
+                    if (t + 1 < ntiles) {
+                        ok = wait_or_abort(&ctl->kv_full[(n + 1) & 1u], ((n + 1) >> 1) & 1u, ctl);
+                        if (!ok) break;
+                        next_wait = n + 2;
+                        tc::fence_after_sync();
+                        issue_s(n + 1);
+                    }
+                    ok = wait_or_abort(&ctl->p_full, n & 1u, ctl);
+                    if (!ok) break;
+                    tc::fence_after_sync();
+                    issue_o(n);
+                    if (t + 2 < ntiles) ok = load(n + 2, t + 2);
+                }
+                (void)ok;
+            }
+            __syncwarp();
+        } else {
+            // ------------------------------------------------------------ softmax warps
+            const int row = tid;
+            const int qpos = first_pos + r0 + row;
+            const uint32_t lane_off = uint32_t(warp * 32) << 16;
+            float o[kHD];
+#pragma unroll
+            for (int j = 0; j < kHD; ++j) o[j] = 0.f;
+            float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
+            bool ok = true;
+            for (int t = 0; t < ntiles; ++t) {
+                const uint32_t n = n0 + t;
+                if (!wait_or_abort(&ctl->s_full[n & 1u], (n >> 1) & 1u, ctl)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                float sc[kKT];
+                tc::tmem_ld32(tS0 + (n & 1u) * 64u + lane_off, sc);
+                tc::tmem_ld32(tS0 + (n & 1u) * 64u + 32u + lane_off, sc + 32);
+                tc::tmem_ld_wait();
+                const int kbase = t * kKT;
+                if (nk - kbase < kKT) {
+                    // last, partial tile: zero V rows past the visible keys so that
+                    // their zero weights cannot meet stale non-finite data
+                    if (!wait_or_abort(&ctl->kv_full[n & 1u], (n >> 1) & 1u, ctl)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* sV = sKV + (n & 1u) * kStageBytes + kKBytes;
+                    const int v0 = nk - kbase;
+                    for (int idx = tid; idx < (kKT - v0) * 32; idx += kQT) {
+                        const int r = v0 + idx / 32;
+                        const int c = idx % 32;
+                        *reinterpret_cast<float4*>(sV + (c >> 3) * kKVAtom + r * 128 + (c & 7) * 16) =
+                            make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    tc::fence_async_smem();
+                }
+                float cm = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < kKT; ++j) {
+                    const int kp = kbase + j;
+                    sc[j] = (kp <= qpos && kp < nk) ? sc[j] * p.qk_scale_log2 : -INFINITY;
+                    cm = fmaxf(cm, sc[j]);
+                }
+                const float m_new = fmaxf(m_run, cm);
+                const float alpha = exp2f(m_run - m_new);
+                float ps = 0.f;
+#pragma unroll
+                for (int j = 0; j < kKT; ++j) {
+                    sc[j] = exp2f(sc[j] - m_new);
+                    ps += sc[j];
+                }
+                l_run = fmaf(l_run, alpha, ps);
+                m_run = m_new;
+                if (t > 0) {
+                    if (!wait_or_abort(&ctl->o_full, (n - 1) & 1u, ctl)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+#pragma unroll
+                    for (int c = 0; c < kHD / 32; ++c) {
+                        float ov[32];
+                        tc::tmem_ld32(tO + c * 32u + lane_off, ov);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) o[c * 32 + j] = fmaf(o[c * 32 + j], alpha_prev, ov[j]);
+                    }
+                }
+                // P (tf32) -> shared memory, 128B-swizzled K-major
+#pragma unroll
+                for (int c = 0; c < kKT / 4; ++c) {
+                    float4 v = make_float4(tc::to_tf32(sc[4 * c]), tc::to_tf32(sc[4 * c + 1]),
+                                           tc::to_tf32(sc[4 * c + 2]), tc::to_tf32(sc[4 * c + 3]));
+                    const int atom = c >> 3;
+                    const int pos = (c & 7) ^ (row & 7);
+                    *reinterpret_cast<float4*>(sP + atom * kPAtom + row * 128 + pos * 16) = v;
+                }
+                tc::fence_async_smem();
+                tc::fence_before_sync();
+                mbar_arrive(&ctl->p_full);
+                alpha_prev = alpha;
+            }
+            if (ok && ntiles > 0) {
+                const uint32_t n = n0 + ntiles - 1;
+                if (wait_or_abort(&ctl->o_full, n & 1u, ctl)) {
+                    tc::fence_after_sync();
+#pragma unroll
+                    for (int c = 0; c < kHD / 32; ++c) {
+                        float ov[32];
+                        tc::tmem_ld32(tO + c * 32u + lane_off, ov);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) o[c * 32 + j] = fmaf(o[c * 32 + j], alpha_prev, ov[j]);
+                    }
+                    if (row < nrows) {
+                        const float inv = 1.0f / fmaxf(l_run, 1e-12f);
+                        float4* op = reinterpret_cast<float4*>(p.out + int64_t(q0 + r0 + row) * g.row +
+                                                               int64_t(h) * kHD);
+#pragma unroll
+                        for (int c = 0; c < kHD / 4; ++c) {
+                            op[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv,
+                                                o[4 * c + 3] * inv);
+                        }
+                    }
+                }
+            }
+            tc::fence_before_sync();
+        }
+        tile_seq += ntiles;
+    }
+
+    // Teardown: on an abort, let this CTA's copies and MMAs finish (bounded)
+    // before its shared memory and TMEM are released.
+    if (warp == 4 && lane == 0) {
+        for (uint32_t n = next_wait; n < next_load; ++n) {
+            mbar_wait(&ctl->kv_full[n & 1u], (n >> 1) & 1u);
+        }
+        if (issued_mma) {
+            tc::commit(&ctl->drain);
+            mbar_wait(&ctl->drain, 0);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 4) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        }
+    });
+    return fn;
+}
+
+// 2D view of an arena: rows (block, layer, slot) x columns H*hd, box = one
+// block's 16 rows x 32 columns, 128-byte swizzle.
+bool make_arena_map(CUtensorMap* map, const float* arena, const ArenaGeom& g) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[2] = {cuuint64_t(g.row),
+                                cuuint64_t(g.num_blocks) * g.num_layers * g.block_size};
+    const cuuint64_t strides[1] = {cuuint64_t(g.row) * sizeof(float)};
+    const cuuint32_t box[2] = {32, 16};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(arena), dims, strides,
+              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool prefill_tc_supported(const ArenaGeom& g) { return g.head_dim == kHD && g.block_size == 16; }
+
+int32_t prefill_tc_tile_rows() { return kQT; }
+
+cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream) {
+    CUtensorMap kmap, vmap;
+    if (!make_arena_map(&kmap, p.k_arena, p.g) || !make_arena_map(&vmap, p.v_arena, p.g)) {
+        return cudaErrorInvalidValue;
+    }
+    static int grid_per_device[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (grid_per_device[dev] == 0) {
+        e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(kSmemBytes));
+        if (e != cudaSuccess) return e;
+        int sms = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        grid_per_device[dev] = sms;  // one CTA per SM (shared memory and TMEM sized for it)
+    }
+    prefill_tc_kernel<<<grid_per_device[dev], kThreads, kSmemBytes, stream>>>(p, kmap, vmap);
+    return cudaGetLastError();
+}
+
+}  // namespace nvllm

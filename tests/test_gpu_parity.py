@@ -14,7 +14,7 @@ import math
 import numpy as np
 import pytest
 
-from helpers import (TOL_FP32, device_run, golden_case, golden_names, layout_of, load_golden,
+from helpers import (TOL_FP32, TOL_TF32, device_run, golden_case, golden_names, layout_of, load_golden,
                      oracle_run)
 
 pytestmark = pytest.mark.gpu
@@ -320,3 +320,61 @@ def test_empty_batch_is_noop(nv):
     st = nv.paged_attention(z, z, ka, ka, torch.zeros(0, 1, dtype=torch.int32, device="cuda"), cu,
                             i0, 1, 1, 0, lay, workspace=ws)
     assert st == nv.OK
+
+
+# ---------------------------------------------------------------------------
+# TF32 tensor-core prefill (tcgen05): tolerance 1e-3
+
+
+@pytest.mark.parametrize("name", ["mixed_h32_hd128_b16", "decode_h32_hd128_b16",
+                                  "mixed_h4_hd32_b4"])
+def test_golden_fixture_tf32(nv, oracle, name):
+    case = golden_case(name)
+    g = load_golden(name)
+    _, _, out, status = device_run(nv, oracle, case, precision=nv.PRECISION_TF32)
+    assert status == nv.OK, nv.status_string(status)
+    err = np.abs(out - g["attn_out"]).max()
+    assert err <= TOL_TF32, f"{name}: tf32 kernel vs reference max-abs {err}"
+
+
+def test_tf32_prefill_mixed_shape_vs_oracle(nv, oracle):
+    """Fresh causal prefills (row counts around the 128-row tile and the
+    64-key tile), a chunked continuation and decodes, TF32 prefill tiles."""
+    rng = np.random.default_rng(21)
+    dec = rng.integers(256, 3001, 12).astype(np.int32)
+    ctx = np.concatenate([[700, 128, 129, 64, 65, 2, 900], dec]).astype(np.int32)
+    ql = np.concatenate([[700, 128, 129, 64, 65, 2, 150], np.ones(12)]).astype(np.int32)
+    b = build_batch(nv, seed=22, num_blocks=4096, block_size=16, num_heads=32, head_dim=128,
+                    ctx_lens=ctx, q_lens=ql)
+    out = run_attention(nv, b, precision=nv.PRECISION_TF32)
+    assert nv.get_last_error() == nv.OK
+    oracle_check(nv, oracle, b, out, list(range(len(ctx))), tol=TOL_TF32)
+
+
+def test_tf32_prefill_stale_nonfinite_rows_do_not_leak(nv, oracle):
+    """Arena rows past a sequence's end inside its last block hold NaN: the
+    tensor-core tile loads whole blocks, so those rows must be neutralised."""
+    torch = _torch()
+    ctx = np.array([37, 200, 90], np.int32)
+    ql = np.array([37, 200, 20], np.int32)
+    b = build_batch(nv, seed=23, num_blocks=256, block_size=16, num_heads=4, head_dim=128,
+                    ctx_lens=ctx, q_lens=ql)
+    # poison every row past each sequence's last position in its last block
+    for s in range(len(ctx)):
+        last = int(b["bt"][s, (ctx[s] - 1) // 16])
+        for slot in range(ctx[s] % 16 or 16, 16):
+            b["ka"][last, 0, slot] = float("nan")
+            b["va"][last, 0, slot] = float("nan")
+    for precision, tol in ((nv.PRECISION_TF32, TOL_TF32), (nv.PRECISION_FP32, TOL_FP32)):
+        out = run_attention(nv, b, precision=precision)
+        assert nv.get_last_error() == nv.OK
+        assert torch.isfinite(out).all()
+        oracle_check(nv, oracle, b, out, [0, 1, 2], tol=tol)
+
+
+def test_tf32_other_geometries_use_fp32_prefill(nv, oracle):
+    b = build_batch(nv, seed=24, num_blocks=512, block_size=8, num_heads=8, head_dim=64,
+                    ctx_lens=[300, 40, 700], q_lens=[300, 1, 33])
+    out = run_attention(nv, b, precision=nv.PRECISION_TF32)
+    assert nv.get_last_error() == nv.OK
+    oracle_check(nv, oracle, b, out, [0, 1, 2], tol=TOL_FP32)
