@@ -8,19 +8,29 @@
 //
 // One CTA per SM (persistent), 5 warps:
 //   warps 0-3  softmax / epilogue: thread t owns query row t of a 128-row tile
-//              and TMEM lane t. Per key tile it reads its row of S from TMEM
-//              (tcgen05.ld), applies the causal mask, updates the online max
-//              and sum, writes P (tf32, 128B-swizzled, K-major) to shared
-//              memory, and folds the previous tile's P.V from TMEM into an
-//              fp32 register accumulator with the usual rescale.
-//   warp 4     producer: one thread issues the TMA gathers of the K and V tiles
-//              (64 keys = 4 physical blocks x 4 swizzle atoms per tensor, into a
-//              double-buffered ring) and all tcgen05.mma: S(t+1) = Q K(t+1)^T is
-//              issued while the softmax warps work on S(t); O(t) = P(t) V(t)
-//              after P(t) is in shared memory.
-// Operands: Q (rounded to tf32 on load), K, P are K-major and V MN-major, all in
-// the 128-byte swizzled layout TMA produces; TMEM holds S twice (2 x 64
-// columns) and O once (128 columns).
+//              and TMEM lane t. Per key tile (32 keys) it reads its row of S
+//              from TMEM (tcgen05.ld), applies the causal mask, updates the
+//              online max and sum, writes P (tf32) to shared memory, writes
+//              column t of V transposed (tf32, zero past the visible keys) to
+//              shared memory, and folds the previous tile's P.V from TMEM into
+//              an fp32 register accumulator with the usual rescale.
+//   warp 4     producer: one thread issues the TMA gathers of the K and V
+//              tiles (2 physical blocks x 4 swizzle atoms per tensor) into a
+//              3-stage ring and all tcgen05.mma: S(t+1) = Q K(t+1)^T is issued
+//              while the softmax warps work on S(t); O(t) = P(t) V(t) once P(t)
+//              and V(t)^T are in shared memory.
+// Both products run as 3xTF32 (A_hi B_hi + A_lo B_hi + A_hi B_lo, every part
+// rounded to nearest), which keeps them at fp32 accuracy: a single tf32 pass
+// errs by ~1e-3 in the output at these magnitudes (one visible key => the
+// output is that key's V row, carried at tf32 precision). Q_hi and Q_lo live
+// in TMEM as the A operand of S; K_hi (rounded in place) and K_lo are written
+// by the producer warp next to the TMA-loaded K tile; P and V^T hi / lo parts
+// by the softmax warps.
+// The shared-memory operands (K, P, V^T parts) are K-major in the 128-byte
+// swizzled layout (TMA writes K that way; P and V^T are written by the softmax
+// threads in the same pattern). V must be transposed on chip: a tf32 operand
+// can only be consumed K-major here, and V arrives key-major. TMEM holds S
+// twice (2 x 32 columns), O (128 columns) and Q_hi, Q_lo (128 columns each).
 // Every wait is bounded; on a timeout the CTA records NVLLM_ERR_TIMEOUT, lets
 // its outstanding copies and MMAs finish and frees its TMEM.
 #include <cuda.h>
@@ -37,30 +47,33 @@ namespace nvllm {
 namespace {
 
 constexpr int kQT = 128;  // query rows per tile (= TMEM lanes)
-constexpr int kKT = 64;   // keys per tile
+constexpr int kKT = 32;   // keys per tile
 constexpr int kHD = 128;
+constexpr int kStages = 3;
 constexpr int kThreads = 160;
-constexpr uint32_t kTmemCols = 256;  // S[0] 0..63, S[1] 64..127, O 128..255
+// TMEM columns: S[0] 0..31, S[1] 32..63, O 128..255, Q_hi 256..383, Q_lo 384..511
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 128;
+constexpr uint32_t kColQhi = 256;
+constexpr uint32_t kColQlo = 384;
 
-constexpr uint32_t kQAtom = kQT * 128;         // 128 rows x 32 fp32
-constexpr uint32_t kQBytes = 4 * kQAtom;       // 64 KiB
-constexpr uint32_t kKVAtom = kKT * 128;        // 64 rows x 32 fp32
-constexpr uint32_t kKBytes = 4 * kKVAtom;      // 32 KiB
-constexpr uint32_t kStageBytes = 2 * kKBytes;  // K + V
-constexpr uint32_t kPAtom = kQT * 128;         // 128 rows x 32 keys
-constexpr uint32_t kPBytes = 2 * kPAtom;       // 32 KiB
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffKV = kOffQ + kQBytes;
-constexpr uint32_t kOffP = kOffKV + 2 * kStageBytes;
-constexpr uint32_t kOffBar = kOffP + kPBytes;
+constexpr uint32_t kKVAtom = kKT * 128;         // 32 rows x 32 fp32
+constexpr uint32_t kKBytes = 4 * kKVAtom;       // 16 KiB per tensor tile
+constexpr uint32_t kStageBytes = 3 * kKBytes;   // K_hi, K_lo, V
+constexpr uint32_t kPBytes = kQT * 128;         // 128 rows x 32 keys (one of hi / lo)
+constexpr uint32_t kVtBytes = kHD * 128;        // 128 dims x 32 keys (one of hi / lo)
+constexpr uint32_t kOffKV = 0;
+constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;
+constexpr uint32_t kOffVt = kOffP + 2 * kPBytes;
+constexpr uint32_t kOffBar = kOffVt + 2 * kVtBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + control block + alignment slack
 
 constexpr uint32_t kIdescS = tc::tf32_idesc(kQT, kKT, false, false);
-constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, true);
+constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, false);
 
 struct Control {
-    uint64_t kv_full[2];
-    uint64_t pv_done[2];
+    uint64_t kv_full[kStages];
+    uint64_t pv_done[kStages];
     uint64_t s_full[2];
     uint64_t p_full;
     uint64_t o_full;
@@ -86,31 +99,29 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Co
     }
 }
 
+__device__ __forceinline__ uint32_t stage_of(uint32_t n) { return n % kStages; }
+__device__ __forceinline__ uint32_t stage_parity(uint32_t n) { return (n / kStages) & 1u; }
+
 __global__ void __launch_bounds__(kThreads, 1)
 prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* sQ = base + kOffQ;
     unsigned char* sKV = base + kOffKV;
     unsigned char* sP = base + kOffP;
+    unsigned char* sVt = base + kOffVt;
     Control* ctl = reinterpret_cast<Control*>(base + kOffBar);
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
 
-    // K/V stages start as zeros: rows past a sequence's end are never loaded
-    // and must be finite (their softmax weight is 0).
-    for (uint32_t i = tid * 16; i < 2 * kStageBytes; i += kThreads * 16) {
-        *reinterpret_cast<float4*>(sKV + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kStages; ++i) {
             mbar_init(&ctl->kv_full[i], 1);
             mbar_init(&ctl->pv_done[i], 1);
-            mbar_init(&ctl->s_full[i], 1);
         }
+        for (int i = 0; i < 2; ++i) mbar_init(&ctl->s_full[i], 1);
         mbar_init(&ctl->p_full, kQT);
         mbar_init(&ctl->o_full, 1);
         mbar_init(&ctl->drain, 1);
@@ -125,8 +136,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = ctl->tmem_base;
-    const uint32_t tS0 = tmem;
-    const uint32_t tO = tmem + 128;
+    const uint32_t tO = tmem + kColO;
 
     const ArenaGeom& g = p.g;
     const int H = g.num_heads;
@@ -157,38 +167,52 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
         const uint32_t n0 = tile_seq;
 
         if (warp < 4) {
-            // Q tile -> shared memory: tf32 (round to nearest), 128B-swizzled, K-major.
+            // Q tile -> TMEM as the A operand of S = Q K^T, split for 3xTF32:
+            // q = q_hi + q_lo with both parts tf32 (round to nearest).
             const int row = tid;
+            const uint32_t lane_off = uint32_t(warp * 32) << 16;
             const float4* qrow = reinterpret_cast<const float4*>(
                 p.q + int64_t(q0 + r0 + row) * g.row + int64_t(h) * kHD);
-#pragma unroll 8
-            for (int c = 0; c < kHD / 4; ++c) {
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (row < nrows) v = __ldg(qrow + c);
-                v.x = tc::to_tf32(v.x);
-                v.y = tc::to_tf32(v.y);
-                v.z = tc::to_tf32(v.z);
-                v.w = tc::to_tf32(v.w);
-                const int atom = c >> 3;
-                const int pos = (c & 7) ^ (row & 7);
-                *reinterpret_cast<float4*>(sQ + atom * kQAtom + row * 128 + pos * 16) = v;
+#pragma unroll 1
+            for (int c = 0; c < kHD / 32; ++c) {
+                float hi[32], lo[32];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (row < nrows) v = __ldg(qrow + c * 8 + i);
+                    const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        hi[4 * i + e] = tc::to_tf32(x[e]);
+                        lo[4 * i + e] = tc::to_tf32(x[e] - hi[4 * i + e]);
+                    }
+                }
+                tc::tmem_st32(tmem + kColQhi + c * 32u + lane_off, hi);
+                tc::tmem_st32(tmem + kColQlo + c * 32u + lane_off, lo);
             }
-            tc::fence_async_smem();
+            tc::tmem_st_wait();
+            tc::fence_before_sync();
         }
         __syncthreads();
 
         if (warp == 4) {
-            if (lane == 0) {
-                // ------------------------------------------------------------ producer
-                const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
-                bool ok = true;
-                auto load = [&](uint32_t n, int t) -> bool {
-                    const int st = int(n & 1u);
-                    if (n >= 2 && !wait_or_abort(&ctl->pv_done[st], ((n - 2) >> 1) & 1u, ctl)) {
-                        return false;
-                    }
+            // ---------------------------------------------------------------- producer
+            // The whole warp waits and rounds each K tile to tf32 in place (the
+            // tensor core would otherwise truncate it); lane 0 alone issues the
+            // TMA copies, the MMAs and their commits.
+            const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
+            auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+                const bool got = wait_or_abort(bar, parity, ctl);
+                return __all_sync(0xffffffffu, got);
+            };
+            auto load = [&](uint32_t n, int t) -> bool {
+                const uint32_t st = stage_of(n);
+                if (n >= uint32_t(kStages) && !wait_all(&ctl->pv_done[st], stage_parity(n - kStages))) {
+                    return false;
+                }
+                if (lane == 0) {
                     unsigned char* sK = sKV + st * kStageBytes;
-                    unsigned char* sV = sK + kKBytes;
+                    unsigned char* sV = sK + 2 * kKBytes;
                     const int kbase = t * kKT;
                     const int nvalid = min(kKT, nk - kbase);
                     const int nblk = (nvalid + 15) / 16;
@@ -212,68 +236,90 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                             tc::tma_load_2d(sV + a * kKVAtom + j * 2048, &vmap, x, y, &ctl->kv_full[st]);
                         }
                     }
-                    next_load = n + 1;
-                    return true;
-                };
-                auto issue_s = [&](uint32_t n) {
-                    const int st = int(n & 1u);
-                    const uint32_t qa = smem_addr(sQ);
-                    const uint32_t ka = smem_addr(sKV + st * kStageBytes);
+                }
+                __syncwarp();
+                next_load = n + 1;
+                return true;
+            };
+            // wait for tile n's K/V, split its K into tf32 hi (in place) and lo
+            // parts, then S(n) = Q_hi K_hi^T + Q_lo K_hi^T + Q_hi K_lo^T
+            auto stage_and_issue_s = [&](uint32_t n) -> bool {
+                if (!wait_all(&ctl->kv_full[stage_of(n)], stage_parity(n))) return false;
+                next_wait = n + 1;
+                float4* kp = reinterpret_cast<float4*>(sKV + stage_of(n) * kStageBytes);
+                float4* klp = kp + kKBytes / 16;
+                for (uint32_t i = lane; i < kKBytes / 16; i += 32) {
+                    const float4 v = kp[i];
+                    const float4 hi = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y),
+                                                  tc::to_tf32(v.z), tc::to_tf32(v.w));
+                    kp[i] = hi;
+                    klp[i] = make_float4(tc::to_tf32(v.x - hi.x), tc::to_tf32(v.y - hi.y),
+                                         tc::to_tf32(v.z - hi.z), tc::to_tf32(v.w - hi.w));
+                }
+                tc::fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tc::fence_after_sync();
+                    const uint32_t ka = smem_addr(sKV + stage_of(n) * kStageBytes);
+                    const uint32_t kla = ka + kKBytes;
+                    const uint32_t ts = tmem + (n & 1u) * kKT;
 #pragma unroll
                     for (int k = 0; k < kHD / 8; ++k) {
-                        const uint32_t off = (k & 3) * 32u;  // 8 tf32 = 32 B within the atom
-                        const uint64_t ad = tc::sw128_desc(qa + (k >> 2) * kQAtom + off, 16, 1024);
-                        const uint64_t bd = tc::sw128_desc(ka + (k >> 2) * kKVAtom + off, 16, 1024);
-                        tc::mma_tf32(tS0 + (n & 1u) * 64u, ad, bd, kIdescS, k > 0);
+                        const uint32_t off = (k >> 2) * kKVAtom + (k & 3) * 32u;  // 8 tf32 = 32 B
+                        const uint64_t bhi = tc::sw128_desc(ka + off, 16, 1024);
+                        const uint64_t blo = tc::sw128_desc(kla + off, 16, 1024);
+                        tc::mma_tf32_ts(ts, tmem + kColQlo + 8u * k, bhi, kIdescS, k > 0);
+                        tc::mma_tf32_ts(ts, tmem + kColQhi + 8u * k, blo, kIdescS, true);
+                        tc::mma_tf32_ts(ts, tmem + kColQhi + 8u * k, bhi, kIdescS, true);
                     }
                     tc::commit(&ctl->s_full[n & 1u]);
                     issued_mma = true;
-                };
-                auto issue_o = [&](uint32_t n) {
-                    const int st = int(n & 1u);
+                }
+                __syncwarp();
+                return true;
+            };
+            auto issue_o = [&](uint32_t n) {
+                if (lane == 0) {
+                    tc::fence_after_sync();
                     const uint32_t pa = smem_addr(sP);
-                    const uint32_t va = smem_addr(sKV + st * kStageBytes + kKBytes);
+                    const uint32_t va = smem_addr(sVt);
 #pragma unroll
                     for (int k = 0; k < kKT / 8; ++k) {
-                        const uint64_t ad = tc::sw128_desc(pa + (k >> 2) * kPAtom + (k & 3) * 32u, 16, 1024);
-                        const uint64_t bd = tc::sw128_desc(va + k * 1024u, kKVAtom, 1024);
-                        tc::mma_tf32(tO, ad, bd, kIdescO, k > 0);
+                        const uint64_t phi = tc::sw128_desc(pa + k * 32u, 16, 1024);
+                        const uint64_t plo = tc::sw128_desc(pa + kPBytes + k * 32u, 16, 1024);
+                        const uint64_t vhi = tc::sw128_desc(va + k * 32u, 16, 1024);
+                        const uint64_t vlo = tc::sw128_desc(va + kVtBytes + k * 32u, 16, 1024);
+                        tc::mma_tf32(tO, plo, vhi, kIdescO, k > 0);
+                        tc::mma_tf32(tO, phi, vlo, kIdescO, true);
+                        tc::mma_tf32(tO, phi, vhi, kIdescO, true);
                     }
                     tc::commit(&ctl->o_full);
-                    tc::commit(&ctl->pv_done[st]);
-                };
+                    tc::commit(&ctl->pv_done[stage_of(n)]);
+                }
+                __syncwarp();
+            };
 
-                ok = load(n0, 0);
-                if (ok && ntiles > 1) ok = load(n0 + 1, 1);
-                if (ok) ok = wait_or_abort(&ctl->kv_full[n0 & 1u], (n0 >> 1) & 1u, ctl);
-                if (ok) {
-                    next_wait = n0 + 1;
-                    tc::fence_after_sync();
-                    issue_s(n0);
-                }
-                for (int t = 0; ok && t < ntiles; ++t) {
-                    const uint32_t n = n0 + t;
-                    if (t + 1 < ntiles) {
-                        ok = wait_or_abort(&ctl->kv_full[(n + 1) & 1u], ((n + 1) >> 1) & 1u, ctl);
-                        if (!ok) break;
-                        next_wait = n + 2;
-                        tc::fence_after_sync();
-                        issue_s(n + 1);
-                    }
-                    ok = wait_or_abort(&ctl->p_full, n & 1u, ctl);
+            bool ok = true;
+            for (int t = 0; ok && t < min(ntiles, kStages); ++t) ok = load(n0 + t, t);
+            if (ok) ok = stage_and_issue_s(n0);
+            for (int t = 0; ok && t < ntiles; ++t) {
+                const uint32_t n = n0 + t;
+                if (t + 1 < ntiles) {
+                    ok = stage_and_issue_s(n + 1);
                     if (!ok) break;
-                    tc::fence_after_sync();
-                    issue_o(n);
-                    if (t + 2 < ntiles) ok = load(n + 2, t + 2);
                 }
-                (void)ok;
+                ok = wait_all(&ctl->p_full, n & 1u);
+                if (!ok) break;
+                issue_o(n);
+                if (t + kStages < ntiles) ok = load(n + kStages, t + kStages);
             }
-            __syncwarp();
         } else {
             // ------------------------------------------------------------ softmax warps
-            const int row = tid;
+            const int row = tid;  // query row, TMEM lane, and (for V^T) head dimension
             const int qpos = first_pos + r0 + row;
             const uint32_t lane_off = uint32_t(warp * 32) << 16;
+            const int vt_atom = row >> 5;   // V atom holding dimension `row`
+            const int vt_dd = row & 31;     // dimension within the atom
             float o[kHD];
 #pragma unroll
             for (int j = 0; j < kHD; ++j) o[j] = 0.f;
@@ -287,27 +333,9 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 }
                 tc::fence_after_sync();
                 float sc[kKT];
-                tc::tmem_ld32(tS0 + (n & 1u) * 64u + lane_off, sc);
-                tc::tmem_ld32(tS0 + (n & 1u) * 64u + 32u + lane_off, sc + 32);
+                tc::tmem_ld32(tmem + (n & 1u) * kKT + lane_off, sc);
                 tc::tmem_ld_wait();
                 const int kbase = t * kKT;
-                if (nk - kbase < kKT) {
-                    // last, partial tile: zero V rows past the visible keys so that
-                    // their zero weights cannot meet stale non-finite data
-                    if (!wait_or_abort(&ctl->kv_full[n & 1u], (n >> 1) & 1u, ctl)) {
-                        ok = false;
-                        break;
-                    }
-                    unsigned char* sV = sKV + (n & 1u) * kStageBytes + kKBytes;
-                    const int v0 = nk - kbase;
-                    for (int idx = tid; idx < (kKT - v0) * 32; idx += kQT) {
-                        const int r = v0 + idx / 32;
-                        const int c = idx % 32;
-                        *reinterpret_cast<float4*>(sV + (c >> 3) * kKVAtom + r * 128 + (c & 7) * 16) =
-                            make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-                    tc::fence_async_smem();
-                }
                 float cm = -INFINITY;
 #pragma unroll
                 for (int j = 0; j < kKT; ++j) {
@@ -326,6 +354,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 l_run = fmaf(l_run, alpha, ps);
                 m_run = m_new;
                 if (t > 0) {
+                    // previous tile's P.V: also frees the P and V^T buffers
                     if (!wait_or_abort(&ctl->o_full, (n - 1) & 1u, ctl)) {
                         ok = false;
                         break;
@@ -340,14 +369,47 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                         for (int j = 0; j < 32; ++j) o[c * 32 + j] = fmaf(o[c * 32 + j], alpha_prev, ov[j]);
                     }
                 }
-                // P (tf32) -> shared memory, 128B-swizzled K-major
+                // P -> shared memory as tf32 hi / lo parts, 128B-swizzled K-major
 #pragma unroll
                 for (int c = 0; c < kKT / 4; ++c) {
-                    float4 v = make_float4(tc::to_tf32(sc[4 * c]), tc::to_tf32(sc[4 * c + 1]),
-                                           tc::to_tf32(sc[4 * c + 2]), tc::to_tf32(sc[4 * c + 3]));
-                    const int atom = c >> 3;
-                    const int pos = (c & 7) ^ (row & 7);
-                    *reinterpret_cast<float4*>(sP + atom * kPAtom + row * 128 + pos * 16) = v;
+                    float hi[4], lo[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        hi[e] = tc::to_tf32(sc[4 * c + e]);
+                        lo[e] = tc::to_tf32(sc[4 * c + e] - hi[e]);
+                    }
+                    const int pos = c ^ (row & 7);
+                    *reinterpret_cast<float4*>(sP + row * 128 + pos * 16) =
+                        make_float4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<float4*>(sP + kPBytes + row * 128 + pos * 16) =
+                        make_float4(lo[0], lo[1], lo[2], lo[3]);
+                }
+                // V^T row `row` (tf32; zero past the visible keys)
+                if (!wait_or_abort(&ctl->kv_full[stage_of(n)], stage_parity(n), ctl)) {
+                    ok = false;
+                    break;
+                }
+                {
+                    const unsigned char* sV = sKV + stage_of(n) * kStageBytes + 2 * kKBytes +
+                                              vt_atom * kKVAtom + (vt_dd & 3) * 4;
+                    const int nvk = nk - kbase;
+#pragma unroll
+                    for (int c = 0; c < kKT / 4; ++c) {
+                        float hi[4], lo[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int k = 4 * c + e;
+                            const float x = *reinterpret_cast<const float*>(
+                                sV + k * 128 + (((vt_dd >> 2) ^ (k & 7)) * 16));
+                            hi[e] = k < nvk ? tc::to_tf32(x) : 0.f;
+                            lo[e] = k < nvk ? tc::to_tf32(x - hi[e]) : 0.f;
+                        }
+                        const int pos = c ^ (row & 7);
+                        *reinterpret_cast<float4*>(sVt + row * 128 + pos * 16) =
+                            make_float4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<float4*>(sVt + kVtBytes + row * 128 + pos * 16) =
+                            make_float4(lo[0], lo[1], lo[2], lo[3]);
+                    }
                 }
                 tc::fence_async_smem();
                 tc::fence_before_sync();
@@ -387,7 +449,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     // before its shared memory and TMEM are released.
     if (warp == 4 && lane == 0) {
         for (uint32_t n = next_wait; n < next_load; ++n) {
-            mbar_wait(&ctl->kv_full[n & 1u], (n >> 1) & 1u);
+            mbar_wait(&ctl->kv_full[stage_of(n)], stage_parity(n));
         }
         if (issued_mma) {
             tc::commit(&ctl->drain);
