@@ -224,6 +224,17 @@ def reference_main(args, spec):
     return 0
 
 
+def cuda_view(ptr: int, shape, dev):
+    """float32 torch tensor over device memory owned elsewhere (the engine)."""
+    import torch
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4",
+                                    "data": (ptr, False), "version": 3}
+
+    return torch.as_tensor(_Mem(), device=dev)
+
+
 def workload_config(spec) -> dict:
     return {"workload": {"decode": "decode paged attention (64 seqs, ctx U[512,4096])",
                          "mixed": "mixed prefill+decode super-batch (8 prefills U[512,2048] "
@@ -266,10 +277,19 @@ def nvllm_main(args, spec):
         spec = make_batch(args.workload, seed=args.seed + rank)
     lay = nvllm.KVLayout(spec.num_blocks, 1, spec.block_size, spec.num_heads, spec.head_dim)
     D = spec.hidden
+    # The arenas belong to the host engine (libnvllm_host: allocator, pinned
+    # metadata upload, host-row attention); the device-resident loop drives the
+    # kernels on the same arenas through libnvllm's C ABI.
+    from nvllm.host import Engine
+    eng = Engine(lay, max_seqs=spec.num_seqs, max_tokens=spec.n_tokens,
+                 max_blocks_per_seq=spec.block_tables.shape[1], device=local)
+    k_ptr, v_ptr = eng.arenas()
+    ka = cuda_view(k_ptr, lay.arena_shape(), dev)
+    va = cuda_view(v_ptr, lay.arena_shape(), dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000 + rank)
-    ka = torch.empty(lay.arena_shape(), dtype=torch.float32, device=dev).normal_(generator=gen)
-    va = torch.empty_like(ka).normal_(generator=gen)
+    ka.normal_(generator=gen)
+    va.normal_(generator=gen)
     n = spec.n_tokens
     q = torch.randn((n, D), generator=gen, device=dev)
     k = torch.randn((n, D), generator=gen, device=dev)
@@ -332,25 +352,27 @@ def nvllm_main(args, spec):
     elapsed_max = max_over_ranks(elapsed)
     attn_max = max_over_ranks(attn_s)
 
-    # ---- end to end through the C ABI with host buffers -----------------
-    h_q = torch.empty((n, D), dtype=torch.float32, pin_memory=True).copy_(q)
-    h_k = torch.empty_like(h_q, pin_memory=True).copy_(k)
-    h_v = torch.empty_like(h_q, pin_memory=True).copy_(v)
-    h_out = torch.empty_like(h_q, pin_memory=True)
-    h_meta = [torch.from_numpy(x).pin_memory() for x in
-              (spec.block_tables, spec.cu_seqlens_q, spec.ctx_lens, spec.slot_mapping())]
-    d_meta = [bt, cu, ctx, slots]
-    h2d = sum(t.numel() * t.element_size() for t in [h_q, h_k, h_v, *h_meta])
-    d2h = h_out.numel() * h_out.element_size()
+    # ---- end to end through the engine's C ABI with host buffers ---------
+    # per step: pack + one pinned upload of the metadata, H2D of the Q/K/V rows
+    # from the engine's pinned buffers, KV write + attention, D2H of the output
+    torch.cuda.synchronize(dev)
+    h_q, h_k, h_v, h_out = (b[:n] for b in eng.pinned)
+    h_q[:] = q.cpu().numpy()
+    h_k[:] = k.cpu().numpy()
+    h_v[:] = v.cpu().numpy()
+    nc = np.ascontiguousarray(spec.ctx_lens - spec.q_lens, np.int32)
+    tl = np.ascontiguousarray(spec.ctx_lens, np.int32)
+    nbs = (spec.ctx_lens + spec.block_size - 1) // spec.block_size
+    ids, lens = eng.prepare_tables([spec.block_tables[s_, :nbs[s_]] for s_ in range(spec.num_seqs)])
+    from nvllm.host import host_lib
+    meta_bytes = int(host_lib().nvllm_metadata_bytes(spec.num_seqs, n, spec.block_tables.shape[1]))
+    h2d = meta_bytes + 3 * n * D * 4
+    d2h = n * D * 4
+    estream = torch.cuda.ExternalStream(eng.stream(), device=dev)
 
     def e2e_step():
-        q.copy_(h_q, non_blocking=True)
-        k.copy_(h_k, non_blocking=True)
-        v.copy_(h_v, non_blocking=True)
-        for d_, h_ in zip(d_meta, h_meta):
-            d_.copy_(h_, non_blocking=True)
-        step()
-        h_out.copy_(out, non_blocking=True)
+        eng.begin_step_raw(nc, tl, ids, lens)
+        eng.attention(0, h_q, h_k, h_v, h_out, precision)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -359,10 +381,10 @@ def nvllm_main(args, spec):
     torch.cuda.synchronize(dev)
     f0 = torch.cuda.Event(enable_timing=True)
     f1 = torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
+    f0.record(estream)
     for _ in range(args.steps):
         e2e_step()
-    f1.record(stream)
+    f1.record(estream)
     torch.cuda.synchronize(dev)
     barrier()
     e2e_elapsed = max_over_ranks(f0.elapsed_time(f1) / 1e3)
@@ -370,6 +392,8 @@ def nvllm_main(args, spec):
     status = nvllm.get_last_error(stream)
     if status != nvllm.OK:
         raise RuntimeError(f"device status {nvllm.status_string(status)}")
+    del ka, va  # views of the engine's arenas
+    eng.close()
 
     tokens = n * args.steps * world
     value = tokens / elapsed_max
@@ -396,7 +420,9 @@ def nvllm_main(args, spec):
                      "ms_per_launch": attn_max * 1e3,
                      "traffic": profile_traffic(spec.name)},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+                "d2h_bytes_per_step": d2h,
+                "path": "libnvllm_host engine C ABI: nvllm_engine_begin_step + "
+                        "nvllm_engine_attention (host rows)"},
         "gpu_launches": KERNELS_PER_STEP * args.steps * 2 + (args.steps if max_q > 1 else 0) * 2,
         "clocks": clocks,
     }

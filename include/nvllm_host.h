@@ -1,0 +1,95 @@
+/*
+ * nvllm host library (libnvllm_host.so): the engine-side half of the boundary,
+ * C ABI over the C++23 classes in nano-vllm-cpp26_b200/host/.
+ *
+ * - Block allocator: the reference BlockManager's semantics
+ *   (PagedKVCache::allocate_block / allocate_blocks / free_blocks,
+ *   src/kv_cache.cpp:23-55): FIFO free list, all-or-nothing allocation.
+ *   Host only, no GPU needed.
+ * - Metadata packer: selective token flattening (src/model.cpp:138-159) and
+ *   the slot mapping (src/model.cpp:192-194) packed into one int32 buffer.
+ *   Host only.
+ * - Engine: per-device K/V arenas in HBM with their allocator, one pinned
+ *   metadata upload per iteration, and a per-layer attention step with host
+ *   rows; the replacement of steps 3c/3d of forward_batch
+ *   (src/model.cpp:188-260) on the engine thread (src/engine.cpp:212-213).
+ *
+ * Block ids are int64 (the reference's BlockId is size_t). Status codes:
+ * NVLLM_OK, NVLLM_HOST_OUT_OF_BLOCKS, NVLLM_HOST_INVALID_BLOCK, or the
+ * nvllm_status values of nvllm.h.
+ */
+#ifndef NVLLM_HOST_H
+#define NVLLM_HOST_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "nvllm.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum nvllm_host_status {
+    NVLLM_HOST_OUT_OF_BLOCKS = 100, /* KVError::OutOfPhysicalBlocks */
+    NVLLM_HOST_INVALID_BLOCK = 101, /* free of an unallocated or out-of-range id */
+    NVLLM_HOST_PACK_ERROR = 102     /* tables too short / too wide, bad lengths */
+};
+
+/* ---- block allocator (kv_cache.hpp:48-55) -------------------------------- */
+typedef struct nvllm_block_allocator nvllm_block_allocator;
+nvllm_block_allocator* nvllm_block_allocator_create(int64_t num_blocks);
+void nvllm_block_allocator_destroy(nvllm_block_allocator* a);
+int nvllm_block_allocator_allocate_block(nvllm_block_allocator* a, int64_t* out_id);
+int nvllm_block_allocator_allocate_blocks(nvllm_block_allocator* a, int64_t count,
+                                          int64_t* out_ids);
+int nvllm_block_allocator_free_blocks(nvllm_block_allocator* a, const int64_t* ids, int64_t n);
+int64_t nvllm_block_allocator_num_free(const nvllm_block_allocator* a);
+
+/* ---- metadata packer (model.cpp:138-159, :192-194) ------------------------ */
+typedef struct nvllm_metadata_offsets {
+    int64_t cu_seqlens_q, context_lens, last_token_idx, slot_mapping, block_tables, bytes;
+    int32_t num_seqs, num_tokens, max_blocks, max_query_len, max_context_len;
+} nvllm_metadata_offsets;
+
+/* Sequence s: num_computed[s] cached tokens, total_len[s] tokens after the
+ * step, table_lens[s] block ids taken in order from block_ids. */
+size_t nvllm_metadata_bytes(int32_t num_seqs, int32_t num_tokens, int32_t max_blocks);
+int nvllm_pack_metadata(int32_t num_seqs, const int32_t* num_computed, const int32_t* total_len,
+                        const int64_t* block_ids, const int32_t* table_lens, int32_t block_size,
+                        int32_t max_blocks, void* buf, size_t buf_bytes,
+                        nvllm_metadata_offsets* out);
+
+/* ---- engine --------------------------------------------------------------- */
+typedef struct nvllm_engine nvllm_engine;
+typedef struct nvllm_engine_config {
+    nvllm_kv_layout layout;
+    int32_t max_seqs;
+    int32_t max_tokens;
+    int32_t max_blocks_per_seq;
+    int32_t device;
+} nvllm_engine_config;
+
+int nvllm_engine_create(const nvllm_engine_config* cfg, nvllm_engine** out);
+void nvllm_engine_destroy(nvllm_engine* e);
+int nvllm_engine_allocate_blocks(nvllm_engine* e, int64_t count, int64_t* out_ids);
+int nvllm_engine_free_blocks(nvllm_engine* e, const int64_t* ids, int64_t n);
+int64_t nvllm_engine_num_free_blocks(const nvllm_engine* e);
+/* Flattens the batch and uploads its metadata (one cudaMemcpyAsync). */
+int nvllm_engine_begin_step(nvllm_engine* e, int32_t num_seqs, const int32_t* num_computed,
+                            const int32_t* total_len, const int64_t* block_ids,
+                            const int32_t* table_lens);
+/* One layer, host rows [num_tokens, H*hd]; returns when out holds the result. */
+int nvllm_engine_attention(nvllm_engine* e, int32_t layer, const float* q, const float* k,
+                           const float* v, float* out, int32_t precision);
+/* The engine's pinned row buffers (pass them to nvllm_engine_attention to skip
+ * the staging copy), its device arenas and its CUDA stream. */
+int nvllm_engine_host_buffers(nvllm_engine* e, float** q, float** k, float** v, float** out);
+int nvllm_engine_arenas(nvllm_engine* e, float** k_arena, float** v_arena);
+void* nvllm_engine_stream(nvllm_engine* e);
+int32_t nvllm_engine_step_tokens(const nvllm_engine* e);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NVLLM_HOST_H */

@@ -1,0 +1,168 @@
+#include "engine.hpp"
+
+#include <cmath>
+#include <cstring>
+
+namespace nvllm {
+
+namespace {
+
+std::unexpected<EngineError> cuda_error(cudaError_t e) {
+    return std::unexpected(EngineError{EngineError::Kind::Cuda, int(e)});
+}
+
+#define NVLLM_CUDA_TRY(expr)                        \
+    do {                                            \
+        const cudaError_t e_ = (expr);              \
+        if (e_ != cudaSuccess) return cuda_error(e_); \
+    } while (0)
+
+}  // namespace
+
+AttentionEngine::AttentionEngine(const EngineConfig& cfg)
+    : cfg_(cfg), allocator_(static_cast<std::size_t>(cfg.layout.num_blocks)) {}
+
+std::expected<std::unique_ptr<AttentionEngine>, EngineError> AttentionEngine::create(
+    const EngineConfig& cfg) {
+    const nvllm_kv_layout& L = cfg.layout;
+    if (L.num_blocks <= 0 || L.num_layers <= 0 || L.block_size <= 0 || L.num_heads <= 0 ||
+        L.head_dim <= 0 || cfg.max_seqs <= 0 || cfg.max_tokens <= 0 ||
+        cfg.max_blocks_per_seq <= 0 || cfg.device < 0) {
+        return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    }
+    std::unique_ptr<AttentionEngine> eng(new AttentionEngine(cfg));
+    if (auto r = eng->init(); !r) return std::unexpected(r.error());
+    return eng;
+}
+
+std::expected<void, EngineError> AttentionEngine::init() {
+    const nvllm_kv_layout& L = cfg_.layout;
+    NVLLM_CUDA_TRY(cudaSetDevice(cfg_.device));
+    NVLLM_CUDA_TRY(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    row_floats_ = std::size_t(L.num_heads) * std::size_t(L.head_dim);
+    const std::size_t arena_bytes = std::size_t(L.num_blocks) * std::size_t(L.num_layers) *
+                                    std::size_t(L.block_size) * row_floats_ * sizeof(float);
+    NVLLM_CUDA_TRY(cudaMalloc(&d_k_, arena_bytes));
+    NVLLM_CUDA_TRY(cudaMalloc(&d_v_, arena_bytes));
+    // the reference zero-fills its arenas (src/kv_cache.cpp:14-15)
+    NVLLM_CUDA_TRY(cudaMemsetAsync(d_k_, 0, arena_bytes, stream_));
+    NVLLM_CUDA_TRY(cudaMemsetAsync(d_v_, 0, arena_bytes, stream_));
+
+    meta_capacity_ = metadata_layout(cfg_.max_seqs, cfg_.max_tokens, cfg_.max_blocks_per_seq).bytes;
+    for (int i = 0; i < 2; ++i) {
+        NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_meta_[i]), meta_capacity_));
+        NVLLM_CUDA_TRY(cudaEventCreateWithFlags(&meta_done_[i], cudaEventDisableTiming));
+        NVLLM_CUDA_TRY(cudaEventRecord(meta_done_[i], stream_));
+    }
+    NVLLM_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&d_meta_), meta_capacity_));
+
+    const std::size_t rows_bytes = std::size_t(cfg_.max_tokens) * row_floats_ * sizeof(float);
+    NVLLM_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&d_rows_), 4 * rows_bytes));
+    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_q_), rows_bytes));
+    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_k_), rows_bytes));
+    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_v_), rows_bytes));
+    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_out_), rows_bytes));
+
+    const int32_t max_ctx = cfg_.max_blocks_per_seq * L.block_size;
+    ws_bytes_ = nvllm_paged_attention_workspace_size(cfg_.max_seqs, cfg_.max_tokens, max_ctx, &L);
+    if (ws_bytes_ == 0) return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    NVLLM_CUDA_TRY(cudaMalloc(&d_ws_, ws_bytes_));
+    NVLLM_CUDA_TRY(cudaStreamSynchronize(stream_));
+    return {};
+}
+
+AttentionEngine::~AttentionEngine() {
+    if (stream_ != nullptr) {
+        cudaSetDevice(cfg_.device);
+        cudaStreamSynchronize(stream_);
+    }
+    for (int i = 0; i < 2; ++i) {
+        if (meta_done_[i]) cudaEventDestroy(meta_done_[i]);
+        if (h_meta_[i]) cudaFreeHost(h_meta_[i]);
+    }
+    for (float* p : {h_q_, h_k_, h_v_, h_out_}) {
+        if (p) cudaFreeHost(p);
+    }
+    if (d_meta_) cudaFree(d_meta_);
+    if (d_rows_) cudaFree(d_rows_);
+    if (d_ws_) cudaFree(d_ws_);
+    if (d_k_) cudaFree(d_k_);
+    if (d_v_) cudaFree(d_v_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+std::expected<void, EngineError> AttentionEngine::begin_step(std::span<const SequenceView> seqs) {
+    if (seqs.size() > std::size_t(cfg_.max_seqs)) {
+        return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    }
+    NVLLM_CUDA_TRY(cudaSetDevice(cfg_.device));
+    // the staging buffer about to be refilled must have finished its last upload
+    NVLLM_CUDA_TRY(cudaEventSynchronize(meta_done_[meta_slot_]));
+    auto packed = pack_metadata(
+        seqs, cfg_.layout.block_size, cfg_.max_blocks_per_seq,
+        std::span<std::byte>(reinterpret_cast<std::byte*>(h_meta_[meta_slot_]), meta_capacity_));
+    if (!packed) return std::unexpected(EngineError{EngineError::Kind::Pack, int(packed.error())});
+    if (packed->num_tokens > cfg_.max_tokens) {
+        return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    }
+    NVLLM_CUDA_TRY(cudaMemcpyAsync(d_meta_, h_meta_[meta_slot_], packed->bytes,
+                                   cudaMemcpyHostToDevice, stream_));
+    NVLLM_CUDA_TRY(cudaEventRecord(meta_done_[meta_slot_], stream_));
+    meta_slot_ ^= 1;
+    step_ = *packed;
+    have_step_ = true;
+    return {};
+}
+
+std::expected<void, EngineError> AttentionEngine::attention_device(int32_t layer, const float* d_q,
+                                                                   const float* d_k,
+                                                                   const float* d_v, float* d_out,
+                                                                   int32_t precision) {
+    if (!have_step_) return std::unexpected(EngineError{EngineError::Kind::NoStep, 0});
+    if (step_.num_tokens == 0) return {};
+    const nvllm_kv_layout& L = cfg_.layout;
+    const auto* meta = d_meta_;
+    const auto* cu = reinterpret_cast<const int32_t*>(meta + step_.cu_off);
+    const auto* ctx = reinterpret_cast<const int32_t*>(meta + step_.ctx_off);
+    const auto* slots = reinterpret_cast<const int32_t*>(meta + step_.slot_off);
+    const auto* tables = reinterpret_cast<const int32_t*>(meta + step_.table_off);
+    int rc = nvllm_reshape_and_cache(d_k, d_v, d_k_, d_v_, slots, step_.num_tokens, layer, &L,
+                                     stream_);
+    if (rc != NVLLM_OK) return std::unexpected(EngineError{EngineError::Kind::Kernel, rc});
+    // softmax scale of the reference, src/model.cpp:205
+    const float scale = 1.0f / std::sqrt(static_cast<float>(L.head_dim));
+    rc = nvllm_paged_attention(d_out, d_q, d_k_, d_v_, tables, step_.max_blocks, cu, ctx,
+                               step_.num_seqs, step_.max_query_len, step_.max_context_len, layer,
+                               scale, precision, d_ws_, ws_bytes_, &L, stream_);
+    if (rc != NVLLM_OK) return std::unexpected(EngineError{EngineError::Kind::Kernel, rc});
+    return {};
+}
+
+std::expected<void, EngineError> AttentionEngine::attention(int32_t layer, const float* q,
+                                                            const float* k, const float* v,
+                                                            float* out, int32_t precision) {
+    if (!have_step_) return std::unexpected(EngineError{EngineError::Kind::NoStep, 0});
+    NVLLM_CUDA_TRY(cudaSetDevice(cfg_.device));
+    const std::size_t n = std::size_t(step_.num_tokens);
+    if (n == 0) return {};
+    const std::size_t bytes = n * row_floats_ * sizeof(float);
+    const std::size_t stride = std::size_t(cfg_.max_tokens) * row_floats_;
+    float* dq = d_rows_;
+    float* dk = d_rows_ + stride;
+    float* dv = d_rows_ + 2 * stride;
+    float* dout = d_rows_ + 3 * stride;
+    const float* srcs[3] = {q, k, v};
+    float* pinned[3] = {h_q_, h_k_, h_v_};
+    float* dsts[3] = {dq, dk, dv};
+    for (int i = 0; i < 3; ++i) {
+        if (srcs[i] != pinned[i]) std::memcpy(pinned[i], srcs[i], bytes);
+        NVLLM_CUDA_TRY(cudaMemcpyAsync(dsts[i], pinned[i], bytes, cudaMemcpyHostToDevice, stream_));
+    }
+    if (auto r = attention_device(layer, dq, dk, dv, dout, precision); !r) return r;
+    NVLLM_CUDA_TRY(cudaMemcpyAsync(h_out_, dout, bytes, cudaMemcpyDeviceToHost, stream_));
+    NVLLM_CUDA_TRY(cudaStreamSynchronize(stream_));
+    if (out != h_out_) std::memcpy(out, h_out_, bytes);
+    return {};
+}
+
+}  // namespace nvllm

@@ -1,0 +1,109 @@
+// AttentionEngine: the per-device host object that replaces steps 3c/3d of
+// TransformerModel::forward_batch (src/model.cpp:188-260) for an engine thread
+// (src/engine.cpp:212-213).
+//
+// It owns, on one CUDA device:
+//   * the K and V arenas in HBM, [num_blocks, num_layers, block_size, H*hd]
+//     fp32 (the reference's PagedKVCache arena, include/nano_vllm/kv_cache.hpp:30-33),
+//     and their BlockAllocator (the reference's allocator semantics);
+//   * the int32 device mirror of the step's metadata, filled by ONE pinned
+//     cudaMemcpyAsync per iteration from a double-buffered pinned staging area;
+//   * pinned host buffers for the step's Q/K/V rows and the attention output,
+//     a device workspace for nvllm_paged_attention, and a CUDA stream.
+//
+// Per iteration: begin_step(sequences) packs and uploads the metadata; then per
+// layer attention(...) copies that layer's Q/K/V rows in, runs
+// nvllm_reshape_and_cache + nvllm_paged_attention and copies the output back
+// (synchronously, like the reference's loop), or attention_device(...) runs on
+// caller-owned device rows asynchronously.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <expected>
+#include <memory>
+#include <span>
+
+#include "../../include/nvllm.h"
+#include "block_allocator.hpp"
+#include "metadata.hpp"
+
+namespace nvllm {
+
+struct EngineConfig {
+    nvllm_kv_layout layout{};
+    int32_t max_seqs = 0;          // sequences per step
+    int32_t max_tokens = 0;        // new tokens (flattened rows) per step
+    int32_t max_blocks_per_seq = 0;
+    int32_t device = 0;
+};
+
+struct EngineError {
+    enum class Kind { Invalid, Cuda, Pack, Kernel, NoStep } kind;
+    int code = 0;  // cudaError_t, PackError or nvllm status, by kind
+};
+
+class AttentionEngine {
+public:
+    static std::expected<std::unique_ptr<AttentionEngine>, EngineError> create(
+        const EngineConfig& cfg);
+    ~AttentionEngine();
+    AttentionEngine(const AttentionEngine&) = delete;
+    AttentionEngine& operator=(const AttentionEngine&) = delete;
+
+    BlockAllocator& allocator() noexcept { return allocator_; }
+    const EngineConfig& config() const noexcept { return cfg_; }
+    float* k_arena() noexcept { return d_k_; }
+    float* v_arena() noexcept { return d_v_; }
+    cudaStream_t stream() noexcept { return stream_; }
+    // pinned staging for one layer's rows ([max_tokens, H*hd] each)
+    float* host_query() noexcept { return h_q_; }
+    float* host_key() noexcept { return h_k_; }
+    float* host_value() noexcept { return h_v_; }
+    float* host_output() noexcept { return h_out_; }
+    const MetadataLayout& step() const noexcept { return step_; }
+
+    // Flattens the batch and uploads its metadata (one cudaMemcpyAsync).
+    std::expected<void, EngineError> begin_step(std::span<const SequenceView> seqs);
+
+    // One layer with host rows: H2D of Q/K/V, KV write, attention, D2H of the
+    // output; returns once `out` holds the result. Rows that already live in
+    // the engine's pinned buffers are not copied again.
+    std::expected<void, EngineError> attention(int32_t layer, const float* q, const float* k,
+                                               const float* v, float* out, int32_t precision);
+
+    // One layer with device rows, asynchronous on stream().
+    std::expected<void, EngineError> attention_device(int32_t layer, const float* d_q,
+                                                      const float* d_k, const float* d_v,
+                                                      float* d_out, int32_t precision);
+
+private:
+    explicit AttentionEngine(const EngineConfig& cfg);
+    std::expected<void, EngineError> init();
+
+    EngineConfig cfg_;
+    BlockAllocator allocator_;
+    MetadataLayout step_{};
+    bool have_step_ = false;
+    std::size_t meta_capacity_ = 0;
+    std::size_t row_floats_ = 0;
+    size_t ws_bytes_ = 0;
+    int meta_slot_ = 0;
+
+    cudaStream_t stream_ = nullptr;
+    cudaEvent_t meta_done_[2] = {nullptr, nullptr};
+    unsigned char* h_meta_[2] = {nullptr, nullptr};
+    unsigned char* d_meta_ = nullptr;
+    float* d_k_ = nullptr;
+    float* d_v_ = nullptr;
+    float* d_rows_ = nullptr;  // Q, K, V, out rows on the device
+    void* d_ws_ = nullptr;
+    float* h_q_ = nullptr;
+    float* h_k_ = nullptr;
+    float* h_v_ = nullptr;
+    float* h_out_ = nullptr;
+};
+
+}  // namespace nvllm

@@ -1,0 +1,226 @@
+// extern "C" wrappers of the host library (declared in include/nvllm_host.h).
+#include <memory>
+#include <new>
+#include <vector>
+
+#include "../../include/nvllm_host.h"
+#include "block_allocator.hpp"
+#include "engine.hpp"
+#include "metadata.hpp"
+
+struct nvllm_block_allocator {
+    nvllm::BlockAllocator impl;
+    explicit nvllm_block_allocator(std::size_t n) : impl(n) {}
+};
+
+struct nvllm_engine {
+    std::unique_ptr<nvllm::AttentionEngine> impl;
+};
+
+namespace {
+
+int kv_status(nvllm::KVError e) {
+    return e == nvllm::KVError::OutOfPhysicalBlocks ? NVLLM_HOST_OUT_OF_BLOCKS
+                                                    : NVLLM_HOST_INVALID_BLOCK;
+}
+
+int engine_status(const nvllm::EngineError& e) {
+    switch (e.kind) {
+        case nvllm::EngineError::Kind::Cuda: return NVLLM_ERR_CUDA;
+        case nvllm::EngineError::Kind::Pack: return NVLLM_HOST_PACK_ERROR;
+        case nvllm::EngineError::Kind::Kernel: return e.code;
+        default: return NVLLM_ERR_INVALID;
+    }
+}
+
+int allocate(nvllm::BlockAllocator& a, int64_t count, int64_t* out) {
+    if (count < 0 || (count > 0 && out == nullptr)) return NVLLM_ERR_INVALID;
+    auto r = a.allocate_blocks(static_cast<std::size_t>(count));
+    if (!r) return kv_status(r.error());
+    for (std::size_t i = 0; i < r->size(); ++i) out[i] = static_cast<int64_t>((*r)[i]);
+    return NVLLM_OK;
+}
+
+int release(nvllm::BlockAllocator& a, const int64_t* ids, int64_t n) {
+    if (n < 0 || (n > 0 && ids == nullptr)) return NVLLM_ERR_INVALID;
+    std::vector<nvllm::BlockId> v;
+    v.reserve(static_cast<std::size_t>(n));
+    for (int64_t i = 0; i < n; ++i) {
+        if (ids[i] < 0) return NVLLM_HOST_INVALID_BLOCK;
+        v.push_back(static_cast<nvllm::BlockId>(ids[i]));
+    }
+    auto r = a.free_blocks(v);
+    return r ? NVLLM_OK : kv_status(r.error());
+}
+
+// Builds the sequence views (tables copied into `storage`).
+bool make_views(int32_t num_seqs, const int32_t* num_computed, const int32_t* total_len,
+                const int64_t* block_ids, const int32_t* table_lens,
+                std::vector<nvllm::BlockId>& storage, std::vector<nvllm::SequenceView>& views) {
+    if (num_seqs < 0) return false;
+    if (num_seqs == 0) return true;
+    if (!num_computed || !total_len || !table_lens) return false;
+    std::size_t total = 0;
+    for (int32_t s = 0; s < num_seqs; ++s) {
+        if (table_lens[s] < 0) return false;
+        total += static_cast<std::size_t>(table_lens[s]);
+    }
+    if (total > 0 && block_ids == nullptr) return false;
+    storage.resize(total);
+    for (std::size_t i = 0; i < total; ++i) {
+        if (block_ids[i] < 0) return false;
+        storage[i] = static_cast<nvllm::BlockId>(block_ids[i]);
+    }
+    views.resize(static_cast<std::size_t>(num_seqs));
+    std::size_t off = 0;
+    for (int32_t s = 0; s < num_seqs; ++s) {
+        const std::size_t len = static_cast<std::size_t>(table_lens[s]);
+        views[s] = nvllm::SequenceView{num_computed[s], total_len[s],
+                                       std::span<const nvllm::BlockId>(storage.data() + off, len)};
+        off += len;
+    }
+    return true;
+}
+
+void fill_offsets(const nvllm::MetadataLayout& m, nvllm_metadata_offsets* out) {
+    out->cu_seqlens_q = int64_t(m.cu_off);
+    out->context_lens = int64_t(m.ctx_off);
+    out->last_token_idx = int64_t(m.last_off);
+    out->slot_mapping = int64_t(m.slot_off);
+    out->block_tables = int64_t(m.table_off);
+    out->bytes = int64_t(m.bytes);
+    out->num_seqs = m.num_seqs;
+    out->num_tokens = m.num_tokens;
+    out->max_blocks = m.max_blocks;
+    out->max_query_len = m.max_query_len;
+    out->max_context_len = m.max_context_len;
+}
+
+}  // namespace
+
+extern "C" {
+
+nvllm_block_allocator* nvllm_block_allocator_create(int64_t num_blocks) {
+    if (num_blocks < 0) return nullptr;
+    return new (std::nothrow) nvllm_block_allocator(static_cast<std::size_t>(num_blocks));
+}
+
+void nvllm_block_allocator_destroy(nvllm_block_allocator* a) { delete a; }
+
+int nvllm_block_allocator_allocate_block(nvllm_block_allocator* a, int64_t* out_id) {
+    if (a == nullptr || out_id == nullptr) return NVLLM_ERR_INVALID;
+    auto r = a->impl.allocate_block();
+    if (!r) return kv_status(r.error());
+    *out_id = static_cast<int64_t>(*r);
+    return NVLLM_OK;
+}
+
+int nvllm_block_allocator_allocate_blocks(nvllm_block_allocator* a, int64_t count,
+                                          int64_t* out_ids) {
+    return a ? allocate(a->impl, count, out_ids) : NVLLM_ERR_INVALID;
+}
+
+int nvllm_block_allocator_free_blocks(nvllm_block_allocator* a, const int64_t* ids, int64_t n) {
+    return a ? release(a->impl, ids, n) : NVLLM_ERR_INVALID;
+}
+
+int64_t nvllm_block_allocator_num_free(const nvllm_block_allocator* a) {
+    return a ? static_cast<int64_t>(a->impl.num_free_blocks()) : -1;
+}
+
+size_t nvllm_metadata_bytes(int32_t num_seqs, int32_t num_tokens, int32_t max_blocks) {
+    if (num_seqs < 0 || num_tokens < 0 || max_blocks < 0) return 0;
+    return nvllm::metadata_layout(num_seqs, num_tokens, max_blocks).bytes;
+}
+
+int nvllm_pack_metadata(int32_t num_seqs, const int32_t* num_computed, const int32_t* total_len,
+                        const int64_t* block_ids, const int32_t* table_lens, int32_t block_size,
+                        int32_t max_blocks, void* buf, size_t buf_bytes,
+                        nvllm_metadata_offsets* out) {
+    std::vector<nvllm::BlockId> storage;
+    std::vector<nvllm::SequenceView> views;
+    if (!make_views(num_seqs, num_computed, total_len, block_ids, table_lens, storage, views) ||
+        buf == nullptr || out == nullptr) {
+        return NVLLM_ERR_INVALID;
+    }
+    auto r = nvllm::pack_metadata(
+        views, block_size, max_blocks,
+        std::span<std::byte>(static_cast<std::byte*>(buf), buf_bytes));
+    if (!r) return NVLLM_HOST_PACK_ERROR;
+    fill_offsets(*r, out);
+    return NVLLM_OK;
+}
+
+int nvllm_engine_create(const nvllm_engine_config* cfg, nvllm_engine** out) {
+    if (cfg == nullptr || out == nullptr) return NVLLM_ERR_INVALID;
+    *out = nullptr;
+    nvllm::EngineConfig c;
+    c.layout = cfg->layout;
+    c.max_seqs = cfg->max_seqs;
+    c.max_tokens = cfg->max_tokens;
+    c.max_blocks_per_seq = cfg->max_blocks_per_seq;
+    c.device = cfg->device;
+    auto r = nvllm::AttentionEngine::create(c);
+    if (!r) return engine_status(r.error());
+    *out = new (std::nothrow) nvllm_engine{std::move(*r)};
+    return *out ? NVLLM_OK : NVLLM_ERR_INVALID;
+}
+
+void nvllm_engine_destroy(nvllm_engine* e) { delete e; }
+
+int nvllm_engine_allocate_blocks(nvllm_engine* e, int64_t count, int64_t* out_ids) {
+    return e ? allocate(e->impl->allocator(), count, out_ids) : NVLLM_ERR_INVALID;
+}
+
+int nvllm_engine_free_blocks(nvllm_engine* e, const int64_t* ids, int64_t n) {
+    return e ? release(e->impl->allocator(), ids, n) : NVLLM_ERR_INVALID;
+}
+
+int64_t nvllm_engine_num_free_blocks(const nvllm_engine* e) {
+    return e ? static_cast<int64_t>(e->impl->allocator().num_free_blocks()) : -1;
+}
+
+int nvllm_engine_begin_step(nvllm_engine* e, int32_t num_seqs, const int32_t* num_computed,
+                            const int32_t* total_len, const int64_t* block_ids,
+                            const int32_t* table_lens) {
+    if (e == nullptr) return NVLLM_ERR_INVALID;
+    std::vector<nvllm::BlockId> storage;
+    std::vector<nvllm::SequenceView> views;
+    if (!make_views(num_seqs, num_computed, total_len, block_ids, table_lens, storage, views)) {
+        return NVLLM_ERR_INVALID;
+    }
+    auto r = e->impl->begin_step(views);
+    return r ? NVLLM_OK : engine_status(r.error());
+}
+
+int nvllm_engine_attention(nvllm_engine* e, int32_t layer, const float* q, const float* k,
+                           const float* v, float* out, int32_t precision) {
+    if (e == nullptr) return NVLLM_ERR_INVALID;
+    if (e->impl->step().num_tokens > 0 && (!q || !k || !v || !out)) return NVLLM_ERR_INVALID;
+    auto r = e->impl->attention(layer, q, k, v, out, precision);
+    return r ? NVLLM_OK : engine_status(r.error());
+}
+
+int nvllm_engine_host_buffers(nvllm_engine* e, float** q, float** k, float** v, float** out) {
+    if (e == nullptr) return NVLLM_ERR_INVALID;
+    if (q) *q = e->impl->host_query();
+    if (k) *k = e->impl->host_key();
+    if (v) *v = e->impl->host_value();
+    if (out) *out = e->impl->host_output();
+    return NVLLM_OK;
+}
+
+int nvllm_engine_arenas(nvllm_engine* e, float** k_arena, float** v_arena) {
+    if (e == nullptr) return NVLLM_ERR_INVALID;
+    if (k_arena) *k_arena = e->impl->k_arena();
+    if (v_arena) *v_arena = e->impl->v_arena();
+    return NVLLM_OK;
+}
+
+void* nvllm_engine_stream(nvllm_engine* e) { return e ? e->impl->stream() : nullptr; }
+
+int32_t nvllm_engine_step_tokens(const nvllm_engine* e) {
+    return e ? e->impl->step().num_tokens : -1;
+}
+
+}  // extern "C"

@@ -1,10 +1,13 @@
-"""Builds libnvllm.so (the sm_100a kernels + C ABI) in-tree.
+"""Builds the two in-tree libraries.
 
     python -m nvllm.build          (from nano-vllm-cpp26_b200/)
 
-nvcc compiles every csrc/*.cu for sm_100a with relocatable device code and
-links them into lib/libnvllm.so; the static CUDA runtime is linked in so the
-library depends only on the driver.
+* lib/libnvllm.so: nvcc compiles every csrc/*.cu for sm_100a with relocatable
+  device code and links them; the static CUDA runtime is linked in so the
+  library depends only on the driver.
+* lib/libnvllm_host.so: g++ -std=c++23 compiles host/*.cpp (block allocator,
+  metadata packer, engine, their C ABI) against libnvllm.so and the static
+  CUDA runtime.
 """
 from __future__ import annotations
 
@@ -18,6 +21,9 @@ CSRC = PKG / "csrc"
 LIB = PKG / "lib"
 INCLUDE = PKG.parent / "include"
 LIBNAME = "libnvllm.so"
+HOSTLIB = "libnvllm_host.so"
+HOST = PKG / "host"
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++20", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC",
@@ -78,7 +84,30 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return out
 
 
+def build_host(force: bool = False, verbose: bool = False) -> Path:
+    """Compiles host/*.cpp into lib/libnvllm_host.so (needs lib/libnvllm.so)."""
+    core = build(force=False, verbose=verbose)
+    out = LIB / HOSTLIB
+    srcs = sorted(HOST.glob("*.cpp"))
+    deps = srcs + sorted(HOST.glob("*.hpp")) + [INCLUDE / "nvllm.h", INCLUDE / "nvllm_host.h",
+                                                 core, Path(__file__)]
+    if not force and not _stale(out, deps):
+        return out
+    cxx = shutil.which("g++") or "g++"
+    tmp = out.with_suffix(".so.tmp")
+    cmd = [cxx, "-std=c++23", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-pthread",
+           f"-I{INCLUDE}", f"-I{CUDA_HOME / 'include'}", *map(str, srcs), "-o", str(tmp),
+           f"-L{LIB}", "-lnvllm", f"-L{CUDA_HOME / 'lib64'}", "-lcudart_static", "-ldl", "-lrt",
+           "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, out)
+    return out
+
+
 if __name__ == "__main__":
     import sys
     p = build(force="--force" in sys.argv, verbose=True)
     print(p)
+    print(build_host(force="--force" in sys.argv, verbose=True))
