@@ -122,6 +122,40 @@ int nvllm_paged_attention_static(float* out, const float* query, const float* k_
                                  int32_t layer, float scale, int32_t precision,
                                  const nvllm_kv_layout* layout, void* stream);
 
+/*
+ * Head split of one decode batch over `world` GPUs (one process each): rank r
+ * holds heads [r*Hl, (r+1)*Hl) of every sequence in its own arena (layout
+ * num_heads = Hl) and computes their attention; the merge epilogue stores each
+ * finished row straight into every rank's full-width output buffer
+ * outs[0..world) ([n_tokens, world*Hl*head_dim], head-major like the
+ * single-GPU output), peer memory reached over NVLink, so that on completion
+ * (in stream order) every rank's outs[rank] holds all heads. The writer of a
+ * rank's last row adds 1 to each rank's flags[r] (a uint32 in that rank's
+ * memory); the call returns its stream to the caller after
+ * flags[rank] >= epoch * world, waiting at most 2 s (then NVLLM_ERR_TIMEOUT in
+ * nvllm_get_last_error). epoch counts the calls on this group from 1; flags
+ * start at 0. Output buffers may be alternated by epoch parity: a rank cannot
+ * write epoch e + 2 before every rank finished epoch e + 1. Decode batches only
+ * (one query row per sequence). The reference has no multi-GPU code; this is
+ * the head-split scheme for one long-context sequence batch.
+ */
+#define NVLLM_MAX_RANKS 8
+typedef struct nvllm_head_split {
+    int32_t rank;
+    int32_t world;
+    uint32_t epoch;
+    float* outs[NVLLM_MAX_RANKS];      /* device pointers valid in this process */
+    uint32_t* flags[NVLLM_MAX_RANKS];  /* device pointers valid in this process */
+} nvllm_head_split;
+
+int nvllm_paged_attention_head_split(const nvllm_head_split* hs, const float* query,
+                                     const float* k_arena, const float* v_arena,
+                                     const int32_t* block_tables, int32_t max_blocks_per_seq,
+                                     const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                                     int32_t num_seqs, int32_t max_context_len, int32_t layer,
+                                     float scale, void* workspace, size_t workspace_bytes,
+                                     const nvllm_kv_layout* layout, void* stream);
+
 /* Synchronizes the stream, then returns (and clears) the device status word
  * of the current device that the kernels set on skipped out-of-range accesses,
  * inconsistent metadata or bounded waits that gave up. The reference has

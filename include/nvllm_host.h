@@ -89,6 +89,17 @@ int nvllm_engine_arenas(nvllm_engine* e, float** k_arena, float** v_arena);
 void* nvllm_engine_stream(nvllm_engine* e);
 int32_t nvllm_engine_step_tokens(const nvllm_engine* e);
 
+/* ---- cross-process device buffers (head split) ---------------------------
+ * nvllm_ipc_alloc: cudaMalloc of `bytes` on the current device, zero-filled,
+ * and its 64-byte CUDA IPC handle. nvllm_ipc_open maps a peer process's buffer
+ * into this process (peer access over NVLink enabled lazily); nvllm_ipc_close
+ * unmaps it; nvllm_ipc_free releases an nvllm_ipc_alloc buffer. */
+#define NVLLM_IPC_HANDLE_BYTES 64
+int nvllm_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+int nvllm_ipc_open(const void* handle, void** dev_ptr);
+int nvllm_ipc_close(void* dev_ptr);
+int nvllm_ipc_free(void* dev_ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,7 +23,12 @@ struct PlanCounters {
     int32_t decode_items;   // number of decode items
     int32_t prefill_next;   // dynamic fetch cursor (prefill)
     int32_t prefill_items;  // number of prefill items
+    int32_t decode_seqs;    // sequences with one query row
+    int32_t rows_done;      // head split: (sequence, head) rows stored so far
 };
+
+// Head split: ranks that share one batch, each owning a slice of the heads.
+constexpr int kMaxRanks = 8;
 
 struct AttnParams {
     float* out;
@@ -49,6 +54,16 @@ struct AttnParams {
     int32_t max_splits;
     int32_t split_tokens;     // P: positions per decode item
     int32_t prefill_tile;     // QT: query rows per prefill item
+    // Head split (num_outs > 0): every decode row leaves through the merge
+    // kernel, which stores it at column out_col of row token in each of the
+    // num_outs output buffers (this rank's and its peers', row stride
+    // out_stride floats), then signals each rank's arrival counter once all
+    // of this rank's rows are out.
+    int32_t num_outs;
+    float* outs[kMaxRanks];
+    uint32_t* flags[kMaxRanks];
+    int64_t out_stride;
+    int64_t out_col;
 };
 
 // Workspace carve-up shared by the size query and the launcher.
@@ -66,6 +81,10 @@ cudaError_t launch_reshape_and_cache(const float* key, const float* value, float
                                      bool vec4, cudaStream_t stream);
 
 cudaError_t launch_plan(const AttnParams& p, cudaStream_t stream);
+// Head split: increments every rank's arrival counter (one thread).
+cudaError_t launch_signal(uint32_t* const* flags, int n, cudaStream_t stream);
+// Waits (bounded) until *flag >= target; one thread.
+cudaError_t launch_flag_wait(const uint32_t* flag, uint32_t target, cudaStream_t stream);
 cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream);
 cudaError_t launch_prefill_fp32(const AttnParams& p, cudaStream_t stream);
 cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream);

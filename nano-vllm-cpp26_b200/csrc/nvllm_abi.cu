@@ -105,17 +105,18 @@ size_t nvllm_paged_attention_workspace_size(int32_t num_seqs, int32_t max_query_
         .total;
 }
 
-int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
-                          const float* v_arena, const int32_t* block_tables,
-                          int32_t max_blocks_per_seq, const int32_t* cu_seqlens_q,
-                          const int32_t* context_lens, int32_t num_seqs, int32_t max_query_len,
-                          int32_t max_context_len, int32_t layer, float scale, int32_t precision,
-                          void* workspace, size_t workspace_bytes, const nvllm_kv_layout* layout,
-                          void* stream) {
-    const int lv = validate_layout(layout);
-    if (lv != NVLLM_OK) return lv;
-    if (num_seqs < 0 || layer < 0 || layer >= layout->num_layers) return NVLLM_ERR_INVALID;
-    if (num_seqs == 0) return NVLLM_OK;
+}  // extern "C"
+
+namespace {
+
+// Validates the arguments shared by the attention entry points and fills p
+// (everything except the output routing).
+int prepare_attention(AttnParams& p, const float* query, const float* k_arena,
+                      const float* v_arena, const int32_t* block_tables,
+                      int32_t max_blocks_per_seq, const int32_t* cu_seqlens_q,
+                      const int32_t* context_lens, int32_t num_seqs, int32_t max_query_len,
+                      int32_t max_context_len, int32_t layer, float scale, int32_t precision,
+                      void* workspace, size_t workspace_bytes, const nvllm_kv_layout* layout) {
     if (precision != NVLLM_PRECISION_FP32 && precision != NVLLM_PRECISION_TF32) {
         return NVLLM_ERR_INVALID;
     }
@@ -124,12 +125,10 @@ int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
         int64_t(max_context_len) > int64_t(max_blocks_per_seq) * layout->block_size) {
         return NVLLM_ERR_INVALID;
     }
-    if (!out || !query || !k_arena || !v_arena || !block_tables || !cu_seqlens_q || !context_lens) {
+    if (!query || !k_arena || !v_arena || !block_tables || !cu_seqlens_q || !context_lens) {
         return NVLLM_ERR_INVALID;
     }
-    if (!aligned16(out) || !aligned16(query) || !aligned16(k_arena) || !aligned16(v_arena)) {
-        return NVLLM_ERR_INVALID;
-    }
+    if (!aligned16(query) || !aligned16(k_arena) || !aligned16(v_arena)) return NVLLM_ERR_INVALID;
     if (!(scale > 0.0f) || scale != scale) return NVLLM_ERR_INVALID;
 
     const WorkspaceLayout w = workspace_layout(num_seqs, max_query_len, max_context_len,
@@ -139,9 +138,7 @@ int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
         return NVLLM_ERR_WORKSPACE;
     }
     auto* ws = static_cast<unsigned char*>(workspace);
-
-    AttnParams p{};
-    p.out = out;
+    p = AttnParams{};
     p.q = query;
     p.k_arena = k_arena;
     p.v_arena = v_arena;
@@ -163,20 +160,99 @@ int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
     p.max_splits = w.max_splits;
     p.split_tokens = w.split_tokens;
     p.prefill_tile = w.prefill_tile;
+    return NVLLM_OK;
+}
 
+// plan -> prefill (if any multi-row sequence) -> decode + merge
+cudaError_t launch_attention(AttnParams& p, int32_t precision, cudaStream_t st) {
     // TF32 prefill runs on the tensor cores where the kernel's geometry allows
     // (hd 128, block size 16); elsewhere the fp32 FFMA kernel serves it, whose
     // error is far inside the TF32 tolerance.
     const bool tc_prefill =
-        precision == NVLLM_PRECISION_TF32 && max_query_len > 1 && prefill_tc_supported(p.g);
+        precision == NVLLM_PRECISION_TF32 && p.max_query_len > 1 && prefill_tc_supported(p.g);
     if (tc_prefill) p.prefill_tile = prefill_tc_tile_rows();
-
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = launch_plan(p, st);
-    if (e == cudaSuccess && max_query_len > 1) {
+    if (e == cudaSuccess && p.max_query_len > 1) {
         e = tc_prefill ? launch_prefill_tc(p, st) : launch_prefill_fp32(p, st);
     }
     if (e == cudaSuccess) e = launch_decode(p, st);
+    return e;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
+                          const float* v_arena, const int32_t* block_tables,
+                          int32_t max_blocks_per_seq, const int32_t* cu_seqlens_q,
+                          const int32_t* context_lens, int32_t num_seqs, int32_t max_query_len,
+                          int32_t max_context_len, int32_t layer, float scale, int32_t precision,
+                          void* workspace, size_t workspace_bytes, const nvllm_kv_layout* layout,
+                          void* stream) {
+    const int lv = validate_layout(layout);
+    if (lv != NVLLM_OK) return lv;
+    if (num_seqs < 0 || layer < 0 || layer >= layout->num_layers) return NVLLM_ERR_INVALID;
+    if (num_seqs == 0) return NVLLM_OK;
+    if (!out || !aligned16(out)) return NVLLM_ERR_INVALID;
+    AttnParams p;
+    const int rc = prepare_attention(p, query, k_arena, v_arena, block_tables, max_blocks_per_seq,
+                                     cu_seqlens_q, context_lens, num_seqs, max_query_len,
+                                     max_context_len, layer, scale, precision, workspace,
+                                     workspace_bytes, layout);
+    if (rc != NVLLM_OK) return rc;
+    p.out = out;
+    const cudaError_t e = launch_attention(p, precision, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? NVLLM_OK : NVLLM_ERR_CUDA;
+}
+
+int nvllm_paged_attention_head_split(const nvllm_head_split* hs, const float* query,
+                                     const float* k_arena, const float* v_arena,
+                                     const int32_t* block_tables, int32_t max_blocks_per_seq,
+                                     const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                                     int32_t num_seqs, int32_t max_context_len, int32_t layer,
+                                     float scale, void* workspace, size_t workspace_bytes,
+                                     const nvllm_kv_layout* layout, void* stream) {
+    const int lv = validate_layout(layout);
+    if (lv != NVLLM_OK) return lv;
+    if (hs == nullptr || hs->world < 1 || hs->world > NVLLM_MAX_RANKS || hs->rank < 0 ||
+        hs->rank >= hs->world || hs->epoch == 0) {
+        return NVLLM_ERR_INVALID;
+    }
+    for (int r = 0; r < hs->world; ++r) {
+        if (!hs->outs[r] || !aligned16(hs->outs[r]) || !hs->flags[r] ||
+            (reinterpret_cast<uintptr_t>(hs->flags[r]) & 3u) != 0) {
+            return NVLLM_ERR_INVALID;
+        }
+    }
+    if (num_seqs < 0 || layer < 0 || layer >= layout->num_layers) return NVLLM_ERR_INVALID;
+    AttnParams p;
+    if (num_seqs > 0) {
+        const int rc = prepare_attention(p, query, k_arena, v_arena, block_tables,
+                                         max_blocks_per_seq, cu_seqlens_q, context_lens, num_seqs,
+                                         1, max_context_len, layer, scale, NVLLM_PRECISION_FP32,
+                                         workspace, workspace_bytes, layout);
+        if (rc != NVLLM_OK) return rc;
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t local_cols = int64_t(layout->num_heads) * layout->head_dim;
+    p.num_outs = hs->world;
+    for (int r = 0; r < hs->world; ++r) {
+        p.outs[r] = hs->outs[r];
+        p.flags[r] = hs->flags[r];
+    }
+    p.out_stride = local_cols * hs->world;
+    p.out_col = local_cols * hs->rank;
+    cudaError_t e = cudaSuccess;
+    if (num_seqs > 0) {
+        e = launch_attention(p, NVLLM_PRECISION_FP32, st);
+    } else {
+        // nothing to store, but the peers still count on this rank's signal
+        e = launch_signal(p.flags, hs->world, st);
+    }
+    if (e == cudaSuccess) {
+        e = launch_flag_wait(hs->flags[hs->rank], hs->epoch * uint32_t(hs->world), st);
+    }
     return e == cudaSuccess ? NVLLM_OK : NVLLM_ERR_CUDA;
 }
 

@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const AttnParams p) 
             }
         }
         if (rg == 0) {
-            if (C.whole) {
+            if (C.whole && p.num_outs == 0) {
                 const float inv = 1.0f / fmaxf(l_tot, 1e-12f);
                 float* op = p.out + int64_t(C.tok) * g.row + int64_t(C.h) * HD;
 #pragma unroll
@@ -424,11 +424,15 @@ __global__ void __launch_bounds__(256) merge_kernel(const AttnParams p) {
     const int s = gw / H;
     const int h = gw % H;
     const int q0 = p.cu_seqlens_q[s];
-    if (p.cu_seqlens_q[s + 1] - q0 != 1) return;
+    if (q0 < 0 || p.cu_seqlens_q[s + 1] - q0 != 1) return;
     const int ctx = p.context_lens[s];
-    if (ctx < 1 || ctx > p.max_context_len) return;
+    if (ctx < 1 || ctx > p.max_context_len ||
+        int64_t(ctx) > int64_t(p.max_blocks) * p.g.block_size) {
+        return;
+    }
     const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
-    if (nsplit <= 1) return;
+    // one split: the decode kernel wrote the row itself, unless it must go to peers
+    if (nsplit <= 1 && p.num_outs == 0) return;
     const int64_t pbase = (int64_t(s) * H + h) * p.max_splits;
     float M = -INFINITY;
     for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, p.part_ml[pbase + j].x);
@@ -450,9 +454,51 @@ __global__ void __launch_bounds__(256) merge_kernel(const AttnParams p) {
 #pragma unroll
         for (int k = 0; k < PER_LANE; ++k) o[k] = fmaf(w, ap[lane + 32 * k], o[k]);
     }
-    float* op = p.out + int64_t(q0) * p.g.row + int64_t(h) * HD;
+    if (p.num_outs == 0) {
+        float* op = p.out + int64_t(q0) * p.g.row + int64_t(h) * HD;
 #pragma unroll
-    for (int k = 0; k < PER_LANE; ++k) op[lane + 32 * k] = o[k] * inv;
+        for (int k = 0; k < PER_LANE; ++k) op[lane + 32 * k] = o[k] * inv;
+        return;
+    }
+    // head split: store the row into every rank's output buffer (peer memory
+    // over NVLink), then the writer of this rank's last row signals all ranks
+    for (int r = 0; r < p.num_outs; ++r) {
+        float* op = p.outs[r] + int64_t(q0) * p.out_stride + p.out_col + int64_t(h) * HD;
+#pragma unroll
+        for (int k = 0; k < PER_LANE; ++k) op[lane + 32 * k] = o[k] * inv;
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) {
+        const int prev = atomicAdd(&p.counters->rows_done, 1);
+        if (prev + 1 == p.counters->decode_seqs * H) {
+            __threadfence_system();
+            for (int r = 0; r < p.num_outs; ++r) atomicAdd_system(p.flags[r], 1u);
+        }
+    }
+}
+
+// Head split with nothing to store: signal every rank directly.
+__global__ void signal_kernel(AttnParams p) {
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    for (int r = 0; r < p.num_outs; ++r) atomicAdd_system(p.flags[r], 1u);
+}
+
+// Head split: the call completes once every rank has signalled this rank.
+__global__ void flag_wait_kernel(const uint32_t* flag, uint32_t target) {
+    if (threadIdx.x != 0) return;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (int32_t(v - target) >= 0) return;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            raise_status(kStatusTimeout);
+            return;
+        }
+        __nanosleep(200);
+    }
 }
 
 // Builds the decode and prefill work lists from the batch metadata (one CTA).
@@ -487,7 +533,7 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int& t
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const AttnParams p) {
     __shared__ int warp_tot[32];
-    int run_d = 0, run_p = 0;
+    int run_d = 0, run_p = 0, run_s = 0;
     const int B = p.g.block_size;
     for (int base = 0; base < p.num_seqs; base += kPlanThreads) {
         const int s = base + threadIdx.x;
@@ -507,6 +553,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const AttnParams p) 
                 np = (qlen + p.prefill_tile - 1) / p.prefill_tile;
             }
         }
+        run_s += __syncthreads_count(nd > 0);
         int tot_d = 0, tot_p = 0;
         const int off_d = block_exclusive_scan(nd, warp_tot, tot_d);
         const int off_p = block_exclusive_scan(np, warp_tot, tot_p);
@@ -521,6 +568,13 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const AttnParams p) 
         p.counters->decode_items = run_d;
         p.counters->prefill_next = 0;
         p.counters->prefill_items = run_p;
+        p.counters->decode_seqs = run_s;
+        p.counters->rows_done = 0;
+        if (p.num_outs > 0 && run_s == 0) {
+            // no row will reach the merge kernel: signal the ranks from here
+            __threadfence_system();
+            for (int r = 0; r < p.num_outs; ++r) atomicAdd_system(p.flags[r], 1u);
+        }
     }
 }
 
@@ -557,6 +611,19 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream) {
 int32_t decode_split_tokens(int32_t head_dim) {
     // 16 chunks of 2048/hd positions: 256 KiB of K+V per item at any head_dim.
     return 16 * (2048 / head_dim);
+}
+
+cudaError_t launch_signal(uint32_t* const* flags, int n, cudaStream_t stream) {
+    AttnParams p{};
+    p.num_outs = n;
+    for (int r = 0; r < n && r < kMaxRanks; ++r) p.flags[r] = flags[r];
+    signal_kernel<<<1, 32, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_flag_wait(const uint32_t* flag, uint32_t target, cudaStream_t stream) {
+    flag_wait_kernel<<<1, 32, 0, stream>>>(flag, target);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_plan(const AttnParams& p, cudaStream_t stream) {

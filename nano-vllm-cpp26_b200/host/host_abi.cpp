@@ -1,4 +1,5 @@
 // extern "C" wrappers of the host library (declared in include/nvllm_host.h).
+#include <cstring>
 #include <memory>
 #include <new>
 #include <vector>
@@ -221,6 +222,37 @@ void* nvllm_engine_stream(nvllm_engine* e) { return e ? e->impl->stream() : null
 
 int32_t nvllm_engine_step_tokens(const nvllm_engine* e) {
     return e ? e->impl->step().num_tokens : -1;
+}
+
+int nvllm_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
+    if (dev_ptr == nullptr || handle == nullptr || bytes == 0) return NVLLM_ERR_INVALID;
+    static_assert(sizeof(cudaIpcMemHandle_t) == NVLLM_IPC_HANDLE_BYTES, "IPC handle size");
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return NVLLM_ERR_CUDA;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess ||
+        cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p) != cudaSuccess) {
+        cudaFree(p);
+        return NVLLM_ERR_CUDA;
+    }
+    *dev_ptr = p;
+    return NVLLM_OK;
+}
+
+int nvllm_ipc_open(const void* handle, void** dev_ptr) {
+    if (dev_ptr == nullptr || handle == nullptr) return NVLLM_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    return cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess
+               ? NVLLM_OK
+               : NVLLM_ERR_CUDA;
+}
+
+int nvllm_ipc_close(void* dev_ptr) {
+    return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? NVLLM_OK : NVLLM_ERR_CUDA;
+}
+
+int nvllm_ipc_free(void* dev_ptr) {
+    return cudaFree(dev_ptr) == cudaSuccess ? NVLLM_OK : NVLLM_ERR_CUDA;
 }
 
 }  // extern "C"

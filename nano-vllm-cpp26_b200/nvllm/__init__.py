@@ -62,6 +62,17 @@ class KVLayout(ctypes.Structure):
                 f"head_dim={self.head_dim})")
 
 
+MAX_RANKS = 8
+
+
+class HeadSplit(ctypes.Structure):
+    """nvllm_head_split: this rank, the group size, the call's epoch, and every
+    rank's output buffer and arrival counter (device pointers valid here)."""
+
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("epoch", ctypes.c_uint32),
+                ("outs", ctypes.c_void_p * MAX_RANKS), ("flags", ctypes.c_void_p * MAX_RANKS)]
+
+
 _LIB: ctypes.CDLL | None = None
 
 
@@ -84,6 +95,9 @@ def lib() -> ctypes.CDLL:
     L.nvllm_paged_attention.restype = ctypes.c_int
     L.nvllm_paged_attention.argtypes = [vp, vp, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32,
                                         i32, vp, sz, lp, vp]
+    L.nvllm_paged_attention_head_split.restype = ctypes.c_int
+    L.nvllm_paged_attention_head_split.argtypes = [ctypes.POINTER(HeadSplit), vp, vp, vp, vp, i32,
+                                                   vp, vp, i32, i32, i32, f32, vp, sz, lp, vp]
     L.nvllm_get_last_error.restype = ctypes.c_int
     L.nvllm_get_last_error.argtypes = [vp]
     L.nvllm_status_string.restype = ctypes.c_char_p
@@ -183,3 +197,29 @@ def paged_attention(out, query, k_arena, v_arena, block_tables, cu_seqlens_q, co
 def get_last_error(stream=None) -> int:
     """Synchronizes and returns/clears the device status word."""
     return lib().nvllm_get_last_error(_stream_ptr(stream))
+
+
+def paged_attention_head_split(hs: HeadSplit, query, k_arena, v_arena, block_tables,
+                               cu_seqlens_q, context_lens, max_context_len: int, layer: int,
+                               layout: KVLayout, scale: float | None = None, workspace=None,
+                               stream=None, check: bool = True) -> int:
+    """Decode attention of this rank's heads; rows land in every rank's output
+    buffer (nvllm_paged_attention_head_split)."""
+    for t, n, d in ((query, "query", "float32"), (k_arena, "k_arena", "float32"),
+                    (v_arena, "v_arena", "float32"), (block_tables, "block_tables", "int32"),
+                    (cu_seqlens_q, "cu_seqlens_q", "int32"),
+                    (context_lens, "context_lens", "int32")):
+        _require(t, d, n)
+    num_seqs = context_lens.numel()
+    if scale is None:
+        scale = 1.0 / math.sqrt(layout.head_dim)
+    if workspace is None:
+        workspace = alloc_workspace(num_seqs, 1, max_context_len, layout, device=query.device)
+    st = lib().nvllm_paged_attention_head_split(
+        ctypes.byref(hs), _dptr(query), _dptr(k_arena), _dptr(v_arena), _dptr(block_tables),
+        block_tables.shape[1], _dptr(cu_seqlens_q), _dptr(context_lens), num_seqs,
+        max_context_len, layer, ctypes.c_float(scale), _dptr(workspace), workspace.numel(),
+        ctypes.byref(layout), _stream_ptr(stream))
+    if check:
+        _check(st, "nvllm_paged_attention_head_split")
+    return st

@@ -1,0 +1,34 @@
+"""Multi-GPU parity: the head-split attention (rows stored into peer GPUs'
+buffers by the merge epilogue) against the single-GPU full-head result, run
+as a 2-rank torchrun job (tests/mp_head_split.py). Needs two GPUs of one box.
+NVLS is disabled in NCCL for the job (no multicast objects are involved in
+the kernels themselves)."""
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_head_split_two_gpus():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           str(ROOT / "tests" / "mp_head_split.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("head split over 2 ranks ok") == 2
