@@ -453,6 +453,116 @@ def nvllm_main(args, spec):
     return 0
 
 
+def headsplit_main(args, spec):
+    """One decode batch split by heads over the ranks (strong scaling): each
+    step writes the new tokens' K/V of this rank's heads and runs
+    nvllm_paged_attention_head_split, whose merge epilogue stores every row into
+    all ranks' output buffers over NVLink. The NCCL variant (local attention +
+    all_gather_into_tensor) is timed beside it as the baseline."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import nvllm
+    from nvllm.headsplit import HeadSplitGroup
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl" if world > 1 else "gloo",
+                            timeout=datetime.timedelta(seconds=120),
+                            **({"device_id": dev} if world > 1 else
+                               {"init_method": "tcp://127.0.0.1:29555", "rank": 0,
+                                "world_size": 1}))
+    nvllm.lib()
+    H, hd = spec.num_heads, spec.head_dim
+    assert H % world == 0, "heads must divide over the ranks"
+    Hl = H // world
+    lay = nvllm.KVLayout(spec.num_blocks, 1, spec.block_size, Hl, hd)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2000 + rank)
+    ka = torch.empty(lay.arena_shape(), device=dev).normal_(generator=gen)
+    va = torch.empty_like(ka).normal_(generator=gen)
+    n = spec.n_tokens
+    q = torch.randn((n, Hl * hd), generator=gen, device=dev)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    bt = torch.from_numpy(spec.block_tables).to(dev)
+    cu = torch.from_numpy(spec.cu_seqlens_q).to(dev)
+    ctx = torch.from_numpy(spec.ctx_lens).to(dev)
+    slots = torch.from_numpy(spec.slot_mapping()).to(dev)
+    max_ctx = int(spec.ctx_lens.max())
+    ws = nvllm.alloc_workspace(spec.num_seqs, 1, max_ctx, lay, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    grp = HeadSplitGroup(dist, n_rows=n, local_cols=Hl * hd, device=dev)
+    local_out = torch.empty_like(q)
+    gathered = torch.empty((world, n, Hl * hd), device=dev)
+
+    def fused_step():
+        nvllm.reshape_and_cache(k, v, ka, va, slots, 0, lay, stream=stream)
+        grp.attention(q, ka, va, bt, cu, ctx, max_ctx, 0, lay, workspace=ws, stream=stream)
+
+    def nccl_step():
+        nvllm.reshape_and_cache(k, v, ka, va, slots, 0, lay, stream=stream)
+        nvllm.paged_attention(local_out, q, ka, va, bt, cu, ctx, 1, max_ctx, 0, lay,
+                              workspace=ws, stream=stream)
+        dist.all_gather_into_tensor(gathered, local_out)
+
+    def timed(fn) -> float:
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        t = torch.tensor([a.elapsed_time(b) / 1e3], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(local).start()
+    t_fused = timed(fused_step)
+    st = nvllm.get_last_error(stream)
+    t_nccl = timed(nccl_step) if world > 1 else None
+    clocks = sampler.stop()
+    if st != nvllm.OK:
+        raise RuntimeError(f"device status {nvllm.status_string(st)}")
+    tokens = n * args.steps
+    value = tokens / t_fused
+    per_rank_bytes = spec.kv_bytes() / world
+    achieved = per_rank_bytes / (t_fused / args.steps) / 1e9
+    peak = measured_peaks().get("hbm_gbs") or FALLBACK_HBM_GBS
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_fused / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic",
+        "config": {**workload_config(spec), "parallelism": f"head-split x{world}",
+                   "heads_per_rank": Hl},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "per": "GPU (KV bytes of its heads / step time)"},
+        "nccl_allgather_baseline_ms_per_step": (t_nccl / args.steps * 1e3) if t_nccl else None,
+        "gpu_launches": 5 * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    grp.close(dist)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -465,6 +575,8 @@ def main() -> int:
     ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32",
                     help="prefill tile arithmetic (decode is always fp32)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--head-split", action="store_true",
+                    help="split the batch's heads over the ranks (long-context decode)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warm-up raised to 3 steps")
@@ -473,6 +585,8 @@ def main() -> int:
     spec = make_batch(args.workload, seed=args.seed)
     if args.impl == "reference":
         return reference_main(args, spec)
+    if args.head_split:
+        return headsplit_main(args, spec)
     return nvllm_main(args, spec)
 
 
