@@ -241,7 +241,9 @@ def workload_config(spec) -> dict:
                                   "+ 120 decodes ctx U[256,8192])",
                          "longctx": "long-context decode (4 seqs x 32768 ctx)",
                          "decode_small": "decode paged attention, profiling size (16 seqs, "
-                                         "ctx U[512,4096], 4096-block arena)"}[spec.name],
+                                         "ctx U[512,4096], 4096-block arena)",
+                         "mixed_small": "mixed prefill+decode, profiling size (2 prefills "
+                                        "U[512,2048] + 8 decodes, 4096-block arena)"}[spec.name],
             "num_seqs": spec.num_seqs, "num_heads": spec.num_heads, "head_dim": spec.head_dim,
             "block_size": spec.block_size, "arena_blocks": spec.num_blocks,
             "new_tokens_per_step": spec.n_tokens,
@@ -569,7 +571,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["nvllm", "reference"], default="nvllm")
-    ap.add_argument("--workload", choices=["decode", "mixed", "longctx", "decode_small"],
+    ap.add_argument("--workload", choices=["decode", "mixed", "longctx", "decode_small",
+                                           "mixed_small"],
                     default="decode")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32",

@@ -9,7 +9,9 @@
 * longctx: 4 sequences with 32768-position contexts, same geometry;
 * decode_small: the decode distribution with 16 sequences on a 4096-block
   arena (2 GiB K+V, ~1.2 GB read per call: still far beyond L2), the case for
-  multi-pass profiler captures.
+  multi-pass profiler captures;
+* mixed_small: the mixed distribution with 2 prefills and 8 decodes on a
+  4096-block arena, the profiler case of the prefill kernels.
 
 Context lengths and block tables come from numpy's PCG64 with the given seed;
 tensor values from torch's CUDA generator. No public dataset is involved.
@@ -25,6 +27,7 @@ WORKLOADS = {
     "mixed": dict(num_heads=32, head_dim=128, block_size=16, num_blocks=65536),
     "longctx": dict(num_heads=32, head_dim=128, block_size=16, num_blocks=8192 + 64),
     "decode_small": dict(num_heads=32, head_dim=128, block_size=16, num_blocks=4096),
+    "mixed_small": dict(num_heads=32, head_dim=128, block_size=16, num_blocks=4096),
 }
 
 
@@ -113,6 +116,11 @@ def make_batch(name: str = "decode", seed: int = 0) -> BatchSpec:
         dec = rng.integers(256, 8192, size=120, endpoint=True).astype(np.int32)
         ctx = np.concatenate([pre, dec]).astype(np.int32)
         ql = np.concatenate([pre, np.ones(120, np.int32)]).astype(np.int32)
+    elif name == "mixed_small":
+        pre = rng.integers(512, 2048, size=2, endpoint=True).astype(np.int32)
+        dec = rng.integers(256, 8192, size=8, endpoint=True).astype(np.int32)
+        ctx = np.concatenate([pre, dec]).astype(np.int32)
+        ql = np.concatenate([pre, np.ones(8, np.int32)]).astype(np.int32)
     elif name == "decode_small":
         ctx = rng.integers(512, 4096, size=16, endpoint=True).astype(np.int32)
         ql = np.ones(16, np.int32)
