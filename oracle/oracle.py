@@ -166,6 +166,9 @@ class RefPath:
                                                 _f32p, _f32p]
         lib.ref_engine_create.restype = vp
         lib.ref_engine_create.argtypes = [ctypes.c_int32] * 4
+        lib.ref_generate.restype = ctypes.c_int64
+        lib.ref_generate.argtypes = [ctypes.c_int64] * 12 + [_i64p, _i64p, _i64p, ctypes.c_int32,
+                                                             ctypes.c_int64, ctypes.c_char_p]
         lib.ref_forward_attention.restype = ctypes.c_int64
         lib.ref_forward_attention.argtypes = [vp, vp, ctypes.c_int32, _i32p, _i32p, _i64p,
                                               ctypes.c_int32, _f32p, _f32p, _f32p, _f32p]
@@ -236,3 +239,64 @@ class RefPath:
         if n < 0:
             raise ValueError("reference harness rejected the batch")
         return n
+
+    # --- continuous batching end to end (src/benchmark.cpp:163-229) -----------
+    def generate(self, model: dict, num_blocks: int, block_size: int, max_batch: int,
+                 max_tokens_per_step: int, watermark: int, prompts, max_new_tokens,
+                 path: str, num_threads: int = 0, max_steps: int = 0) -> list[dict]:
+        """Runs the reference scheduler + forward_batch and returns its trace
+        (see read_trace)."""
+        lens = np.array([len(p) for p in prompts], np.int64)
+        toks = np.concatenate([np.asarray(p, np.int64) for p in prompts]) if len(prompts) else \
+            np.zeros(1, np.int64)
+        mnt = np.asarray(max_new_tokens, np.int64)
+        n = self.lib.ref_generate(model["vocab"], model["hidden"], model["layers"], model["heads"],
+                                  model["head_dim"], model["ffn"], num_blocks, block_size,
+                                  max_batch, max_tokens_per_step, watermark, len(prompts),
+                                  _ptr(lens, _i64p), _ptr(np.ascontiguousarray(toks), _i64p),
+                                  _ptr(mnt, _i64p), num_threads, max_steps, path.encode())
+        if n < 0:
+            raise RuntimeError("ref_generate failed")
+        return read_trace(path)
+
+
+def read_trace(path_or_array) -> list[dict]:
+    """Parses a ref_generate trace (file path or its integer array): one dict
+    per step with the running sequences (seq_id, num_computed, total_len,
+    prev_token, table, uncomputed) and the sampled tokens."""
+    if isinstance(path_or_array, np.ndarray):
+        a = path_or_array.astype(np.int64)
+    else:
+        a = np.fromfile(path_or_array, dtype="<i8")
+    i = 0
+    steps = []
+    while i < len(a):
+        assert a[i] == -1
+        n = int(a[i + 2])
+        i += 3
+        seqs = []
+        for _ in range(n):
+            sid, nc, tl, prev, tlen = (int(x) for x in a[i:i + 5])
+            i += 5
+            table = a[i:i + tlen].copy()
+            i += tlen
+            nu = int(a[i])
+            unc = a[i + 1:i + 1 + nu].copy()
+            i += 1 + nu
+            seqs.append(dict(seq_id=sid, num_computed=nc, total_len=tl, prev_token=prev,
+                             table=table, uncomputed=unc))
+        assert a[i] == -2
+        sampled = a[i + 1:i + 1 + n].copy()
+        i += 1 + n
+        margins = np.zeros(n, np.float32)
+        top_idx = np.zeros((n, 8), np.int64)
+        top_val = np.zeros((n, 8), np.float32)
+        for j in range(n):
+            margins[j] = np.array([a[i]], np.int64).astype(np.uint32).view(np.float32)[0]
+            pairs = a[i + 1:i + 17].reshape(8, 2)
+            top_idx[j] = pairs[:, 0]
+            top_val[j] = pairs[:, 1].astype(np.uint32).view(np.float32)
+            i += 17
+        steps.append(dict(seqs=seqs, sampled=sampled, margin=margins, top_idx=top_idx,
+                          top_val=top_val))
+    return steps

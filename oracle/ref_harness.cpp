@@ -19,15 +19,21 @@
 // harness answers the Q/K/V calls with caller-supplied projections, records the
 // attention output that arrives as the A operand of the W_o call, and returns
 // zeros for the rest. The attention outputs are therefore exactly what the
-// reference's own loop computes for the given Q/K/V and KV history.
+// reference's own loop computes for the given Q/K/V and KV history. With no
+// capture active the definition forwards to the reference's own matmul_batched,
+// so ref_generate runs the unmodified model end to end.
 
 #include "nano_vllm/kv_cache.hpp"
 #include "nano_vllm/model.hpp"
 #include "nano_vllm/scheduler.hpp"
 #include "nano_vllm/thread_pool.hpp"
 
+#include <dlfcn.h>
+
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <vector>
@@ -48,6 +54,23 @@ struct MatmulPlan {
 
 MatmulPlan g_plan;
 
+// LM-head capture for ref_generate: the (6 * layers)-th matmul_batched call of a
+// forward_batch is the LM head (src/model.cpp:291); its output is kept.
+struct LogitsCapture {
+    bool active = false;
+    std::size_t call = 0;
+    std::size_t target = 0;
+    std::vector<float> logits;
+};
+LogitsCapture g_lm;
+
+using MatmulFn = void (*)(std::span<const float>, std::span<const float>, std::span<float>,
+                          std::size_t, std::size_t, std::size_t, nano_vllm::ThreadPool&);
+
+// The reference's own matmul_batched (src/model.cpp:42-62), found behind the
+// harness's interposing definition; used whenever no attention capture is active.
+MatmulFn reference_matmul();
+
 struct RefEngine {
     std::unique_ptr<nano_vllm::TransformerModel> model;
     std::unique_ptr<nano_vllm::ThreadPool> pool;
@@ -61,15 +84,20 @@ namespace nano_vllm {
 
 void matmul_batched(
     std::span<const float> a,
-    std::span<const float> /*w*/,
+    std::span<const float> w,
     std::span<float> c,
     std::size_t batch_size,
-    std::size_t /*k_dim*/,
+    std::size_t k_dim,
     std::size_t n_dim,
-    ThreadPool& /*pool*/) {
+    ThreadPool& pool) {
     const std::size_t count = batch_size * n_dim;
     if (!g_plan.active) {
-        std::fill_n(c.data(), count, 0.0f);
+        if (MatmulFn f = reference_matmul()) {
+            f(a, w, c, batch_size, k_dim, n_dim, pool);
+        } else {
+            std::fill_n(c.data(), count, 0.0f);
+        }
+        if (g_lm.active && g_lm.call++ == g_lm.target) g_lm.logits.assign(c.begin(), c.begin() + count);
         return;
     }
     const std::size_t call = g_plan.call++;
@@ -88,6 +116,20 @@ void matmul_batched(
 }
 
 }  // namespace nano_vllm
+
+namespace {
+MatmulFn reference_matmul() {
+    static MatmulFn fn = [] {
+        Dl_info info{};
+        if (dladdr(reinterpret_cast<void*>(&nano_vllm::matmul_batched), &info) == 0 ||
+            info.dli_sname == nullptr) {
+            return MatmulFn{nullptr};
+        }
+        return reinterpret_cast<MatmulFn>(dlsym(RTLD_NEXT, info.dli_sname));
+    }();
+    return fn;
+}
+}  // namespace
 
 using nano_vllm::BlockId;
 using nano_vllm::PagedKVCache;
@@ -240,6 +282,102 @@ int64_t ref_forward_attention(void* engine, void* cache, int32_t num_seqs,
     g_plan.active = false;
     (void)sampled;
     return static_cast<int64_t>(n_tok);
+}
+
+// Runs the reference's continuous-batching loop (src/benchmark.cpp:163-229:
+// schedule_step -> forward_batch over running() -> process_step_outputs) with
+// the reference TransformerModel (real matmuls, LCG weights of
+// src/model.cpp:64-122) on `num_requests` requests, and writes a trace of every
+// step to `path` as little-endian int64 records:
+//   step header:  -1, step index, n_running
+//   per running sequence, in running() order:
+//     seq_id, num_computed, total_len, prev_token (tokens.back()),
+//     table_len, table[table_len], n_uncomputed, uncomputed tokens[n_uncomputed]
+//   step footer:  -2, then n_running sampled token ids, then per sequence the
+//     top-2 margin of the penalised logits (src/model.cpp:294-309) and the 8
+//     largest raw logits as (index, value) pairs; float values are stored as
+//     their 32-bit patterns
+// Returns the number of steps, or -1 (cannot open path / bad arguments).
+int64_t ref_generate(int64_t vocab, int64_t hidden, int64_t layers, int64_t heads, int64_t head_dim,
+                     int64_t ffn, int64_t num_blocks, int64_t block_size, int64_t max_batch,
+                     int64_t max_tokens_per_step, int64_t watermark, int64_t num_requests,
+                     const int64_t* prompt_lens, const int64_t* prompt_tokens,
+                     const int64_t* max_new_tokens, int32_t num_threads, int64_t max_steps,
+                     const char* path) {
+    if (num_requests < 0 || hidden != heads * head_dim) return -1;
+    std::FILE* f = std::fopen(path, "wb");
+    if (f == nullptr) return -1;
+    auto put = [f](int64_t v) { std::fwrite(&v, sizeof(v), 1, f); };
+    nano_vllm::ModelConfig mc{.vocab_size = std::size_t(vocab), .hidden_dim = std::size_t(hidden),
+                              .num_layers = std::size_t(layers), .num_heads = std::size_t(heads),
+                              .head_dim = std::size_t(head_dim), .ffn_dim = std::size_t(ffn)};
+    nano_vllm::TransformerModel model(mc);
+    nano_vllm::ThreadPool pool(num_threads > 0 ? std::size_t(num_threads)
+                                               : std::thread::hardware_concurrency());
+    nano_vllm::PagedKVCache cache(nano_vllm::KVCacheConfig{
+        .num_blocks = std::size_t(num_blocks), .block_size = std::size_t(block_size),
+        .num_layers = std::size_t(layers), .num_heads = std::size_t(heads),
+        .head_dim = std::size_t(head_dim)});
+    nano_vllm::ContinuousScheduler sched(nano_vllm::SchedulerConfig{
+        .max_batch_size = std::size_t(max_batch),
+        .max_tokens_per_step = std::size_t(max_tokens_per_step),
+        .watermark_blocks = std::size_t(watermark), .eos_token_id = std::nullopt});
+    int64_t off = 0;
+    for (int64_t i = 0; i < num_requests; ++i) {
+        std::vector<std::size_t> prompt;
+        for (int64_t j = 0; j < prompt_lens[i]; ++j) prompt.push_back(std::size_t(prompt_tokens[off + j]));
+        off += prompt_lens[i];
+        sched.add_request(nano_vllm::SequenceState(nano_vllm::SeqId(i + 1), std::move(prompt),
+                                                   std::size_t(max_new_tokens[i]), nullptr));
+    }
+    int64_t step = 0;
+    g_plan.active = false;
+    while (sched.has_pending_work() && (max_steps <= 0 || step < max_steps)) {
+        (void)sched.schedule_step(cache);
+        const auto running = sched.running();
+        put(-1);
+        put(step);
+        put(int64_t(running.size()));
+        for (const auto& seq : running) {
+            put(int64_t(seq.seq_id));
+            put(int64_t(seq.num_computed_tokens));
+            put(int64_t(seq.tokens.size()));
+            put(seq.tokens.empty() ? 0 : int64_t(seq.tokens.back()));
+            put(int64_t(seq.block_table.size()));
+            for (const BlockId b : seq.block_table) put(int64_t(b));
+            const auto unc = seq.uncomputed_tokens();
+            put(int64_t(unc.size()));
+            for (const std::size_t t : unc) put(int64_t(t));
+        }
+        g_lm = LogitsCapture{.active = true, .call = 0, .target = std::size_t(6 * layers), .logits = {}};
+        const auto sampled = model.forward_batch(running, cache, pool);
+        g_lm.active = false;
+        put(-2);
+        for (const std::size_t t : sampled) put(int64_t(t));
+        auto bits = [](float x) { uint32_t u; std::memcpy(&u, &x, 4); return int64_t(u); };
+        for (std::size_t i = 0; i < running.size(); ++i) {
+            const float* row = g_lm.logits.data() + i * std::size_t(vocab);
+            const std::size_t prev = running[i].tokens.empty() ? 0 : running[i].tokens.back();
+            float b1 = -INFINITY, b2 = -INFINITY;
+            for (int64_t t = 0; t < vocab; ++t) {
+                const float adj = std::size_t(t) == prev ? row[t] - 1.5f : row[t];
+                if (adj > b1) { b2 = b1; b1 = adj; } else if (adj > b2) { b2 = adj; }
+            }
+            put(bits(b1 - b2));
+            std::vector<int64_t> idx(static_cast<std::size_t>(vocab));
+            for (int64_t t = 0; t < vocab; ++t) idx[std::size_t(t)] = t;
+            std::partial_sort(idx.begin(), idx.begin() + 8, idx.end(),
+                              [row](int64_t x, int64_t y) { return row[x] > row[y] || (row[x] == row[y] && x < y); });
+            for (int j = 0; j < 8; ++j) {
+                put(idx[std::size_t(j)]);
+                put(bits(row[idx[std::size_t(j)]]));
+            }
+        }
+        (void)sched.process_step_outputs(sampled, cache, model.vocab());
+        ++step;
+    }
+    std::fclose(f);
+    return step;
 }
 
 }  // extern "C"

@@ -165,3 +165,20 @@ def golden_cases() -> list[Case]:
     cases.append(make_case("mixed_h2_hd256_b16", 108, num_heads=2, head_dim=256, block_size=16,
                            num_layers=1, num_computed=[0, 70], total_len=[19, 71]))
     return cases
+
+
+def bimodal_workload(num_requests: int, vocab: int):
+    """The reference benchmark's request set (src/benchmark.cpp:46-67):
+    request i has a prompt of 8 + i % 12 tokens ((i*31 + j*17) % (vocab-1)) + 1
+    and asks for 128 new tokens when i % 5 == 0, else 16."""
+    prompts, max_new = [], []
+    for i in range(num_requests):
+        plen = 8 + i % 12
+        prompts.append([((i * 31 + j * 17) % (vocab - 1)) + 1 for j in range(plen)])
+        max_new.append(128 if i % 5 == 0 else 16)
+    return prompts, max_new
+
+
+# Model configurations of the token-stream fixtures.
+TOY_MODEL = dict(vocab=512, hidden=128, layers=2, heads=4, head_dim=32, ffn=256)
+WIDE_MODEL = dict(vocab=32000, hidden=4096, layers=4, heads=32, head_dim=128, ffn=11008)

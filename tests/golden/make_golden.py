@@ -15,6 +15,13 @@ K and V rows of each new token are read back through read_head_kv at
 ``allocator_trace.npz`` records a seeded sequence of allocate_block /
 allocate_blocks / free_blocks calls on the reference PagedKVCache with the
 block ids and free counts it returned.
+
+``tokens_*.npz`` are traces of the reference's continuous-batching loop
+(ContinuousScheduler + TransformerModel::forward_batch with its real matmuls and
+LCG weights; see ref_generate in oracle/ref_harness.cpp): every step's running
+sequences (computed / total lengths, block tables, uncomputed token ids, the
+previous token), the tokens the reference sampled for them, the top-2 margin
+of the penalised logits and the 8 largest logits of each sampled row.
 """
 from __future__ import annotations
 
@@ -122,9 +129,66 @@ def allocator_trace(ref: RefPath, seed: int = 7, num_blocks: int = 40, n_ops: in
                 free_after=np.array(free_after, np.int64))
 
 
+TOKEN_TRACES = {
+    # the reference benchmark's own workload and configuration
+    # (src/benchmark.cpp:46-67, :238-261): toy model, 96 requests, batch 16
+    "tokens_toy_bench": dict(model="toy", num_blocks=1024, block_size=16, max_batch=16,
+                             max_tokens_per_step=512, watermark=2, requests="bench"),
+    # seeded prompts of 8-32 tokens, block size 8, a tight arena that forces
+    # preemption by recompute (src/scheduler.cpp:44-76)
+    "tokens_toy_seeded": dict(model="toy", num_blocks=48, block_size=8, max_batch=12,
+                              max_tokens_per_step=256, watermark=1, requests="seeded"),
+    # the 4096-hidden, 32-head, 4-layer, vocab-32000 model of the serving workload
+    "tokens_wide": dict(model="wide", num_blocks=64, block_size=16, max_batch=4,
+                        max_tokens_per_step=512, watermark=0, requests="wide"),
+}
+
+
+def token_requests(kind: str):
+    from casegen import TOY_MODEL, bimodal_workload
+    if kind == "bench":
+        return bimodal_workload(96, TOY_MODEL["vocab"])
+    if kind == "seeded":
+        lens = det_ints(11, 1, 24, 8, 32)
+        toks = det_ints(11, 2, int(lens.sum()), 1, TOY_MODEL["vocab"] - 1)
+        prompts, off = [], 0
+        for n in lens:
+            prompts.append(toks[off:off + n].tolist())
+            off += int(n)
+        max_new = [int(x) for x in det_ints(11, 3, 24, 4, 40)]
+        return prompts, max_new
+    prompts = [[int(x) for x in det_ints(12, i, n, 1, 31999)] for i, n in enumerate((12, 7, 20))]
+    return prompts, [3, 2, 3]
+
+
+def token_trace(ref: RefPath, spec: dict) -> dict:
+    import tempfile
+
+    from casegen import TOY_MODEL, WIDE_MODEL
+    model = TOY_MODEL if spec["model"] == "toy" else WIDE_MODEL
+    prompts, max_new = token_requests(spec["requests"])
+    with tempfile.NamedTemporaryFile(suffix=".trace") as f:
+        ref.generate(model, spec["num_blocks"], spec["block_size"], spec["max_batch"],
+                     spec["max_tokens_per_step"], spec["watermark"], prompts, max_new, f.name)
+        raw = np.fromfile(f.name, dtype="<i8")
+    # float bit patterns are uint32: keep the trace as int64
+    return dict(trace=raw, model=np.array([model[k] for k in
+                ("vocab", "hidden", "layers", "heads", "head_dim", "ffn")], np.int64),
+                num_blocks=np.int64(spec["num_blocks"]), block_size=np.int64(spec["block_size"]))
+
+
 def main() -> None:
+    import sys
     build(with_reference=True)
     ref = RefPath()
+    if "--tokens-only" not in sys.argv:
+        _main_cases(ref)
+    for name, spec in TOKEN_TRACES.items():
+        np.savez_compressed(OUT / f"{name}.npz", **token_trace(ref, spec))
+        print(f"{name} saved")
+
+
+def _main_cases(ref: RefPath) -> None:
     for case in golden_cases():
         data = run_case(ref, case)
         np.savez_compressed(OUT / f"{case.name}.npz", **data)
