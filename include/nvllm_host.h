@@ -89,6 +89,35 @@ int nvllm_engine_arenas(nvllm_engine* e, float** k_arena, float** v_arena);
 void* nvllm_engine_stream(nvllm_engine* e);
 int32_t nvllm_engine_step_tokens(const nvllm_engine* e);
 
+/* ---- device model (TransformerModel, src/model.cpp:64-312) ----------------
+ * The reference's LCG-weighted transformer on the engine's GPU: weights
+ * generated on the device in the constructor's draw order, forward_batch as
+ * device kernels (embedding gather, RMSNorm, fp32 projections, paged KV write
+ * and attention through the engine, SiLU, residual adds, last-token gather,
+ * LM head, repetition-penalised greedy sampling). The engine's layout must
+ * match (layers, heads, head_dim); destroy the model before its engine. */
+typedef struct nvllm_model nvllm_model;
+typedef struct nvllm_model_config {
+    int64_t vocab, hidden, layers, heads, head_dim, ffn;
+    float emb_scale, ffn_scale; /* weight scales; 0 = 1/sqrt(hidden), 1/sqrt(ffn) */
+} nvllm_model_config;
+
+int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvllm_model** out);
+void nvllm_model_destroy(nvllm_model* m);
+/* forward_batch over the step begun with nvllm_engine_begin_step: token_ids =
+ * the uncomputed tokens of every sequence in batch order (num_tokens of them,
+ * taken modulo the vocabulary), prev_tokens[s] = sequence s's last token.
+ * Writes sampled[num_seqs]. With top_k in 1..32 also writes margins[s] (top-1
+ * minus top-2 of the penalised logits) and the top_k largest raw logits of
+ * each row (top_idx / top_val, [num_seqs, top_k]). Returns once the results
+ * are on the host. */
+int nvllm_model_forward(nvllm_model* m, const int64_t* token_ids, int64_t num_tokens,
+                        const int64_t* prev_tokens, int64_t num_seqs, int64_t* sampled,
+                        int32_t precision, float* margins, int32_t* top_idx, float* top_val,
+                        int32_t top_k);
+/* The device weight buffer (read-only; count floats in draw order). */
+int nvllm_model_weights(const nvllm_model* m, const float** weights, int64_t* count);
+
 /* ---- cross-process device buffers (head split) ---------------------------
  * nvllm_ipc_alloc: cudaMalloc of `bytes` on the current device, zero-filled,
  * and its 64-byte CUDA IPC handle. nvllm_ipc_open maps a peer process's buffer

@@ -1,0 +1,58 @@
+/*
+ * nvllm device ops (libnvllm.so): the rest of TransformerModel::forward_batch
+ * around the paged-attention path (src/model.cpp:64-122, :161-187, :262-311),
+ * for running the whole forward on the GPU. fp32 device pointers, asynchronous
+ * on `stream` (a cudaStream_t), NVLLM_OK or an nvllm_status code.
+ */
+#ifndef NVLLM_OPS_H
+#define NVLLM_OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Weight initialisation of TransformerModel (src/model.cpp:71-112):
+ * out[r * ld + c] (r < rows, c < cols) is draw number
+ * stream_offset + r * cols + c of the model's 64-bit LCG (seed 0x5DEECE66D,
+ * multiplier 6364136223846793005, increment 1), each draw
+ * (float(state >> 33) / 2^32 - 0.5) * scale. Every lane jumps ahead in the
+ * LCG, so the fill is parallel and bit-identical to the sequential loop. */
+int nvllm_lcg_fill(float* out, int64_t rows, int64_t cols, int64_t ld, uint64_t stream_offset,
+                   float scale, void* stream);
+
+/* out[t] = table[token_ids[t] % vocab] (src/model.cpp:161-166). */
+int nvllm_embedding_gather(float* out, const float* table, const int32_t* token_ids, int64_t n,
+                           int64_t vocab, int64_t dim, void* stream);
+
+/* RMSNorm per row: out = x / sqrt(mean(x^2) + eps) * weight (weight NULL = 1),
+ * src/model.cpp:20-38. out may alias in. */
+int nvllm_rms_norm(float* out, const float* in, const float* weight, int64_t rows, int64_t dim,
+                   float eps, void* stream);
+
+/* x = x / (1 + exp(-x)) in place (src/model.cpp:271-273). */
+int nvllm_silu(float* x, int64_t count, void* stream);
+
+/* x += y (residual adds, src/model.cpp:264-266, :275-277). */
+int nvllm_add(float* x, const float* y, int64_t count, void* stream);
+
+/* out[i] = in[rows[i]] for i < count, in holding num_in_rows rows (last-token
+ * gather, src/model.cpp:280-286); rows outside in raise NVLLM_ERR_BOUNDS. */
+int nvllm_gather_rows(float* out, const float* in, const int32_t* rows, int64_t count,
+                      int64_t num_in_rows, int64_t dim, void* stream);
+
+/* Greedy sampling with the reference's repetition penalty
+ * (src/model.cpp:293-309): sampled[r] = argmax_t (logits[r][t] - penalty if
+ * t == prev_tokens[r]), lowest index on ties. Optional outputs (NULL to skip):
+ * margin[r] = top-1 minus top-2 of those penalised values; top_idx / top_val
+ * [rows, top_k] = the top_k largest raw logits, descending (top_k <= 32). */
+int nvllm_penalized_argmax(const float* logits, const int64_t* prev_tokens, int64_t rows,
+                           int64_t vocab, float penalty, int32_t* sampled, float* margin,
+                           int32_t* top_idx, float* top_val, int32_t top_k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NVLLM_OPS_H */

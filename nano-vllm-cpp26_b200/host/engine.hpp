@@ -41,8 +41,8 @@ struct EngineConfig {
 };
 
 struct EngineError {
-    enum class Kind { Invalid, Cuda, Pack, Kernel, NoStep } kind;
-    int code = 0;  // cudaError_t, PackError or nvllm status, by kind
+    enum class Kind { Invalid, Cuda, Pack, Kernel, NoStep, Blas } kind;
+    int code = 0;  // cudaError_t, PackError, nvllm status or cublasStatus_t, by kind
 };
 
 class AttentionEngine {
@@ -64,6 +64,9 @@ public:
     float* host_value() noexcept { return h_v_; }
     float* host_output() noexcept { return h_out_; }
     const MetadataLayout& step() const noexcept { return step_; }
+    bool has_step() const noexcept { return have_step_; }
+    // the step's packed metadata on the device (offsets in step())
+    const unsigned char* device_metadata() const noexcept { return d_meta_; }
 
     // Flattens the batch and uploads its metadata (one cudaMemcpyAsync).
     std::expected<void, EngineError> begin_step(std::span<const SequenceView> seqs);

@@ -8,6 +8,7 @@
 #include "block_allocator.hpp"
 #include "engine.hpp"
 #include "metadata.hpp"
+#include "model.hpp"
 
 struct nvllm_block_allocator {
     nvllm::BlockAllocator impl;
@@ -16,6 +17,10 @@ struct nvllm_block_allocator {
 
 struct nvllm_engine {
     std::unique_ptr<nvllm::AttentionEngine> impl;
+};
+
+struct nvllm_model {
+    std::unique_ptr<nvllm::DeviceModel> impl;
 };
 
 namespace {
@@ -28,6 +33,7 @@ int kv_status(nvllm::KVError e) {
 int engine_status(const nvllm::EngineError& e) {
     switch (e.kind) {
         case nvllm::EngineError::Kind::Cuda: return NVLLM_ERR_CUDA;
+        case nvllm::EngineError::Kind::Blas: return NVLLM_ERR_CUDA;
         case nvllm::EngineError::Kind::Pack: return NVLLM_HOST_PACK_ERROR;
         case nvllm::EngineError::Kind::Kernel: return e.code;
         default: return NVLLM_ERR_INVALID;
@@ -222,6 +228,44 @@ void* nvllm_engine_stream(nvllm_engine* e) { return e ? e->impl->stream() : null
 
 int32_t nvllm_engine_step_tokens(const nvllm_engine* e) {
     return e ? e->impl->step().num_tokens : -1;
+}
+
+int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvllm_model** out) {
+    if (cfg == nullptr || engine == nullptr || out == nullptr) return NVLLM_ERR_INVALID;
+    nvllm::ModelConfig mc{.vocab = cfg->vocab, .hidden = cfg->hidden, .layers = cfg->layers,
+                          .heads = cfg->heads, .head_dim = cfg->head_dim, .ffn = cfg->ffn,
+                          .emb_scale = cfg->emb_scale, .ffn_scale = cfg->ffn_scale};
+    auto r = nvllm::DeviceModel::create(mc, *engine->impl);
+    if (!r) return engine_status(r.error());
+    auto* m = new (std::nothrow) nvllm_model{std::move(*r)};
+    if (m == nullptr) return NVLLM_ERR_INVALID;
+    *out = m;
+    return NVLLM_OK;
+}
+
+void nvllm_model_destroy(nvllm_model* m) { delete m; }
+
+int nvllm_model_forward(nvllm_model* m, const int64_t* token_ids, int64_t num_tokens,
+                        const int64_t* prev_tokens, int64_t num_seqs, int64_t* sampled,
+                        int32_t precision, float* margins, int32_t* top_idx, float* top_val,
+                        int32_t top_k) {
+    if (m == nullptr || num_tokens < 0 || num_seqs < 0 ||
+        (num_tokens > 0 && token_ids == nullptr) ||
+        (num_seqs > 0 && (prev_tokens == nullptr || sampled == nullptr))) {
+        return NVLLM_ERR_INVALID;
+    }
+    auto r = m->impl->forward(
+        std::span<const int64_t>(token_ids, std::size_t(num_tokens)),
+        std::span<const int64_t>(prev_tokens, std::size_t(num_seqs)), sampled, precision, margins,
+        top_idx, top_val, top_k);
+    return r ? NVLLM_OK : engine_status(r.error());
+}
+
+int nvllm_model_weights(const nvllm_model* m, const float** weights, int64_t* count) {
+    if (m == nullptr || weights == nullptr || count == nullptr) return NVLLM_ERR_INVALID;
+    *weights = m->impl->weights();
+    *count = int64_t(m->impl->weight_floats());
+    return NVLLM_OK;
 }
 
 int nvllm_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {

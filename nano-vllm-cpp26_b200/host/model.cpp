@@ -1,0 +1,245 @@
+#include "model.hpp"
+
+#include <climits>
+#include <cmath>
+
+#include "../../include/nvllm_ops.h"
+
+namespace nvllm {
+
+namespace {
+
+constexpr float kRmsEps = 1e-5f;        // src/model.cpp:33
+constexpr float kRepeatPenalty = 1.5f;  // src/model.cpp:301
+constexpr int32_t kMaxTopK = 32;
+
+std::unexpected<EngineError> cuda_error(cudaError_t e) {
+    return std::unexpected(EngineError{EngineError::Kind::Cuda, int(e)});
+}
+std::unexpected<EngineError> blas_error(cublasStatus_t s) {
+    return std::unexpected(EngineError{EngineError::Kind::Blas, int(s)});
+}
+std::unexpected<EngineError> kernel_error(int rc) {
+    return std::unexpected(EngineError{EngineError::Kind::Kernel, rc});
+}
+std::unexpected<EngineError> invalid() {
+    return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+}
+
+#define NVLLM_CUDA_TRY(expr)                          \
+    do {                                              \
+        const cudaError_t e_ = (expr);                \
+        if (e_ != cudaSuccess) return cuda_error(e_); \
+    } while (0)
+#define NVLLM_BLAS_TRY(expr)                                    \
+    do {                                                        \
+        const cublasStatus_t s_ = (expr);                       \
+        if (s_ != CUBLAS_STATUS_SUCCESS) return blas_error(s_); \
+    } while (0)
+#define NVLLM_OP_TRY(expr)                           \
+    do {                                             \
+        const int rc_ = (expr);                      \
+        if (rc_ != NVLLM_OK) return kernel_error(rc_); \
+    } while (0)
+
+constexpr std::size_t align16(std::size_t x) { return (x + 15) & ~std::size_t(15); }
+
+}  // namespace
+
+std::expected<std::unique_ptr<DeviceModel>, EngineError> DeviceModel::create(
+    const ModelConfig& cfg, AttentionEngine& eng) {
+    const nvllm_kv_layout& L = eng.config().layout;
+    if (cfg.vocab <= 0 || cfg.vocab > INT32_MAX || cfg.hidden <= 0 || cfg.layers <= 0 ||
+        cfg.heads <= 0 || cfg.head_dim <= 0 || cfg.ffn <= 0 ||
+        cfg.hidden != cfg.heads * cfg.head_dim || cfg.hidden > INT32_MAX ||
+        cfg.ffn > INT32_MAX || L.num_layers != cfg.layers || L.num_heads != cfg.heads ||
+        L.head_dim != cfg.head_dim || cfg.emb_scale < 0.0f || cfg.ffn_scale < 0.0f) {
+        return invalid();
+    }
+    std::unique_ptr<DeviceModel> m(new DeviceModel(cfg, eng));
+    if (auto r = m->init(); !r) return std::unexpected(r.error());
+    return m;
+}
+
+std::expected<void, EngineError> DeviceModel::init() {
+    const int64_t V = cfg_.vocab, D = cfg_.hidden, F = cfg_.ffn;
+    const int64_t T = eng_.config().max_tokens, S = eng_.config().max_seqs;
+    cudaStream_t st = eng_.stream();
+    NVLLM_CUDA_TRY(cudaSetDevice(eng_.config().device));
+    NVLLM_BLAS_TRY(cublasCreate(&blas_));
+    NVLLM_BLAS_TRY(cublasSetStream(blas_, st));
+    // plain fp32 arithmetic: no TF32 down-conversion inside cuBLAS
+    NVLLM_BLAS_TRY(cublasSetMathMode(blas_, CUBLAS_DEFAULT_MATH));
+
+    // weights, in the reference constructor's draw order
+    layer_floats_ = std::size_t(4 * D * D + 2 * D * F);
+    w_floats_ = std::size_t(V * D) + std::size_t(cfg_.layers) * layer_floats_ + std::size_t(D * V);
+    NVLLM_CUDA_TRY(cudaMalloc(&d_w_, w_floats_ * sizeof(float)));
+    const float emb_scale =
+        cfg_.emb_scale > 0.0f ? cfg_.emb_scale : 1.0f / std::sqrt(static_cast<float>(D));
+    const float ffn_scale =
+        cfg_.ffn_scale > 0.0f ? cfg_.ffn_scale : 1.0f / std::sqrt(static_cast<float>(F));
+    uint64_t draw = 0;
+    auto fill = [&](int64_t rows, int64_t cols, float scale) -> int {
+        const int rc = nvllm_lcg_fill(d_w_ + draw, rows, cols, cols, draw, scale, st);
+        draw += uint64_t(rows * cols);
+        return rc;
+    };
+    NVLLM_OP_TRY(fill(V, D, emb_scale));
+    for (int64_t l = 0; l < cfg_.layers; ++l) {
+        for (int i = 0; i < 4; ++i) NVLLM_OP_TRY(fill(D, D, emb_scale));  // w_q, w_k, w_v, w_o
+        NVLLM_OP_TRY(fill(D, F, emb_scale));                               // w_up
+        NVLLM_OP_TRY(fill(F, D, ffn_scale));                               // w_down
+    }
+    NVLLM_OP_TRY(fill(D, V, emb_scale));  // LM head
+    if (draw != w_floats_) return invalid();
+
+    const std::size_t act = std::size_t(T * D * 6 + T * F + S * D + S * V);
+    NVLLM_CUDA_TRY(cudaMalloc(&d_act_, act * sizeof(float)));
+    d_hidden_ = d_act_;
+    d_norm_ = d_hidden_ + T * D;
+    d_qkv_ = d_norm_ + T * D;
+    d_attn_ = d_qkv_ + 3 * T * D;
+    d_up_ = d_attn_ + T * D;
+    d_last_ = d_up_ + T * F;
+    d_logits_ = d_last_ + S * D;
+
+    io_in_bytes_ = align16(std::size_t(T) * 4) + align16(std::size_t(S) * 8);
+    io_out_bytes_ = 2 * align16(std::size_t(S) * 4) + 2 * std::size_t(S) * kMaxTopK * 4;
+    NVLLM_CUDA_TRY(cudaMalloc(&d_io_, io_in_bytes_ + io_out_bytes_));
+    NVLLM_CUDA_TRY(cudaMallocHost(&h_io_, io_in_bytes_ + io_out_bytes_));
+    d_tokens_ = reinterpret_cast<int32_t*>(d_io_);
+    d_prev_ = reinterpret_cast<int64_t*>(d_io_ + align16(std::size_t(T) * 4));
+    unsigned char* out = d_io_ + io_in_bytes_;
+    d_sampled_ = reinterpret_cast<int32_t*>(out);
+    d_margin_ = reinterpret_cast<float*>(out + align16(std::size_t(S) * 4));
+    d_top_idx_ = reinterpret_cast<int32_t*>(out + 2 * align16(std::size_t(S) * 4));
+    d_top_val_ = reinterpret_cast<float*>(d_top_idx_ + S * kMaxTopK);
+    NVLLM_CUDA_TRY(cudaEventCreateWithFlags(&io_done_, cudaEventDisableTiming));
+    NVLLM_CUDA_TRY(cudaEventRecord(io_done_, st));
+    NVLLM_CUDA_TRY(cudaStreamSynchronize(st));
+    return {};
+}
+
+DeviceModel::~DeviceModel() {
+    cudaSetDevice(eng_.config().device);
+    cudaStreamSynchronize(eng_.stream());
+    if (blas_) cublasDestroy(blas_);
+    if (io_done_) cudaEventDestroy(io_done_);
+    if (h_io_) cudaFreeHost(h_io_);
+    if (d_io_) cudaFree(d_io_);
+    if (d_act_) cudaFree(d_act_);
+    if (d_w_) cudaFree(d_w_);
+}
+
+// Row-major C[m, n] = A[m, k] . W[k, n] + beta * C: the column-major product
+// C^T = W^T A^T, with W^T and A^T being the row-major buffers read as
+// column-major.
+std::expected<void, EngineError> DeviceModel::gemm(const float* a, const float* w, float* c,
+                                                   int64_t m, int64_t k, int64_t n, float beta) {
+    const float one = 1.0f;
+    NVLLM_BLAS_TRY(cublasSgemm(blas_, CUBLAS_OP_N, CUBLAS_OP_N, int(n), int(m), int(k), &one, w,
+                               int(n), a, int(k), &beta, c, int(n)));
+    return {};
+}
+
+std::expected<void, EngineError> DeviceModel::enqueue(std::span<const int64_t> token_ids,
+                                                      std::span<const int64_t> prev_tokens,
+                                                      int32_t precision, int32_t top_k) {
+    const MetadataLayout& step = eng_.step();
+    if (!eng_.has_step() || token_ids.size() != std::size_t(step.num_tokens) ||
+        prev_tokens.size() != std::size_t(step.num_seqs) || top_k < 0 || top_k > kMaxTopK) {
+        return invalid();
+    }
+    const int64_t V = cfg_.vocab, D = cfg_.hidden, F = cfg_.ffn;
+    const int64_t T = step.num_tokens, S = step.num_seqs;
+    last_rows_ = int32_t(S);
+    if (S == 0) return {};
+    cudaStream_t st = eng_.stream();
+    NVLLM_CUDA_TRY(cudaSetDevice(eng_.config().device));
+
+    // inputs: token ids modulo the vocabulary (src/model.cpp:152) and the
+    // previous tokens, one upload from pinned staging
+    NVLLM_CUDA_TRY(cudaEventSynchronize(io_done_));
+    auto* h_tok = reinterpret_cast<int32_t*>(h_io_);
+    auto* h_prev = reinterpret_cast<int64_t*>(h_io_ + align16(std::size_t(eng_.config().max_tokens) * 4));
+    for (int64_t t = 0; t < T; ++t) {
+        if (token_ids[t] < 0) return invalid();
+        h_tok[t] = int32_t(token_ids[t] % V);
+    }
+    for (int64_t s = 0; s < S; ++s) h_prev[s] = prev_tokens[s];
+    NVLLM_CUDA_TRY(cudaMemcpyAsync(d_io_, h_io_, io_in_bytes_, cudaMemcpyHostToDevice, st));
+    NVLLM_CUDA_TRY(cudaEventRecord(io_done_, st));
+
+    const float* emb = d_w_;
+    NVLLM_OP_TRY(nvllm_embedding_gather(d_hidden_, emb, d_tokens_, T, V, D, st));
+    const float one = 1.0f, zero = 0.0f;
+    for (int64_t l = 0; l < cfg_.layers; ++l) {
+        const float* lw = d_w_ + V * D + std::size_t(l) * layer_floats_;
+        const float* w_q = lw;  // w_q, w_k, w_v: three adjacent [D, D]
+        const float* w_o = lw + 3 * D * D;
+        const float* w_up = lw + 4 * D * D;
+        const float* w_down = w_up + D * F;
+        NVLLM_OP_TRY(nvllm_rms_norm(d_norm_, d_hidden_, nullptr, T, D, kRmsEps, st));
+        // Q, K, V = norm . {w_q, w_k, w_v} as one batched GEMM (src/model.cpp:184-186)
+        NVLLM_BLAS_TRY(cublasSgemmStridedBatched(blas_, CUBLAS_OP_N, CUBLAS_OP_N, int(D), int(T),
+                                                 int(D), &one, w_q, int(D), D * D, d_norm_,
+                                                 int(D), 0, &zero, d_qkv_, int(D), T * D, 3));
+        const float* q = d_qkv_;
+        const float* k = d_qkv_ + T * D;
+        const float* v = d_qkv_ + 2 * T * D;
+        if (auto r = eng_.attention_device(int32_t(l), q, k, v, d_attn_, precision); !r) return r;
+        // hidden += attn . w_o (src/model.cpp:263-266)
+        if (auto r = gemm(d_attn_, w_o, d_hidden_, T, D, D, 1.0f); !r) return r;
+        NVLLM_OP_TRY(nvllm_rms_norm(d_norm_, d_hidden_, nullptr, T, D, kRmsEps, st));
+        if (auto r = gemm(d_norm_, w_up, d_up_, T, D, F, 0.0f); !r) return r;
+        NVLLM_OP_TRY(nvllm_silu(d_up_, T * F, st));
+        // hidden += silu(up) . w_down (src/model.cpp:274-277)
+        if (auto r = gemm(d_up_, w_down, d_hidden_, T, F, D, 1.0f); !r) return r;
+    }
+    const auto* last_idx = reinterpret_cast<const int32_t*>(eng_.device_metadata() + step.last_off);
+    NVLLM_OP_TRY(nvllm_gather_rows(d_last_, d_hidden_, last_idx, S, T, D, st));
+    const float* lm = d_w_ + V * D + std::size_t(cfg_.layers) * layer_floats_;
+    if (auto r = gemm(d_last_, lm, d_logits_, S, D, V, 0.0f); !r) return r;
+    NVLLM_OP_TRY(nvllm_penalized_argmax(d_logits_, d_prev_, S, V, kRepeatPenalty, d_sampled_,
+                                        top_k > 0 ? d_margin_ : nullptr,
+                                        top_k > 0 ? d_top_idx_ : nullptr,
+                                        top_k > 0 ? d_top_val_ : nullptr, top_k, st));
+    return {};
+}
+
+std::expected<void, EngineError> DeviceModel::forward(std::span<const int64_t> token_ids,
+                                                      std::span<const int64_t> prev_tokens,
+                                                      int64_t* sampled, int32_t precision,
+                                                      float* margins, int32_t* top_idx,
+                                                      float* top_val, int32_t top_k) {
+    if (auto r = enqueue(token_ids, prev_tokens, precision, top_k); !r) return r;
+    const int64_t S = last_rows_;
+    if (S == 0) return {};
+    if (sampled == nullptr) return invalid();
+    cudaStream_t st = eng_.stream();
+    unsigned char* h_out = h_io_ + io_in_bytes_;
+    const std::size_t bytes = top_k > 0 ? io_out_bytes_ : std::size_t(S) * 4;
+    NVLLM_CUDA_TRY(cudaMemcpyAsync(h_out, d_io_ + io_in_bytes_, bytes, cudaMemcpyDeviceToHost, st));
+    NVLLM_CUDA_TRY(cudaStreamSynchronize(st));
+    const int32_t status = nvllm_get_last_error(st);
+    if (status != NVLLM_OK) return kernel_error(status);
+    const int64_t S_cap = eng_.config().max_seqs;
+    const auto* h_sampled = reinterpret_cast<const int32_t*>(h_out);
+    for (int64_t s = 0; s < S; ++s) sampled[s] = h_sampled[s];
+    if (top_k > 0) {
+        const auto* h_margin = reinterpret_cast<const float*>(h_out + align16(std::size_t(S_cap) * 4));
+        const auto* h_ti = reinterpret_cast<const int32_t*>(h_out + 2 * align16(std::size_t(S_cap) * 4));
+        const auto* h_tv = reinterpret_cast<const float*>(h_ti + S_cap * kMaxTopK);
+        for (int64_t s = 0; s < S; ++s) {
+            if (margins) margins[s] = h_margin[s];
+            for (int32_t j = 0; j < top_k; ++j) {
+                if (top_idx) top_idx[s * top_k + j] = h_ti[s * top_k + j];
+                if (top_val) top_val[s * top_k + j] = h_tv[s * top_k + j];
+            }
+        }
+    }
+    return {};
+}
+
+}  // namespace nvllm

@@ -1,0 +1,106 @@
+// DeviceModel: TransformerModel::forward_batch (src/model.cpp:124-312) on one
+// GPU, around the AttentionEngine that holds the paged KV arenas.
+//
+// Weights are the reference's LCG weights (src/model.cpp:64-112), generated on
+// the device in the constructor's draw order into one allocation laid out as
+// that order: embedding [V, D]; per layer w_q, w_k, w_v, w_o [D, D], w_up
+// [D, F], w_down [F, D]; LM head [D, V] (all row-major [k, n], the operand
+// layout of matmul_batched). The RMSNorm weights are all ones and are not
+// stored (src/model.cpp:88-89).
+//
+// One forward per engine step, all on the engine's stream: embedding gather,
+// per layer RMSNorm, one strided-batched GEMM for Q/K/V (w_q, w_k, w_v are
+// adjacent), KV write + paged attention (the engine), W_o GEMM accumulating
+// into the residual, RMSNorm, up GEMM, SiLU, down GEMM accumulating into the
+// residual; then the last-token gather, the LM-head GEMM and the penalised
+// argmax. The projections are fp32 cuBLAS SGEMMs (no TF32).
+#pragma once
+
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <expected>
+#include <memory>
+#include <span>
+
+#include "engine.hpp"
+
+namespace nvllm {
+
+struct ModelConfig {
+    int64_t vocab = 0, hidden = 0, layers = 0, heads = 0, head_dim = 0, ffn = 0;
+    // weight scales of src/model.cpp:81-82; 0 = 1/sqrt(hidden), 1/sqrt(ffn)
+    float emb_scale = 0.0f, ffn_scale = 0.0f;
+};
+
+class DeviceModel {
+public:
+    // The engine's layout must match the model (layers, heads, head_dim); the
+    // model keeps a reference to it.
+    static std::expected<std::unique_ptr<DeviceModel>, EngineError> create(const ModelConfig& cfg,
+                                                                           AttentionEngine& eng);
+    ~DeviceModel();
+    DeviceModel(const DeviceModel&) = delete;
+    DeviceModel& operator=(const DeviceModel&) = delete;
+
+    const ModelConfig& config() const noexcept { return cfg_; }
+    const float* weights() const noexcept { return d_w_; }
+    std::size_t weight_floats() const noexcept { return w_floats_; }
+
+    // forward_batch over the step begun with AttentionEngine::begin_step:
+    // token_ids = the uncomputed tokens of every sequence in flatten order
+    // (taken modulo the vocabulary, src/model.cpp:152), prev_tokens[s] = the
+    // sequence's last token (src/model.cpp:297-298). Writes sampled[s]; with
+    // top_k > 0 also the top-2 margin of the penalised logits and the top_k
+    // largest raw logits of every row. Returns once the results are on the host.
+    std::expected<void, EngineError> forward(std::span<const int64_t> token_ids,
+                                             std::span<const int64_t> prev_tokens,
+                                             int64_t* sampled, int32_t precision,
+                                             float* margins = nullptr, int32_t* top_idx = nullptr,
+                                             float* top_val = nullptr, int32_t top_k = 0);
+
+    // Asynchronous half of forward(): enqueues the whole step on the engine's
+    // stream, with the sampled ids left in device memory (device_sampled()).
+    std::expected<void, EngineError> enqueue(std::span<const int64_t> token_ids,
+                                             std::span<const int64_t> prev_tokens,
+                                             int32_t precision, int32_t top_k = 0);
+    const int32_t* device_sampled() const noexcept { return d_sampled_; }
+
+private:
+    DeviceModel(const ModelConfig& cfg, AttentionEngine& eng) : cfg_(cfg), eng_(eng) {}
+    std::expected<void, EngineError> init();
+    std::expected<void, EngineError> gemm(const float* a, const float* w, float* c, int64_t m,
+                                          int64_t k, int64_t n, float beta);
+
+    ModelConfig cfg_;
+    AttentionEngine& eng_;
+    cublasHandle_t blas_ = nullptr;
+    float* d_w_ = nullptr;
+    std::size_t w_floats_ = 0;
+    std::size_t layer_floats_ = 0;
+    // activations, sized for the engine's max_tokens (T) and max_seqs (S)
+    float* d_act_ = nullptr;
+    float* d_hidden_ = nullptr;  // [T, D]
+    float* d_norm_ = nullptr;    // [T, D]
+    float* d_qkv_ = nullptr;     // [3, T, D]
+    float* d_attn_ = nullptr;    // [T, D]
+    float* d_up_ = nullptr;      // [T, F]
+    float* d_last_ = nullptr;    // [S, D]
+    float* d_logits_ = nullptr;  // [S, V]
+    // per-step inputs (one upload) and results (one download)
+    unsigned char* d_io_ = nullptr;
+    unsigned char* h_io_ = nullptr;
+    std::size_t io_in_bytes_ = 0, io_out_bytes_ = 0;
+    int32_t* d_tokens_ = nullptr;   // [T]
+    int64_t* d_prev_ = nullptr;     // [S]
+    int32_t* d_sampled_ = nullptr;  // [S]
+    float* d_margin_ = nullptr;     // [S]
+    int32_t* d_top_idx_ = nullptr;  // [S, 32]
+    float* d_top_val_ = nullptr;    // [S, 32]
+    cudaEvent_t io_done_ = nullptr;
+    int32_t last_rows_ = 0;
+};
+
+}  // namespace nvllm

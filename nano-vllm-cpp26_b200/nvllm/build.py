@@ -6,8 +6,8 @@
   device code and links them; the static CUDA runtime is linked in so the
   library depends only on the driver.
 * lib/libnvllm_host.so: g++ -std=c++23 compiles host/*.cpp (block allocator,
-  metadata packer, engine, their C ABI) against libnvllm.so and the static
-  CUDA runtime.
+  metadata packer, engine, device model, their C ABI) against libnvllm.so,
+  cuBLAS (the model's fp32 projections) and the static CUDA runtime.
 """
 from __future__ import annotations
 
@@ -51,7 +51,7 @@ def _stale(target: Path, deps: list[Path]) -> bool:
 def build(force: bool = False, verbose: bool = False) -> Path:
     LIB.mkdir(exist_ok=True)
     out = LIB / LIBNAME
-    deps = sources() + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "nvllm.h", Path(__file__)]
+    deps = sources() + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h")) + [Path(__file__)]
     if not force and not _stale(out, deps):
         return out
     objdir = LIB / "_obj"
@@ -89,15 +89,15 @@ def build_host(force: bool = False, verbose: bool = False) -> Path:
     core = build(force=False, verbose=verbose)
     out = LIB / HOSTLIB
     srcs = sorted(HOST.glob("*.cpp"))
-    deps = srcs + sorted(HOST.glob("*.hpp")) + [INCLUDE / "nvllm.h", INCLUDE / "nvllm_host.h",
-                                                 core, Path(__file__)]
+    deps = srcs + sorted(HOST.glob("*.hpp")) + sorted(INCLUDE.glob("*.h")) + [core, Path(__file__)]
     if not force and not _stale(out, deps):
         return out
     cxx = shutil.which("g++") or "g++"
     tmp = out.with_suffix(".so.tmp")
     cmd = [cxx, "-std=c++23", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-pthread",
            f"-I{INCLUDE}", f"-I{CUDA_HOME / 'include'}", *map(str, srcs), "-o", str(tmp),
-           f"-L{LIB}", "-lnvllm", f"-L{CUDA_HOME / 'lib64'}", "-lcudart_static", "-ldl", "-lrt",
+           f"-L{LIB}", "-lnvllm", f"-L{CUDA_HOME / 'lib64'}", "-lcublas", "-lcudart_static",
+           "-ldl", "-lrt",
            "-Wl,-rpath,$ORIGIN"]
     if verbose:
         print(" ".join(cmd))

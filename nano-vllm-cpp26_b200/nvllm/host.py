@@ -36,6 +36,12 @@ class EngineConfig(ctypes.Structure):
                 ("device", ctypes.c_int32)]
 
 
+class ModelConfig(ctypes.Structure):
+    _fields_ = [("vocab", ctypes.c_int64), ("hidden", ctypes.c_int64), ("layers", ctypes.c_int64),
+                ("heads", ctypes.c_int64), ("head_dim", ctypes.c_int64), ("ffn", ctypes.c_int64),
+                ("emb_scale", ctypes.c_float), ("ffn_scale", ctypes.c_float)]
+
+
 _HOST: ctypes.CDLL | None = None
 
 
@@ -75,6 +81,11 @@ def host_lib() -> ctypes.CDLL:
     L.nvllm_engine_stream.argtypes = [_vp]
     L.nvllm_engine_step_tokens.restype = ctypes.c_int32
     L.nvllm_engine_step_tokens.argtypes = [_vp]
+    L.nvllm_model_create.argtypes = [ctypes.POINTER(ModelConfig), _vp, ctypes.POINTER(_vp)]
+    L.nvllm_model_destroy.argtypes = [_vp]
+    L.nvllm_model_forward.argtypes = [_vp, _i64p, ctypes.c_int64, _i64p, ctypes.c_int64, _i64p,
+                                      ctypes.c_int32, _f32p, _i32p, _f32p, ctypes.c_int32]
+    L.nvllm_model_weights.argtypes = [_vp, ctypes.POINTER(_f32p), _i64p]
     _HOST = L
     return L
 
@@ -231,3 +242,58 @@ class Engine:
 
     def step_tokens(self) -> int:
         return self.L.nvllm_engine_step_tokens(self.h)
+
+
+class Model:
+    """The reference TransformerModel on the engine's GPU (nvllm_model_*):
+    LCG weights generated on the device, forward_batch as device kernels.
+    ``cfg`` holds vocab, hidden, layers, heads, head_dim, ffn; ``scales`` the
+    optional [emb_scale, ffn_scale] of the weights."""
+
+    def __init__(self, cfg: dict, engine: Engine, scales=None):
+        self.L = host_lib()
+        self.engine = engine  # the model uses the engine's arenas and stream
+        self.cfg = dict(cfg)
+        es, fs = (0.0, 0.0) if scales is None else (float(scales[0]), float(scales[1]))
+        mc = ModelConfig(cfg["vocab"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["head_dim"],
+                         cfg["ffn"], es, fs)
+        h = _vp()
+        rc = self.L.nvllm_model_create(ctypes.byref(mc), engine.h, ctypes.byref(h))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_model_create")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.nvllm_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def forward(self, token_ids, prev_tokens, precision: int = 0, top_k: int = 0):
+        """forward_batch over the step begun on the engine. Returns the sampled
+        ids, or (sampled, margins, top_idx, top_val) when top_k > 0."""
+        tok = np.ascontiguousarray(token_ids, np.int64)
+        prev = np.ascontiguousarray(prev_tokens, np.int64)
+        s = len(prev)
+        sampled = np.zeros(max(s, 1), np.int64)
+        margins = np.zeros(max(s, 1), np.float32)
+        ti = np.zeros((max(s, 1), max(top_k, 1)), np.int32)
+        tv = np.zeros((max(s, 1), max(top_k, 1)), np.float32)
+        rc = self.L.nvllm_model_forward(self.h, _ptr(tok, _i64p), len(tok), _ptr(prev, _i64p), s,
+                                        _ptr(sampled, _i64p), precision, _ptr(margins, _f32p),
+                                        _ptr(ti, _i32p), _ptr(tv, _f32p), top_k)
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_model_forward")
+        if top_k > 0:
+            return sampled[:s], margins[:s], ti[:s, :top_k], tv[:s, :top_k]
+        return sampled[:s]
+
+    def weights(self) -> tuple[int, int]:
+        """(device pointer, float count) of the weight buffer."""
+        p, n = _f32p(), ctypes.c_int64()
+        rc = self.L.nvllm_model_weights(self.h, ctypes.byref(p), ctypes.byref(n))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_model_weights")
+        return ctypes.cast(p, _vp).value, n.value

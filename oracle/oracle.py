@@ -169,6 +169,14 @@ class RefPath:
         lib.ref_generate.restype = ctypes.c_int64
         lib.ref_generate.argtypes = [ctypes.c_int64] * 12 + [_i64p, _i64p, _i64p, ctypes.c_int32,
                                                              ctypes.c_int64, ctypes.c_char_p]
+        lib.ref_inv_sqrt.restype = ctypes.c_float
+        lib.ref_inv_sqrt.argtypes = [ctypes.c_float]
+        lib.ref_model_operands.restype = ctypes.c_int64
+        lib.ref_model_operands.argtypes = [ctypes.c_int64] * 7
+        lib.ref_operand_dims.restype = ctypes.c_int
+        lib.ref_operand_dims.argtypes = [ctypes.c_int64, _i64p, _i64p, _i64p]
+        lib.ref_operand_copy.restype = ctypes.c_int
+        lib.ref_operand_copy.argtypes = [ctypes.c_int64, _f32p, _f32p]
         lib.ref_forward_attention.restype = ctypes.c_int64
         lib.ref_forward_attention.argtypes = [vp, vp, ctypes.c_int32, _i32p, _i32p, _i64p,
                                               ctypes.c_int32, _f32p, _f32p, _f32p, _f32p]
@@ -258,6 +266,35 @@ class RefPath:
         if n < 0:
             raise RuntimeError("ref_generate failed")
         return read_trace(path)
+
+    def inv_sqrt(self, x: float) -> np.float32:
+        """1.0f / std::sqrt(x) as the reference build evaluates it."""
+        return np.float32(self.lib.ref_inv_sqrt(x))
+
+    def model_scales(self, model: dict) -> np.ndarray:
+        """[emb_scale, ffn_scale, softmax scale] of the reference build
+        (src/model.cpp:81-82, :205)."""
+        return np.array([self.inv_sqrt(model["hidden"]), self.inv_sqrt(model["ffn"]),
+                         self.inv_sqrt(model["head_dim"])], np.float32)
+
+    def model_operands(self, model: dict, token: int) -> list[tuple[np.ndarray, np.ndarray]]:
+        """The (A, W) operands of every matmul_batched call of one reference
+        forward_batch over a single one-token sequence: per layer Q, K, V, W_o,
+        up, down, then the LM head. The W operands are the model's LCG weights
+        as [k, n] matrices."""
+        n = self.lib.ref_model_operands(model["vocab"], model["hidden"], model["layers"],
+                                        model["heads"], model["head_dim"], model["ffn"], token)
+        if n < 0:
+            raise RuntimeError("ref_model_operands failed")
+        out = []
+        for i in range(n):
+            b, k, m = (np.zeros(1, np.int64) for _ in range(3))
+            self.lib.ref_operand_dims(i, _ptr(b, _i64p), _ptr(k, _i64p), _ptr(m, _i64p))
+            a = np.zeros((int(b[0]), int(k[0])), np.float32)
+            w = np.zeros((int(k[0]), int(m[0])), np.float32)
+            self.lib.ref_operand_copy(i, _ptr(a, _f32p), _ptr(w, _f32p))
+            out.append((a, w))
+        return out
 
 
 def read_trace(path_or_array) -> list[dict]:

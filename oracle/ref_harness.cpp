@@ -31,6 +31,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -63,6 +64,17 @@ struct LogitsCapture {
     std::vector<float> logits;
 };
 LogitsCapture g_lm;
+
+// Operand capture for ref_model_operands: every matmul_batched call of one
+// forward_batch keeps copies of its A and W operands and its (batch, k, n).
+// The W operands are the model's LCG weights (src/model.cpp:71-112) in the
+// order forward_batch uses them.
+struct OperandCapture {
+    bool active = false;
+    std::vector<std::vector<float>> a, w;
+    std::vector<std::array<std::size_t, 3>> dims;
+};
+OperandCapture g_ops;
 
 using MatmulFn = void (*)(std::span<const float>, std::span<const float>, std::span<float>,
                           std::size_t, std::size_t, std::size_t, nano_vllm::ThreadPool&);
@@ -98,6 +110,11 @@ void matmul_batched(
             std::fill_n(c.data(), count, 0.0f);
         }
         if (g_lm.active && g_lm.call++ == g_lm.target) g_lm.logits.assign(c.begin(), c.begin() + count);
+        if (g_ops.active) {
+            g_ops.a.emplace_back(a.begin(), a.begin() + batch_size * k_dim);
+            g_ops.w.emplace_back(w.begin(), w.begin() + k_dim * n_dim);
+            g_ops.dims.push_back({batch_size, k_dim, n_dim});
+        }
         return;
     }
     const std::size_t call = g_plan.call++;
@@ -378,6 +395,54 @@ int64_t ref_generate(int64_t vocab, int64_t hidden, int64_t layers, int64_t head
     }
     std::fclose(f);
     return step;
+}
+
+// 1.0f / std::sqrt(x) as the reference computes its weight and softmax scales
+// (src/model.cpp:81-82, :205), compiled with the reference's flags: under
+// -ffast-math GCC lowers it to rsqrtss plus one Newton step, which can differ
+// from the correctly rounded value in the last place.
+float ref_inv_sqrt(float x) { return 1.0f / std::sqrt(x); }
+
+// Builds the reference TransformerModel for the given configuration and runs one
+// forward_batch over a single one-token sequence (token id `token`, one block of
+// a fresh cache), capturing the A and W operands of every matmul_batched call
+// (per layer Q, K, V, W_o, up, down; then the LM head). Returns the number of
+// calls captured; ref_operand_dims / ref_operand_copy read them back.
+int64_t ref_model_operands(int64_t vocab, int64_t hidden, int64_t layers, int64_t heads,
+                           int64_t head_dim, int64_t ffn, int64_t token) {
+    if (hidden != heads * head_dim || token < 0) return -1;
+    nano_vllm::ModelConfig mc{.vocab_size = std::size_t(vocab), .hidden_dim = std::size_t(hidden),
+                              .num_layers = std::size_t(layers), .num_heads = std::size_t(heads),
+                              .head_dim = std::size_t(head_dim), .ffn_dim = std::size_t(ffn)};
+    nano_vllm::TransformerModel model(mc);
+    nano_vllm::ThreadPool pool(1);
+    nano_vllm::PagedKVCache cache(nano_vllm::KVCacheConfig{
+        .num_blocks = 1, .block_size = 1, .num_layers = std::size_t(layers),
+        .num_heads = std::size_t(heads), .head_dim = std::size_t(head_dim)});
+    std::vector<nano_vllm::SequenceState> seqs;
+    seqs.emplace_back(nano_vllm::SeqId(1), std::vector<std::size_t>{std::size_t(token)}, 1);
+    seqs.back().block_table.push_back(BlockId(0));
+    g_plan.active = false;
+    g_ops = OperandCapture{};
+    g_ops.active = true;
+    (void)model.forward_batch(seqs, cache, pool);
+    g_ops.active = false;
+    return int64_t(g_ops.dims.size());
+}
+
+int ref_operand_dims(int64_t i, int64_t* batch, int64_t* k, int64_t* n) {
+    if (i < 0 || std::size_t(i) >= g_ops.dims.size()) return -1;
+    *batch = int64_t(g_ops.dims[std::size_t(i)][0]);
+    *k = int64_t(g_ops.dims[std::size_t(i)][1]);
+    *n = int64_t(g_ops.dims[std::size_t(i)][2]);
+    return 0;
+}
+
+int ref_operand_copy(int64_t i, float* a, float* w) {
+    if (i < 0 || std::size_t(i) >= g_ops.dims.size()) return -1;
+    std::copy(g_ops.a[std::size_t(i)].begin(), g_ops.a[std::size_t(i)].end(), a);
+    std::copy(g_ops.w[std::size_t(i)].begin(), g_ops.w[std::size_t(i)].end(), w);
+    return 0;
 }
 
 }  // extern "C"

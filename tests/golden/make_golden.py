@@ -21,7 +21,9 @@ block ids and free counts it returned.
 LCG weights; see ref_generate in oracle/ref_harness.cpp): every step's running
 sequences (computed / total lengths, block tables, uncomputed token ids, the
 previous token), the tokens the reference sampled for them, the top-2 margin
-of the penalised logits and the 8 largest logits of each sampled row.
+of the penalised logits and the 8 largest logits of each sampled row, plus the
+reference build's weight and softmax scales (``scales``: 1/sqrt of hidden, ffn
+and head_dim as its -ffast-math code evaluates them).
 """
 from __future__ import annotations
 
@@ -174,7 +176,8 @@ def token_trace(ref: RefPath, spec: dict) -> dict:
     # float bit patterns are uint32: keep the trace as int64
     return dict(trace=raw, model=np.array([model[k] for k in
                 ("vocab", "hidden", "layers", "heads", "head_dim", "ffn")], np.int64),
-                num_blocks=np.int64(spec["num_blocks"]), block_size=np.int64(spec["block_size"]))
+                num_blocks=np.int64(spec["num_blocks"]), block_size=np.int64(spec["block_size"]),
+                scales=ref.model_scales(model))
 
 
 def main() -> None:

@@ -16,6 +16,21 @@ TOL_TF32 = 1e-3       # kernel with tcgen05 TF32 prefill tiles vs reference
 TOL_ORACLE = 5e-6     # C restatement vs the reference's own build (-ffast-math)
 
 
+# LM-head logits (device model vs the reference's), relative to the row's
+# largest |logit|: fp32 GEMMs in a different summation order than the
+# reference's k-outer loop
+LOGIT_RTOL = 1e-5
+
+
+def load_trace(name: str):
+    """A reference token trace: (model config, the npz, parsed steps)."""
+    from oracle.oracle import read_trace
+    z = np.load(GOLDEN / f"{name}.npz")
+    v, d, layers, heads, hd, ffn = (int(x) for x in z["model"])
+    cfg = dict(vocab=v, hidden=d, layers=layers, heads=heads, head_dim=hd, ffn=ffn)
+    return cfg, z, read_trace(z["trace"])
+
+
 def load_golden(name: str) -> dict:
     with np.load(GOLDEN / f"{name}.npz") as z:
         return {k: z[k] for k in z.files}

@@ -11,7 +11,8 @@ ROOT = Path(__file__).resolve().parents[1]
 DECL = re.compile(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(nvllm_\w+)\s*\(", re.M)
 
 
-HEADER_LIBS = {"nvllm.h": "libnvllm.so", "nvllm_host.h": "libnvllm_host.so"}
+HEADER_LIBS = {"nvllm.h": "libnvllm.so", "nvllm_ops.h": "libnvllm.so",
+               "nvllm_host.h": "libnvllm_host.so"}
 
 
 def declared(header: str) -> list[str]:
@@ -119,3 +120,30 @@ def test_validation_returns_before_any_launch(nvlib, nvmod):
                                      ctypes.c_float(0.1), 0, vp(8), 1 << 20, ctypes.byref(lay),
                                      None)  # misaligned workspace
     assert rc == nvmod.ERR_WORKSPACE
+
+
+def test_model_ops_validate_on_the_host(nvlib, nvmod):
+    """nvllm_ops.h entry points refuse bad arguments and treat empty work as a
+    no-op without touching the device."""
+    vp, i64, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float
+    st = None
+    assert nvlib.nvllm_lcg_fill(vp(256), i64(2), i64(4), i64(3), ctypes.c_uint64(0), f32(1.0),
+                                st) == nvmod.ERR_INVALID  # ld < cols
+    assert nvlib.nvllm_lcg_fill(None, i64(0), i64(4), i64(4), ctypes.c_uint64(0), f32(1.0),
+                                st) == nvmod.OK
+    assert nvlib.nvllm_embedding_gather(vp(256), vp(256), vp(256), i64(3), i64(0), i64(8),
+                                        st) == nvmod.ERR_INVALID  # empty vocabulary
+    assert nvlib.nvllm_embedding_gather(None, None, None, i64(0), i64(5), i64(8), st) == nvmod.OK
+    assert nvlib.nvllm_gather_rows(None, vp(256), vp(256), i64(2), i64(4), i64(8),
+                                   st) == nvmod.ERR_INVALID
+    assert nvlib.nvllm_rms_norm(vp(256), vp(256), None, i64(-1), i64(8), f32(1e-5),
+                                st) == nvmod.ERR_INVALID
+    assert nvlib.nvllm_rms_norm(None, None, None, i64(0), i64(8), f32(1e-5), st) == nvmod.OK
+    assert nvlib.nvllm_silu(None, i64(4), st) == nvmod.ERR_INVALID
+    assert nvlib.nvllm_add(vp(256), None, i64(4), st) == nvmod.ERR_INVALID
+    assert nvlib.nvllm_penalized_argmax(vp(256), vp(256), i64(1), i64(10), f32(1.5), vp(256),
+                                        None, vp(256), vp(256), ctypes.c_int32(33),
+                                        st) == nvmod.ERR_INVALID  # top_k > 32
+    assert nvlib.nvllm_penalized_argmax(vp(256), vp(256), i64(1), i64(10), f32(1.5), vp(256),
+                                        None, None, None, ctypes.c_int32(4),
+                                        st) == nvmod.ERR_INVALID  # top-k outputs missing
