@@ -97,9 +97,17 @@ int32_t nvllm_engine_step_tokens(const nvllm_engine* e);
  * LM head, repetition-penalised greedy sampling). The engine's layout must
  * match (layers, heads, head_dim); destroy the model before its engine. */
 typedef struct nvllm_model nvllm_model;
+/* Arithmetic of the projections (fp32 in, fp32 out either way). */
+enum nvllm_gemm_math {
+    NVLLM_GEMM_FP32 = 0,  /* fp32 FFMA (CUDA cores) */
+    NVLLM_GEMM_BF16X9 = 1 /* fp32 emulated on the tensor cores: each operand split into three
+                             bf16 terms, products accumulated in fp32 (cuBLAS's bf16x9 mode;
+                             NVLLM_ERR_UNSUPPORTED when the cuBLAS in the process lacks it) */
+};
 typedef struct nvllm_model_config {
     int64_t vocab, hidden, layers, heads, head_dim, ffn;
     float emb_scale, ffn_scale; /* weight scales; 0 = 1/sqrt(hidden), 1/sqrt(ffn) */
+    int32_t gemm_math;          /* nvllm_gemm_math */
 } nvllm_model_config;
 
 int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvllm_model** out);
@@ -117,6 +125,79 @@ int nvllm_model_forward(nvllm_model* m, const int64_t* token_ids, int64_t num_to
                         int32_t top_k);
 /* The device weight buffer (read-only; count floats in draw order). */
 int nvllm_model_weights(const nvllm_model* m, const float** weights, int64_t* count);
+
+/* ---- continuous-batching scheduler (src/scheduler.cpp) ---------------------
+ * The reference ContinuousScheduler's policy: recompute preemption of the
+ * youngest running sequences when the arena is full, admission in queue order
+ * under a batch-size, token-budget and free-block watermark limit, retirement
+ * by swap with the last running sequence. Host logic only; it draws blocks from
+ * the allocator passed to each call. */
+typedef struct nvllm_scheduler_config {
+    int64_t max_batch_size, max_tokens_per_step, watermark_blocks;
+    int64_t eos_token_id; /* < 0: none */
+} nvllm_scheduler_config;
+typedef struct nvllm_step_summary {
+    int64_t admitted, preempted, retired, batch_size, scheduled_tokens;
+} nvllm_step_summary;
+typedef struct nvllm_scheduler nvllm_scheduler;
+
+nvllm_scheduler* nvllm_scheduler_create(const nvllm_scheduler_config* cfg, int32_t block_size);
+void nvllm_scheduler_destroy(nvllm_scheduler* s);
+/* An empty prompt becomes {1}; max_new_tokens below 1 becomes 1. */
+int nvllm_scheduler_add_request(nvllm_scheduler* s, uint64_t seq_id, const int64_t* prompt,
+                                int64_t prompt_len, int64_t max_new_tokens);
+int nvllm_scheduler_schedule_step(nvllm_scheduler* s, nvllm_block_allocator* blocks,
+                                  nvllm_step_summary* out);
+/* The running batch as one trace record (int64): -1, step, n, then per
+ * sequence seq_id, num_computed, total_len, last token, table_len, table...,
+ * n_uncomputed, uncomputed.... Returns the record's length; writes it only when
+ * it fits in cap. */
+int64_t nvllm_scheduler_batch_record(const nvllm_scheduler* s, int64_t step, int64_t* out,
+                                     int64_t cap);
+/* One sampled token per running sequence, in batch order. */
+int nvllm_scheduler_process_outputs(nvllm_scheduler* s, nvllm_block_allocator* blocks,
+                                    const int64_t* sampled, int64_t n, int64_t* retired);
+int nvllm_scheduler_counts(const nvllm_scheduler* s, int64_t* running, int64_t* waiting,
+                           int64_t* preemptions, int64_t* completed);
+
+/* ---- generator: the engine loop on one GPU (src/engine.cpp:163-246) -------
+ * schedule_step -> device forward_batch -> process_step_outputs, on the
+ * engine's arena and allocator and the model's forward. Destroy before the
+ * model and the engine. */
+typedef struct nvllm_generator nvllm_generator;
+/* The reference's MetricsSnapshot (include/nano_vllm/engine.hpp:43-60). */
+typedef struct nvllm_metrics {
+    double uptime_secs;
+    uint64_t total_requests_received, total_requests_completed, total_tokens_generated;
+    double throughput_tokens_per_sec;
+    uint64_t active_batch_size, waiting_queue_depth, kv_cache_used_blocks, kv_cache_total_blocks;
+    double kv_cache_utilization_pct, avg_ttft_ms, avg_iteration_latency_ms;
+    uint64_t total_preemptions, total_iterations;
+} nvllm_metrics;
+
+int nvllm_generator_create(nvllm_engine* engine, nvllm_model* model,
+                           const nvllm_scheduler_config* cfg, int32_t precision,
+                           nvllm_generator** out);
+void nvllm_generator_destroy(nvllm_generator* g);
+int nvllm_generator_add_request(nvllm_generator* g, uint64_t seq_id, const int64_t* prompt,
+                                int64_t prompt_len, int64_t max_new_tokens);
+int nvllm_generator_step(nvllm_generator* g, nvllm_step_summary* out);
+/* Steps until no work is pending (max_steps <= 0) or max_steps steps ran;
+ * NVLLM_ERR_INVALID when the queue head can never be admitted. */
+int nvllm_generator_run(nvllm_generator* g, int64_t max_steps, int64_t* steps_done);
+int nvllm_generator_has_pending_work(const nvllm_generator* g);
+/* Token list (prompt + generated) of finished sequence seq_id: returns its
+ * length (writing it when it fits in cap), or -1 if it has not finished. */
+int64_t nvllm_generator_output(const nvllm_generator* g, uint64_t seq_id, int64_t* tokens,
+                               int64_t cap);
+/* Records every following step to path (trace record + -2, sampled ids, per
+ * sequence the top-2 margin and 8 largest logits as float bits); NULL or ""
+ * stops recording. */
+int nvllm_generator_trace(nvllm_generator* g, const char* path);
+int nvllm_generator_metrics(const nvllm_generator* g, nvllm_metrics* out);
+/* MetricsSnapshot::to_json layout (src/engine.cpp:8-38); returns the length
+ * (without the terminator), writing it when it fits in cap. */
+int64_t nvllm_metrics_to_json(const nvllm_metrics* m, char* buf, int64_t cap);
 
 /* ---- cross-process device buffers (head split) ---------------------------
  * nvllm_ipc_alloc: cudaMalloc of `bytes` on the current device, zero-filled,

@@ -41,7 +41,7 @@ struct EngineConfig {
 };
 
 struct EngineError {
-    enum class Kind { Invalid, Cuda, Pack, Kernel, NoStep, Blas } kind;
+    enum class Kind { Invalid, Cuda, Pack, Kernel, NoStep, Blas, Unsupported } kind;
     int code = 0;  // cudaError_t, PackError, nvllm status or cublasStatus_t, by kind
 };
 

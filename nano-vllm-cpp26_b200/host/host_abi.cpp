@@ -1,4 +1,5 @@
 // extern "C" wrappers of the host library (declared in include/nvllm_host.h).
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <new>
@@ -8,7 +9,9 @@
 #include "block_allocator.hpp"
 #include "engine.hpp"
 #include "metadata.hpp"
+#include "generator.hpp"
 #include "model.hpp"
+#include "scheduler.hpp"
 
 struct nvllm_block_allocator {
     nvllm::BlockAllocator impl;
@@ -23,6 +26,14 @@ struct nvllm_model {
     std::unique_ptr<nvllm::DeviceModel> impl;
 };
 
+struct nvllm_scheduler {
+    nvllm::Scheduler impl;
+};
+
+struct nvllm_generator {
+    std::unique_ptr<nvllm::Generator> impl;
+};
+
 namespace {
 
 int kv_status(nvllm::KVError e) {
@@ -34,6 +45,7 @@ int engine_status(const nvllm::EngineError& e) {
     switch (e.kind) {
         case nvllm::EngineError::Kind::Cuda: return NVLLM_ERR_CUDA;
         case nvllm::EngineError::Kind::Blas: return NVLLM_ERR_CUDA;
+        case nvllm::EngineError::Kind::Unsupported: return NVLLM_ERR_UNSUPPORTED;
         case nvllm::EngineError::Kind::Pack: return NVLLM_HOST_PACK_ERROR;
         case nvllm::EngineError::Kind::Kernel: return e.code;
         default: return NVLLM_ERR_INVALID;
@@ -85,6 +97,36 @@ bool make_views(int32_t num_seqs, const int32_t* num_computed, const int32_t* to
         views[s] = nvllm::SequenceView{num_computed[s], total_len[s],
                                        std::span<const nvllm::BlockId>(storage.data() + off, len)};
         off += len;
+    }
+    return true;
+}
+
+bool scheduler_config(const nvllm_scheduler_config* c, nvllm::SchedulerConfig& out) {
+    if (c == nullptr || c->max_batch_size < 0 || c->max_tokens_per_step < 0 ||
+        c->watermark_blocks < 0) {
+        return false;
+    }
+    out.max_batch_size = std::size_t(c->max_batch_size);
+    out.max_tokens_per_step = std::size_t(c->max_tokens_per_step);
+    out.watermark_blocks = std::size_t(c->watermark_blocks);
+    if (c->eos_token_id >= 0) out.eos_token_id = c->eos_token_id;
+    return true;
+}
+
+void fill_summary(const nvllm::StepSummary& s, nvllm_step_summary* out) {
+    if (out == nullptr) return;
+    out->admitted = int64_t(s.admitted);
+    out->preempted = int64_t(s.preempted);
+    out->retired = int64_t(s.retired);
+    out->batch_size = int64_t(s.batch_size);
+    out->scheduled_tokens = int64_t(s.scheduled_tokens);
+}
+
+bool make_prompt(const int64_t* prompt, int64_t len, std::vector<int64_t>& out) {
+    if (len < 0 || (len > 0 && prompt == nullptr)) return false;
+    out.assign(prompt, prompt + len);
+    for (const int64_t t : out) {
+        if (t < 0) return false;
     }
     return true;
 }
@@ -234,7 +276,8 @@ int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvll
     if (cfg == nullptr || engine == nullptr || out == nullptr) return NVLLM_ERR_INVALID;
     nvllm::ModelConfig mc{.vocab = cfg->vocab, .hidden = cfg->hidden, .layers = cfg->layers,
                           .heads = cfg->heads, .head_dim = cfg->head_dim, .ffn = cfg->ffn,
-                          .emb_scale = cfg->emb_scale, .ffn_scale = cfg->ffn_scale};
+                          .emb_scale = cfg->emb_scale, .ffn_scale = cfg->ffn_scale,
+                          .gemm_math = cfg->gemm_math};
     auto r = nvllm::DeviceModel::create(mc, *engine->impl);
     if (!r) return engine_status(r.error());
     auto* m = new (std::nothrow) nvllm_model{std::move(*r)};
@@ -266,6 +309,155 @@ int nvllm_model_weights(const nvllm_model* m, const float** weights, int64_t* co
     *weights = m->impl->weights();
     *count = int64_t(m->impl->weight_floats());
     return NVLLM_OK;
+}
+
+nvllm_scheduler* nvllm_scheduler_create(const nvllm_scheduler_config* cfg, int32_t block_size) {
+    nvllm::SchedulerConfig sc;
+    if (!scheduler_config(cfg, sc) || block_size <= 0) return nullptr;
+    return new (std::nothrow) nvllm_scheduler{nvllm::Scheduler(sc, std::size_t(block_size))};
+}
+
+void nvllm_scheduler_destroy(nvllm_scheduler* s) { delete s; }
+
+int nvllm_scheduler_add_request(nvllm_scheduler* s, uint64_t seq_id, const int64_t* prompt,
+                                int64_t prompt_len, int64_t max_new_tokens) {
+    std::vector<int64_t> p;
+    if (s == nullptr || !make_prompt(prompt, prompt_len, p)) return NVLLM_ERR_INVALID;
+    s->impl.add_request(
+        nvllm::Sequence(seq_id, std::move(p), std::size_t(std::max<int64_t>(max_new_tokens, 1))));
+    return NVLLM_OK;
+}
+
+int nvllm_scheduler_schedule_step(nvllm_scheduler* s, nvllm_block_allocator* blocks,
+                                  nvllm_step_summary* out) {
+    if (s == nullptr || blocks == nullptr) return NVLLM_ERR_INVALID;
+    fill_summary(s->impl.schedule_step(blocks->impl), out);
+    return NVLLM_OK;
+}
+
+int64_t nvllm_scheduler_batch_record(const nvllm_scheduler* s, int64_t step, int64_t* out,
+                                     int64_t cap) {
+    if (s == nullptr) return -1;
+    std::vector<int64_t> rec;
+    nvllm::append_batch_record(s->impl, step, rec);
+    if (out != nullptr && int64_t(rec.size()) <= cap) std::memcpy(out, rec.data(), rec.size() * 8);
+    return int64_t(rec.size());
+}
+
+int nvllm_scheduler_process_outputs(nvllm_scheduler* s, nvllm_block_allocator* blocks,
+                                    const int64_t* sampled, int64_t n, int64_t* retired) {
+    if (s == nullptr || blocks == nullptr || n < 0 || (n > 0 && sampled == nullptr) ||
+        std::size_t(n) != s->impl.running().size()) {
+        return NVLLM_ERR_INVALID;
+    }
+    const std::size_t r = s->impl.process_step_outputs(
+        std::span<const int64_t>(sampled, std::size_t(n)), blocks->impl);
+    if (retired != nullptr) *retired = int64_t(r);
+    return NVLLM_OK;
+}
+
+int nvllm_scheduler_counts(const nvllm_scheduler* s, int64_t* running, int64_t* waiting,
+                           int64_t* preemptions, int64_t* completed) {
+    if (s == nullptr) return NVLLM_ERR_INVALID;
+    if (running) *running = int64_t(s->impl.running().size());
+    if (waiting) *waiting = int64_t(s->impl.waiting().size());
+    if (preemptions) *preemptions = int64_t(s->impl.total_preemptions());
+    if (completed) *completed = int64_t(s->impl.total_completed());
+    return NVLLM_OK;
+}
+
+int nvllm_generator_create(nvllm_engine* engine, nvllm_model* model,
+                           const nvllm_scheduler_config* cfg, int32_t precision,
+                           nvllm_generator** out) {
+    nvllm::SchedulerConfig sc;
+    if (engine == nullptr || model == nullptr || out == nullptr || !scheduler_config(cfg, sc)) {
+        return NVLLM_ERR_INVALID;
+    }
+    auto g = std::make_unique<nvllm::Generator>(*engine->impl, *model->impl, sc, precision);
+    auto* h = new (std::nothrow) nvllm_generator{std::move(g)};
+    if (h == nullptr) return NVLLM_ERR_INVALID;
+    *out = h;
+    return NVLLM_OK;
+}
+
+void nvllm_generator_destroy(nvllm_generator* g) { delete g; }
+
+int nvllm_generator_add_request(nvllm_generator* g, uint64_t seq_id, const int64_t* prompt,
+                                int64_t prompt_len, int64_t max_new_tokens) {
+    std::vector<int64_t> p;
+    if (g == nullptr || !make_prompt(prompt, prompt_len, p)) return NVLLM_ERR_INVALID;
+    g->impl->add_request(seq_id, std::move(p),
+                         std::size_t(std::max<int64_t>(max_new_tokens, 1)));
+    return NVLLM_OK;
+}
+
+int nvllm_generator_step(nvllm_generator* g, nvllm_step_summary* out) {
+    if (g == nullptr) return NVLLM_ERR_INVALID;
+    auto r = g->impl->step();
+    if (!r) return engine_status(r.error());
+    fill_summary(*r, out);
+    return NVLLM_OK;
+}
+
+int nvllm_generator_run(nvllm_generator* g, int64_t max_steps, int64_t* steps_done) {
+    if (g == nullptr) return NVLLM_ERR_INVALID;
+    auto r = g->impl->run(max_steps);
+    if (!r) return engine_status(r.error());
+    if (steps_done != nullptr) *steps_done = *r;
+    return NVLLM_OK;
+}
+
+int nvllm_generator_has_pending_work(const nvllm_generator* g) {
+    return g != nullptr && g->impl->has_pending_work() ? 1 : 0;
+}
+
+int64_t nvllm_generator_output(const nvllm_generator* g, uint64_t seq_id, int64_t* tokens,
+                               int64_t cap) {
+    if (g == nullptr) return -1;
+    const auto* t = g->impl->output(seq_id);
+    if (t == nullptr) return -1;
+    if (tokens != nullptr && int64_t(t->size()) <= cap) {
+        std::memcpy(tokens, t->data(), t->size() * sizeof(int64_t));
+    }
+    return int64_t(t->size());
+}
+
+int nvllm_generator_trace(nvllm_generator* g, const char* path) {
+    if (g == nullptr) return NVLLM_ERR_INVALID;
+    return g->impl->set_trace(path ? std::string(path) : std::string()) ? NVLLM_OK
+                                                                         : NVLLM_ERR_INVALID;
+}
+
+int nvllm_generator_metrics(const nvllm_generator* g, nvllm_metrics* out) {
+    if (g == nullptr || out == nullptr) return NVLLM_ERR_INVALID;
+    const nvllm::Metrics m = g->impl->metrics();
+    *out = nvllm_metrics{m.uptime_secs, m.total_requests_received, m.total_requests_completed,
+                         m.total_tokens_generated, m.throughput_tokens_per_sec,
+                         m.active_batch_size, m.waiting_queue_depth, m.kv_cache_used_blocks,
+                         m.kv_cache_total_blocks, m.kv_cache_utilization_pct, m.avg_ttft_ms,
+                         m.avg_iteration_latency_ms, m.total_preemptions, m.total_iterations};
+    return NVLLM_OK;
+}
+
+int64_t nvllm_metrics_to_json(const nvllm_metrics* m, char* buf, int64_t cap) {
+    if (m == nullptr) return -1;
+    nvllm::Metrics x;
+    x.uptime_secs = m->uptime_secs;
+    x.total_requests_received = m->total_requests_received;
+    x.total_requests_completed = m->total_requests_completed;
+    x.total_tokens_generated = m->total_tokens_generated;
+    x.throughput_tokens_per_sec = m->throughput_tokens_per_sec;
+    x.active_batch_size = m->active_batch_size;
+    x.waiting_queue_depth = m->waiting_queue_depth;
+    x.kv_cache_used_blocks = m->kv_cache_used_blocks;
+    x.kv_cache_total_blocks = m->kv_cache_total_blocks;
+    x.kv_cache_utilization_pct = m->kv_cache_utilization_pct;
+    x.avg_ttft_ms = m->avg_ttft_ms;
+    x.avg_iteration_latency_ms = m->avg_iteration_latency_ms;
+    x.total_preemptions = m->total_preemptions;
+    const std::string js = x.to_json();
+    if (buf != nullptr && int64_t(js.size()) < cap) std::memcpy(buf, js.c_str(), js.size() + 1);
+    return int64_t(js.size());
 }
 
 int nvllm_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {

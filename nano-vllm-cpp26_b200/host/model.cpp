@@ -1,5 +1,7 @@
 #include "model.hpp"
 
+#include <dlfcn.h>
+
 #include <climits>
 #include <cmath>
 
@@ -53,7 +55,8 @@ std::expected<std::unique_ptr<DeviceModel>, EngineError> DeviceModel::create(
         cfg.heads <= 0 || cfg.head_dim <= 0 || cfg.ffn <= 0 ||
         cfg.hidden != cfg.heads * cfg.head_dim || cfg.hidden > INT32_MAX ||
         cfg.ffn > INT32_MAX || L.num_layers != cfg.layers || L.num_heads != cfg.heads ||
-        L.head_dim != cfg.head_dim || cfg.emb_scale < 0.0f || cfg.ffn_scale < 0.0f) {
+        L.head_dim != cfg.head_dim || cfg.emb_scale < 0.0f || cfg.ffn_scale < 0.0f ||
+        cfg.gemm_math < 0 || cfg.gemm_math > 1) {
         return invalid();
     }
     std::unique_ptr<DeviceModel> m(new DeviceModel(cfg, eng));
@@ -68,8 +71,23 @@ std::expected<void, EngineError> DeviceModel::init() {
     NVLLM_CUDA_TRY(cudaSetDevice(eng_.config().device));
     NVLLM_BLAS_TRY(cublasCreate(&blas_));
     NVLLM_BLAS_TRY(cublasSetStream(blas_, st));
-    // plain fp32 arithmetic: no TF32 down-conversion inside cuBLAS
-    NVLLM_BLAS_TRY(cublasSetMathMode(blas_, CUBLAS_DEFAULT_MATH));
+    // fp32 arithmetic: FFMA, or the bf16x9 emulation of fp32 on the tensor
+    // cores; never a TF32 down-conversion
+    if (cfg_.gemm_math == 1) {
+        // the bf16x9 mode needs the cuBLAS of CUDA 12.9 or later in the process
+        if (cublasSetMathMode(blas_, CUBLAS_FP32_EMULATED_BF16X9_MATH) != CUBLAS_STATUS_SUCCESS) {
+            return std::unexpected(EngineError{EngineError::Kind::Unsupported, 0});
+        }
+        // Prefer the emulation for every shape where the loaded cuBLAS lets us
+        // choose (the setter is absent from some 12.9 builds, which then pick
+        // per shape by their own heuristics).
+        using SetStrategy = cublasStatus_t (*)(cublasHandle_t, cublasEmulationStrategy_t);
+        if (auto fn = reinterpret_cast<SetStrategy>(dlsym(RTLD_DEFAULT, "cublasSetEmulationStrategy"))) {
+            NVLLM_BLAS_TRY(fn(blas_, CUBLAS_EMULATION_STRATEGY_EAGER));
+        }
+    } else {
+        NVLLM_BLAS_TRY(cublasSetMathMode(blas_, CUBLAS_DEFAULT_MATH));
+    }
 
     // weights, in the reference constructor's draw order
     layer_floats_ = std::size_t(4 * D * D + 2 * D * F);

@@ -13,7 +13,10 @@
 // adjacent), KV write + paged attention (the engine), W_o GEMM accumulating
 // into the residual, RMSNorm, up GEMM, SiLU, down GEMM accumulating into the
 // residual; then the last-token gather, the LM-head GEMM and the penalised
-// argmax. The projections are fp32 cuBLAS SGEMMs (no TF32).
+// argmax. The projections are cuBLAS SGEMMs on fp32 data: FFMA on the CUDA
+// cores, or (gemm_math 1) cuBLAS's bf16x9 emulation of fp32 on the tensor
+// cores (each fp32 operand split into three bf16 terms, fp32 accumulation);
+// never TF32.
 #pragma once
 
 #include <cublas_v2.h>
@@ -33,6 +36,8 @@ struct ModelConfig {
     int64_t vocab = 0, hidden = 0, layers = 0, heads = 0, head_dim = 0, ffn = 0;
     // weight scales of src/model.cpp:81-82; 0 = 1/sqrt(hidden), 1/sqrt(ffn)
     float emb_scale = 0.0f, ffn_scale = 0.0f;
+    // 0: fp32 FFMA; 1: fp32 emulated with bf16x9 on the tensor cores
+    int32_t gemm_math = 0;
 };
 
 class DeviceModel {

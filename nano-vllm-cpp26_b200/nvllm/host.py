@@ -36,10 +36,42 @@ class EngineConfig(ctypes.Structure):
                 ("device", ctypes.c_int32)]
 
 
+class SchedulerConfig(ctypes.Structure):
+    _fields_ = [("max_batch_size", ctypes.c_int64), ("max_tokens_per_step", ctypes.c_int64),
+                ("watermark_blocks", ctypes.c_int64), ("eos_token_id", ctypes.c_int64)]
+
+
+class StepSummary(ctypes.Structure):
+    _fields_ = [("admitted", ctypes.c_int64), ("preempted", ctypes.c_int64),
+                ("retired", ctypes.c_int64), ("batch_size", ctypes.c_int64),
+                ("scheduled_tokens", ctypes.c_int64)]
+
+
+class Metrics(ctypes.Structure):
+    _fields_ = [("uptime_secs", ctypes.c_double), ("total_requests_received", ctypes.c_uint64),
+                ("total_requests_completed", ctypes.c_uint64),
+                ("total_tokens_generated", ctypes.c_uint64),
+                ("throughput_tokens_per_sec", ctypes.c_double),
+                ("active_batch_size", ctypes.c_uint64), ("waiting_queue_depth", ctypes.c_uint64),
+                ("kv_cache_used_blocks", ctypes.c_uint64),
+                ("kv_cache_total_blocks", ctypes.c_uint64),
+                ("kv_cache_utilization_pct", ctypes.c_double), ("avg_ttft_ms", ctypes.c_double),
+                ("avg_iteration_latency_ms", ctypes.c_double),
+                ("total_preemptions", ctypes.c_uint64), ("total_iterations", ctypes.c_uint64)]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
 class ModelConfig(ctypes.Structure):
     _fields_ = [("vocab", ctypes.c_int64), ("hidden", ctypes.c_int64), ("layers", ctypes.c_int64),
                 ("heads", ctypes.c_int64), ("head_dim", ctypes.c_int64), ("ffn", ctypes.c_int64),
-                ("emb_scale", ctypes.c_float), ("ffn_scale", ctypes.c_float)]
+                ("emb_scale", ctypes.c_float), ("ffn_scale", ctypes.c_float),
+                ("gemm_math", ctypes.c_int32)]
+
+
+GEMM_FP32 = 0
+GEMM_BF16X9 = 1
 
 
 _HOST: ctypes.CDLL | None = None
@@ -86,6 +118,30 @@ def host_lib() -> ctypes.CDLL:
     L.nvllm_model_forward.argtypes = [_vp, _i64p, ctypes.c_int64, _i64p, ctypes.c_int64, _i64p,
                                       ctypes.c_int32, _f32p, _i32p, _f32p, ctypes.c_int32]
     L.nvllm_model_weights.argtypes = [_vp, ctypes.POINTER(_f32p), _i64p]
+    L.nvllm_scheduler_create.restype = _vp
+    L.nvllm_scheduler_create.argtypes = [ctypes.POINTER(SchedulerConfig), ctypes.c_int32]
+    L.nvllm_scheduler_destroy.argtypes = [_vp]
+    L.nvllm_scheduler_add_request.argtypes = [_vp, ctypes.c_uint64, _i64p, ctypes.c_int64,
+                                              ctypes.c_int64]
+    L.nvllm_scheduler_schedule_step.argtypes = [_vp, _vp, ctypes.POINTER(StepSummary)]
+    L.nvllm_scheduler_batch_record.restype = ctypes.c_int64
+    L.nvllm_scheduler_batch_record.argtypes = [_vp, ctypes.c_int64, _i64p, ctypes.c_int64]
+    L.nvllm_scheduler_process_outputs.argtypes = [_vp, _vp, _i64p, ctypes.c_int64, _i64p]
+    L.nvllm_scheduler_counts.argtypes = [_vp, _i64p, _i64p, _i64p, _i64p]
+    L.nvllm_generator_create.argtypes = [_vp, _vp, ctypes.POINTER(SchedulerConfig),
+                                         ctypes.c_int32, ctypes.POINTER(_vp)]
+    L.nvllm_generator_destroy.argtypes = [_vp]
+    L.nvllm_generator_add_request.argtypes = [_vp, ctypes.c_uint64, _i64p, ctypes.c_int64,
+                                              ctypes.c_int64]
+    L.nvllm_generator_step.argtypes = [_vp, ctypes.POINTER(StepSummary)]
+    L.nvllm_generator_run.argtypes = [_vp, ctypes.c_int64, _i64p]
+    L.nvllm_generator_has_pending_work.argtypes = [_vp]
+    L.nvllm_generator_output.restype = ctypes.c_int64
+    L.nvllm_generator_output.argtypes = [_vp, ctypes.c_uint64, _i64p, ctypes.c_int64]
+    L.nvllm_generator_trace.argtypes = [_vp, ctypes.c_char_p]
+    L.nvllm_generator_metrics.argtypes = [_vp, ctypes.POINTER(Metrics)]
+    L.nvllm_metrics_to_json.restype = ctypes.c_int64
+    L.nvllm_metrics_to_json.argtypes = [ctypes.POINTER(Metrics), ctypes.c_char_p, ctypes.c_int64]
     _HOST = L
     return L
 
@@ -248,15 +304,16 @@ class Model:
     """The reference TransformerModel on the engine's GPU (nvllm_model_*):
     LCG weights generated on the device, forward_batch as device kernels.
     ``cfg`` holds vocab, hidden, layers, heads, head_dim, ffn; ``scales`` the
-    optional [emb_scale, ffn_scale] of the weights."""
+    optional [emb_scale, ffn_scale] of the weights; ``gemm_math`` GEMM_FP32
+    (FFMA) or GEMM_BF16X9 (fp32 emulated on the tensor cores)."""
 
-    def __init__(self, cfg: dict, engine: Engine, scales=None):
+    def __init__(self, cfg: dict, engine: Engine, scales=None, gemm_math: int = GEMM_FP32):
         self.L = host_lib()
         self.engine = engine  # the model uses the engine's arenas and stream
         self.cfg = dict(cfg)
         es, fs = (0.0, 0.0) if scales is None else (float(scales[0]), float(scales[1]))
         mc = ModelConfig(cfg["vocab"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["head_dim"],
-                         cfg["ffn"], es, fs)
+                         cfg["ffn"], es, fs, gemm_math)
         h = _vp()
         rc = self.L.nvllm_model_create(ctypes.byref(mc), engine.h, ctypes.byref(h))
         if rc != OK:
@@ -297,3 +354,138 @@ class Model:
         if rc != OK:
             raise NvllmError(rc, "nvllm_model_weights")
         return ctypes.cast(p, _vp).value, n.value
+
+
+def _sched_config(max_batch_size: int, max_tokens_per_step: int, watermark_blocks: int,
+                  eos_token_id: int | None) -> SchedulerConfig:
+    return SchedulerConfig(max_batch_size, max_tokens_per_step, watermark_blocks,
+                           -1 if eos_token_id is None else eos_token_id)
+
+
+class Scheduler:
+    """The continuous-batching scheduler alone (nvllm_scheduler_*), drawing
+    blocks from a :class:`BlockAllocator`."""
+
+    def __init__(self, block_size: int, max_batch_size: int = 32, max_tokens_per_step: int = 512,
+                 watermark_blocks: int = 4, eos_token_id: int | None = None):
+        self.L = host_lib()
+        cfg = _sched_config(max_batch_size, max_tokens_per_step, watermark_blocks, eos_token_id)
+        self.h = self.L.nvllm_scheduler_create(ctypes.byref(cfg), block_size)
+        if not self.h:
+            raise NvllmError(1, "nvllm_scheduler_create")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.nvllm_scheduler_destroy(self.h)
+            self.h = None
+
+    def add_request(self, seq_id: int, prompt, max_new_tokens: int) -> None:
+        p = np.ascontiguousarray(prompt, np.int64)
+        rc = self.L.nvllm_scheduler_add_request(self.h, seq_id, _ptr(p, _i64p), len(p),
+                                                max_new_tokens)
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_scheduler_add_request")
+
+    def schedule_step(self, blocks: BlockAllocator) -> dict:
+        out = StepSummary()
+        rc = self.L.nvllm_scheduler_schedule_step(self.h, blocks.h, ctypes.byref(out))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_scheduler_schedule_step")
+        return {name: getattr(out, name) for name, _ in StepSummary._fields_}
+
+    def batch_record(self, step: int) -> np.ndarray:
+        n = self.L.nvllm_scheduler_batch_record(self.h, step, None, 0)
+        out = np.zeros(n, np.int64)
+        self.L.nvllm_scheduler_batch_record(self.h, step, _ptr(out, _i64p), n)
+        return out
+
+    def process_outputs(self, blocks: BlockAllocator, sampled) -> int:
+        smp = np.ascontiguousarray(sampled, np.int64)
+        retired = ctypes.c_int64()
+        rc = self.L.nvllm_scheduler_process_outputs(self.h, blocks.h, _ptr(smp, _i64p), len(smp),
+                                                    ctypes.byref(retired))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_scheduler_process_outputs")
+        return retired.value
+
+    def counts(self) -> dict:
+        v = [ctypes.c_int64() for _ in range(4)]
+        self.L.nvllm_scheduler_counts(self.h, *[ctypes.byref(x) for x in v])
+        return dict(zip(("running", "waiting", "preemptions", "completed"), (x.value for x in v)))
+
+
+def metrics_json(m: Metrics) -> str:
+    n = host_lib().nvllm_metrics_to_json(ctypes.byref(m), None, 0)
+    buf = ctypes.create_string_buffer(n + 1)
+    host_lib().nvllm_metrics_to_json(ctypes.byref(m), buf, n + 1)
+    return buf.value.decode()
+
+
+class Generator:
+    """The engine loop on one GPU (nvllm_generator_*): scheduler + engine +
+    device model."""
+
+    def __init__(self, engine: Engine, model: Model, max_batch_size: int = 32,
+                 max_tokens_per_step: int = 512, watermark_blocks: int = 4,
+                 eos_token_id: int | None = None, precision: int = 0):
+        self.L = host_lib()
+        self.engine, self.model = engine, model
+        cfg = _sched_config(max_batch_size, max_tokens_per_step, watermark_blocks, eos_token_id)
+        h = _vp()
+        rc = self.L.nvllm_generator_create(engine.h, model.h, ctypes.byref(cfg), precision,
+                                           ctypes.byref(h))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_generator_create")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.nvllm_generator_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def add_request(self, seq_id: int, prompt, max_new_tokens: int) -> None:
+        p = np.ascontiguousarray(prompt, np.int64)
+        rc = self.L.nvllm_generator_add_request(self.h, seq_id, _ptr(p, _i64p), len(p),
+                                                max_new_tokens)
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_generator_add_request")
+
+    def step(self) -> dict:
+        out = StepSummary()
+        rc = self.L.nvllm_generator_step(self.h, ctypes.byref(out))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_generator_step")
+        return {name: getattr(out, name) for name, _ in StepSummary._fields_}
+
+    def run(self, max_steps: int = 0) -> int:
+        done = ctypes.c_int64()
+        rc = self.L.nvllm_generator_run(self.h, max_steps, ctypes.byref(done))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_generator_run")
+        return done.value
+
+    def has_pending_work(self) -> bool:
+        return bool(self.L.nvllm_generator_has_pending_work(self.h))
+
+    def output(self, seq_id: int):
+        n = self.L.nvllm_generator_output(self.h, seq_id, None, 0)
+        if n < 0:
+            return None
+        out = np.zeros(n, np.int64)
+        self.L.nvllm_generator_output(self.h, seq_id, _ptr(out, _i64p), n)
+        return out
+
+    def trace(self, path: str | None) -> None:
+        rc = self.L.nvllm_generator_trace(self.h, (path or "").encode())
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_generator_trace")
+
+    def metrics(self) -> Metrics:
+        m = Metrics()
+        rc = self.L.nvllm_generator_metrics(self.h, ctypes.byref(m))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_generator_metrics")
+        return m

@@ -300,7 +300,8 @@ class RefPath:
 def read_trace(path_or_array) -> list[dict]:
     """Parses a ref_generate trace (file path or its integer array): one dict
     per step with the running sequences (seq_id, num_computed, total_len,
-    prev_token, table, uncomputed) and the sampled tokens."""
+    prev_token, table, uncomputed), the sampled tokens, the margins and top-8
+    logits, and ``record``, the step's raw batch record (header and sequences)."""
     if isinstance(path_or_array, np.ndarray):
         a = path_or_array.astype(np.int64)
     else:
@@ -308,6 +309,7 @@ def read_trace(path_or_array) -> list[dict]:
     i = 0
     steps = []
     while i < len(a):
+        start = i
         assert a[i] == -1
         n = int(a[i + 2])
         i += 3
@@ -323,6 +325,7 @@ def read_trace(path_or_array) -> list[dict]:
             seqs.append(dict(seq_id=sid, num_computed=nc, total_len=tl, prev_token=prev,
                              table=table, uncomputed=unc))
         assert a[i] == -2
+        record = a[start:i].copy()
         sampled = a[i + 1:i + 1 + n].copy()
         i += 1 + n
         margins = np.zeros(n, np.float32)
@@ -335,5 +338,5 @@ def read_trace(path_or_array) -> list[dict]:
             top_val[j] = pairs[:, 1].astype(np.uint32).view(np.float32)
             i += 17
         steps.append(dict(seqs=seqs, sampled=sampled, margin=margins, top_idx=top_idx,
-                          top_val=top_val))
+                          top_val=top_val, record=record))
     return steps

@@ -23,7 +23,10 @@ sequences (computed / total lengths, block tables, uncomputed token ids, the
 previous token), the tokens the reference sampled for them, the top-2 margin
 of the penalised logits and the 8 largest logits of each sampled row, plus the
 reference build's weight and softmax scales (``scales``: 1/sqrt of hidden, ffn
-and head_dim as its -ffast-math code evaluates them).
+and head_dim as its -ffast-math code evaluates them), the requests
+(``prompt_lens``, ``prompt_tokens``, ``max_new``; sequence i + 1 is request i)
+and the scheduler settings (``sched``: max_batch, max_tokens_per_step,
+watermark_blocks).
 """
 from __future__ import annotations
 
@@ -177,7 +180,12 @@ def token_trace(ref: RefPath, spec: dict) -> dict:
     return dict(trace=raw, model=np.array([model[k] for k in
                 ("vocab", "hidden", "layers", "heads", "head_dim", "ffn")], np.int64),
                 num_blocks=np.int64(spec["num_blocks"]), block_size=np.int64(spec["block_size"]),
-                scales=ref.model_scales(model))
+                scales=ref.model_scales(model),
+                sched=np.array([spec["max_batch"], spec["max_tokens_per_step"],
+                                spec["watermark"]], np.int64),
+                prompt_lens=np.array([len(p) for p in prompts], np.int64),
+                prompt_tokens=np.concatenate([np.asarray(p, np.int64) for p in prompts]),
+                max_new=np.asarray(max_new, np.int64))
 
 
 def main() -> None:

@@ -31,6 +31,13 @@ def load_trace(name: str):
     return cfg, z, read_trace(z["trace"])
 
 
+def trace_requests(z):
+    """(prompts, max_new) of a token trace; sequence i + 1 is request i."""
+    lens, toks = z["prompt_lens"], z["prompt_tokens"]
+    offs = np.concatenate([[0], np.cumsum(lens)])
+    return [toks[offs[i]:offs[i + 1]] for i in range(len(lens))], [int(x) for x in z["max_new"]]
+
+
 def load_golden(name: str) -> dict:
     with np.load(GOLDEN / f"{name}.npz") as z:
         return {k: z[k] for k in z.files}

@@ -1,0 +1,94 @@
+"""The generator (scheduler + engine + device model, nvllm_generator_*) end to
+end on the GPU against the reference's continuous-batching run: given the same
+requests it must write the reference's trace — every step's batch (sequences,
+lengths, block tables, uncomputed tokens) and every sampled token identical,
+the top-2 margins and top-8 logits within LOGIT_RTOL — and finish every request
+with the reference's token stream."""
+import json
+
+import numpy as np
+import pytest
+
+from helpers import LOGIT_RTOL, load_trace, trace_requests
+
+pytestmark = pytest.mark.gpu
+
+
+def build(name, precision=0):
+    import nvllm
+    from nvllm.host import Engine, Generator, Model
+    cfg, z, steps = load_trace(name)
+    max_batch, max_tokens, watermark = (int(x) for x in z["sched"])
+    lay = nvllm.KVLayout(int(z["num_blocks"]), cfg["layers"], int(z["block_size"]), cfg["heads"],
+                         cfg["head_dim"])
+    prompts, max_new = trace_requests(z)
+    longest = max(len(p) + m for p, m in zip(prompts, max_new))
+    B = int(z["block_size"])
+    eng = Engine(lay, max_seqs=max_batch, max_tokens=max(max_tokens, longest),
+                 max_blocks_per_seq=(longest + B - 1) // B)
+    model = Model(cfg, eng, scales=z["scales"][:2])
+    gen = Generator(eng, model, max_batch, max_tokens, watermark, precision=precision)
+    for i, (p, m) in enumerate(zip(prompts, max_new)):
+        gen.add_request(i + 1, p, m)
+    return cfg, z, steps, (eng, model, gen), prompts
+
+
+@pytest.mark.parametrize("name", ["tokens_toy_seeded", "tokens_toy_bench", "tokens_wide"])
+def test_generator_reproduces_reference_run(name, tmp_path):
+    from nvllm.host import metrics_json
+    from oracle.oracle import read_trace
+    cfg, z, steps, objs, prompts = build(name)
+    eng, model, gen = objs
+    try:
+        path = str(tmp_path / "run.trace")
+        gen.trace(path)
+        n_steps = gen.run()
+        gen.trace(None)
+        assert n_steps == len(steps)
+        mine = read_trace(path)
+        assert len(mine) == len(steps)
+        streams = {i + 1: list(p) for i, p in enumerate(prompts)}
+        for i, (a, b) in enumerate(zip(mine, steps)):
+            assert np.array_equal(a["record"], b["record"]), f"{name} step {i}: batch"
+            assert np.array_equal(a["sampled"], b["sampled"]), f"{name} step {i}: tokens"
+            scale = np.abs(b["top_val"]).max(axis=1, keepdims=True)
+            assert (np.abs(a["top_val"] - b["top_val"]) <= LOGIT_RTOL * scale).all()
+            np.testing.assert_allclose(a["margin"], b["margin"], rtol=0,
+                                       atol=2 * LOGIT_RTOL * float(scale.max()))
+            for s, t in zip(b["seqs"], b["sampled"]):
+                streams[s["seq_id"]].append(int(t))
+        for sid, want in streams.items():
+            got = gen.output(sid)
+            assert got is not None and got.tolist() == want, f"sequence {sid}"
+        m = gen.metrics()
+        assert m.total_requests_received == m.total_requests_completed == len(prompts)
+        assert m.total_tokens_generated == sum(len(st["seqs"]) for st in steps)
+        assert m.total_iterations == len(steps)
+        assert m.active_batch_size == 0 and m.waiting_queue_depth == 0
+        assert m.kv_cache_used_blocks == 0
+        snap = json.loads(metrics_json(m))
+        assert snap["total_requests_completed"] == len(prompts)
+        assert not gen.has_pending_work()
+    finally:
+        gen.close()
+        model.close()
+        eng.close()
+
+
+def test_generator_step_by_step_and_preemption_count():
+    """Stepping by hand gives the same summaries as the reference's batches,
+    and the tight arena of the seeded run preempts."""
+    cfg, z, steps, objs, prompts = build("tokens_toy_seeded")
+    eng, model, gen = objs
+    try:
+        preempted = 0
+        for st in steps:
+            s = gen.step()
+            assert s["batch_size"] == len(st["seqs"])
+            preempted += s["preempted"]
+        assert not gen.has_pending_work()
+        assert preempted > 0 and gen.metrics().total_preemptions == preempted
+    finally:
+        gen.close()
+        model.close()
+        eng.close()

@@ -138,7 +138,7 @@ def _device_copy(torch, ptr: int, count: int) -> np.ndarray:
     return torch.as_tensor(View(), device="cuda").cpu().numpy()
 
 
-def _engine_for(cfg, z, steps, device_model=True):
+def _engine_for(cfg, z, steps, device_model=True, gemm_math=0):
     import nvllm
     from nvllm.host import Engine, Model
     lay = nvllm.KVLayout(int(z["num_blocks"]), cfg["layers"], int(z["block_size"]), cfg["heads"],
@@ -147,7 +147,7 @@ def _engine_for(cfg, z, steps, device_model=True):
     max_tokens = max(sum(len(s["uncomputed"]) for s in st["seqs"]) for st in steps)
     max_blocks = max(len(s["table"]) for st in steps for s in st["seqs"])
     eng = Engine(lay, max_seqs=max_seqs, max_tokens=max_tokens, max_blocks_per_seq=max_blocks)
-    model = Model(cfg, eng, scales=z["scales"][:2]) if device_model else None
+    model = Model(cfg, eng, scales=z["scales"][:2], gemm_math=gemm_math) if device_model else None
     return eng, model
 
 
@@ -169,10 +169,10 @@ def test_device_weights_bit_exact(torch_cuda):
         eng.close()
 
 
-def replay(name: str, precision: int = 0):
+def replay(name: str, precision: int = 0, gemm_math: int = 0):
     import nvllm
     cfg, z, steps = load_trace(name)
-    eng, model = _engine_for(cfg, z, steps)
+    eng, model = _engine_for(cfg, z, steps, gemm_math=gemm_math)
     try:
         for i, st in enumerate(steps):
             seqs = st["seqs"]
@@ -209,3 +209,17 @@ def test_device_model_tf32_attention_wide():
     """The wide model (head_dim 128, block 16) with tcgen05 TF32 prefill tiles:
     the 3xTF32 split keeps the sampled tokens and logits at fp32 quality."""
     assert replay("tokens_wide", precision=1) > 0
+
+
+@pytest.mark.parametrize("name", ["tokens_toy_seeded", "tokens_wide"])
+def test_device_model_bf16x9_gemms(name):
+    """Projections in cuBLAS's bf16x9 emulation of fp32 on the tensor cores:
+    the same tokens and the logits within the same fp32 tolerance."""
+    import nvllm
+    from nvllm.host import GEMM_BF16X9
+    try:
+        assert replay(name, gemm_math=GEMM_BF16X9) > 0
+    except nvllm.NvllmError as e:
+        if e.status != nvllm.ERR_UNSUPPORTED:
+            raise
+        pytest.skip("the cuBLAS loaded in this process has no bf16x9 mode")
