@@ -2,7 +2,7 @@
 """Benchmark of the B200 paged-KV write + paged attention path.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl nvllm|reference]
-                    [--workload decode|mixed|longctx]
+                    [--workload decode|mixed|longctx|serve|serve_toy|serve_toy_seeded]
 
 One step = one pass of the hot path over one batch: nvllm_reshape_and_cache of
 the step's new K/V rows, then nvllm_paged_attention (plan, split-K decode and
@@ -14,6 +14,11 @@ Under torchrun each rank runs its own batch on its own GPU (sequence
 partitioning: no collective on the data path, weak scaling); the timed region
 is bracketed by a barrier and torch.cuda.synchronize(), timed with CUDA events
 on the launching stream, and the maximum over ranks is reported.
+
+The serving workloads (``serve``, ``serve_toy``, ``serve_toy_seeded``) time the
+whole engine loop instead: one step is a complete run of the workload's
+requests through the generator (continuous-batching scheduler + device
+forward_batch + sampling), reported as output tokens/s.
 
 ``--impl reference`` times the reference's own CPU implementation of the path
 (TransformerModel::forward_batch's KV write + paged attention on its
@@ -565,15 +570,229 @@ def headsplit_main(args, spec):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# serving: the reference's engine loop (scheduler + forward_batch) end to end
+
+SERVE_WORKLOADS = ("serve", "serve_toy", "serve_toy_seeded")
+SERVE_METRIC = "e2e serving output tokens/s (continuous batching, greedy)"
+SERVE_DEFAULT_STEPS = {"serve": 3, "serve_toy": 10, "serve_toy_seeded": 10}
+
+
+def model_flops(model: dict, tokens_computed: int, rows_sampled: int) -> float:
+    """Projection FLOPs of forward_batch: 2 * (4 d^2 + 2 d ffn) per layer per
+    flattened token, plus the LM head (2 d vocab) per sampled row."""
+    d, f, v, L = model["hidden"], model["ffn"], model["vocab"], model["layers"]
+    return 2.0 * L * (4 * d * d + 2 * d * f) * tokens_computed + 2.0 * d * v * rows_sampled
+
+
+def reference_serve(spec, budget_s: float = 20.0) -> dict:
+    """The reference's own engine loop (ContinuousScheduler + forward_batch with
+    its real matmuls, oracle/_ref) on the host cores. The toy workloads run
+    whole; for the 4096-wide model the sample is the workload's first requests
+    with completions capped at 8 tokens, as many as fit the time budget."""
+    from oracle.oracle import RefPath
+    ref = RefPath()
+    threads = os.cpu_count() or 1
+    if spec.name != "serve":
+        steps, secs = ref.generate_timed(spec.model, spec.num_blocks, spec.block_size,
+                                         spec.max_batch, spec.max_tokens_per_step, spec.watermark,
+                                         spec.prompts, spec.max_new)
+        return {"tokens": spec.output_tokens, "seconds": secs, "steps": steps, "threads": threads,
+                "sample": f"the whole workload ({len(spec.prompts)} requests, "
+                          f"{spec.output_tokens} output tokens)"}
+    cap = 8
+    n = 1
+    prompts, max_new = spec.prompts[:n], [min(m, cap) for m in spec.max_new[:n]]
+    steps, secs = ref.generate_timed(spec.model, 2 * spec.engine_limits()["max_blocks_per_seq"] + 8,
+                                     spec.block_size, spec.max_batch, spec.max_tokens_per_step, 0,
+                                     prompts, max_new)
+    return {"tokens": int(sum(max_new)), "seconds": secs, "steps": steps, "threads": threads,
+            "sample": f"first {n} request(s) of the workload ({sum(len(p) for p in prompts)} prompt "
+                      f"tokens), completions capped at {cap} tokens; scheduling loop only "
+                      f"(model construction excluded)"}
+
+
+def reference_serve_main(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from nvllm.serving import make_serve, serve_config
+    from oracle.oracle import reference_available
+    spec = make_serve(args.workload, seed=args.seed)
+    if not reference_available():
+        print(json.dumps({"impl": "reference", "metric": SERVE_METRIC,
+                          "unavailable": "oracle/_ref (the reference's C++ built from its sources) "
+                                         "is not present on this machine"}))
+        return 0
+    runs = []
+    for _ in range(args.steps if spec.name != "serve" else 1):
+        runs.append(reference_serve(spec))
+    tok = sum(r["tokens"] for r in runs)
+    secs = sum(r["seconds"] for r in runs)
+    value = tok / secs
+    line = {
+        "impl": "reference", "metric": SERVE_METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": len(runs), "warmup": 0,
+        "ms_per_step": secs / len(runs) * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "config": serve_config(spec),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": runs[0]["threads"],
+                         "kind": "reference", "sample": runs[0]["sample"]},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def serve_main(args):
+    """K complete serving runs of the workload's requests (one run = one step)
+    per GPU: the generator schedules, uploads each iteration's metadata and
+    token ids from pinned host memory, runs forward_batch on the device and
+    reads the sampled ids back, until every request has finished. Under
+    torchrun every rank serves its own requests (sequence partitioning)."""
+    # The host library is loaded before torch so that its cuBLAS references bind
+    # to the CUDA toolkit's cuBLAS it was linked against (which has the bf16x9
+    # mode) rather than to the copy torch brings.
+    from nvllm.host import GEMM_BF16X9, GEMM_FP32, Engine, Generator, Model, host_lib
+    host_lib()
+    import torch
+    import nvllm
+    from nvllm.serving import make_serve, serve_config
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    nvllm.lib()
+    spec = make_serve(args.workload, seed=args.seed + (rank if args.workload == "serve" else 0))
+    lay = nvllm.KVLayout(spec.num_blocks, spec.model["layers"], spec.block_size,
+                         spec.model["heads"], spec.model["head_dim"])
+    eng = Engine(lay, device=local, **spec.engine_limits())
+    gemm = GEMM_BF16X9 if args.gemm == "bf16x9" else GEMM_FP32
+    model = Model(spec.model, eng, gemm_math=gemm)
+    precision = nvllm.PRECISION_TF32 if args.precision == "tf32" else nvllm.PRECISION_FP32
+    estream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+
+    def one_run():
+        gen = Generator(eng, model, spec.max_batch, spec.max_tokens_per_step, spec.watermark,
+                        precision=precision)
+        for i, (p, m) in enumerate(zip(spec.prompts, spec.max_new)):
+            gen.add_request(i + 1, p, m)
+        gen.run()
+        m = gen.metrics()
+        gen.close()
+        return m
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(local).start()
+    for _ in range(args.warmup):
+        one_run()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(estream)
+    ms = [one_run() for _ in range(args.steps)]
+    e1.record(estream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    elapsed = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    clocks = sampler.stop()
+    status = nvllm.get_last_error(eng.stream())
+    if status != nvllm.OK:
+        raise RuntimeError(f"device status {nvllm.status_string(status)}")
+    model.close()
+    eng.close()
+
+    out_tokens = sum(m.total_tokens_generated for m in ms)
+    assert out_tokens == spec.output_tokens * args.steps
+    computed = sum(m.total_tokens_computed for m in ms)
+    iters = sum(m.total_iterations for m in ms)
+    value = out_tokens * world / elapsed
+    flops = model_flops(spec.model, computed, out_tokens)
+    peaks = measured_peaks()
+    peak = peaks.get("bf16_tflops")
+    peak_src = "measured (dense bf16, burst)" if peak else "fallback"
+    if not peak:
+        peak = 1590.0
+    achieved = flops / elapsed / 1e12
+    h2d = sum(m.h2d_bytes for m in ms) // args.steps
+    d2h = sum(m.d2h_bytes for m in ms) // args.steps
+    line = {
+        "metric": SERVE_METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded prompts; LCG weights of the reference model)",
+        "config": {**serve_config(spec), "gemm": args.gemm, "prefill_precision": args.precision,
+                   "parallelism": f"sequence-partitioned x{world}",
+                   "engine_iterations_per_step": iters / args.steps,
+                   "tokens_computed_per_step": computed / args.steps,
+                   "l2": "weights (>= 1.5 MB toy, 3.4 GB wide) and KV stream every iteration; "
+                         "no flush"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peak_src,
+                     "kernel": "whole engine iteration (fp32 projections dominate)",
+                     "algorithmic_flops_per_step": flops / args.steps,
+                     "note": "projection FLOPs over the timed region; the GEMMs run in fp32 "
+                             "(FFMA, or bf16x9 emulation) against the dense bf16 peak",
+                     "traffic": None},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "libnvllm_host generator C ABI (nvllm_generator_add_request + "
+                        "nvllm_generator_run): every engine iteration uploads its metadata and "
+                        "token ids from pinned host memory and reads the sampled ids back, so "
+                        "the timed value is itself end to end"},
+        "gpu_launches": sum(m.kernel_launches for m in ms),
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.oracle import reference_available
+        try:
+            if reference_available():
+                r = reference_serve(spec)
+                line["cpu_baseline"] = {"value": r["tokens"] / r["seconds"], "unit": UNIT,
+                                        "cores": r["threads"], "kind": "reference",
+                                        "sample": r["sample"]}
+            else:
+                line["cpu_baseline"] = None
+        except Exception as exc:  # reported, never fatal
+            line["cpu_baseline"] = {"error": str(exc)}
+    if rank == 0:
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 1000 attention calls; 3 or 10 serving runs)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["nvllm", "reference"], default="nvllm")
     ap.add_argument("--workload", choices=["decode", "mixed", "longctx", "decode_small",
-                                           "mixed_small"],
+                                           "mixed_small", *SERVE_WORKLOADS],
                     default="decode")
+    ap.add_argument("--gemm", choices=["fp32", "bf16x9"], default="fp32",
+                    help="projection arithmetic of the serving workloads")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32",
                     help="prefill tile arithmetic (decode is always fp32)")
@@ -584,6 +803,12 @@ def main() -> int:
     if args.warmup < 3:
         log("warm-up raised to 3 steps")
         args.warmup = 3
+    if args.workload in SERVE_WORKLOADS:
+        if args.steps is None:
+            args.steps = SERVE_DEFAULT_STEPS[args.workload]
+        return reference_serve_main(args) if args.impl == "reference" else serve_main(args)
+    if args.steps is None:
+        args.steps = 1000
     from nvllm.workload import make_batch
     spec = make_batch(args.workload, seed=args.seed)
     if args.impl == "reference":

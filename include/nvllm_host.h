@@ -173,6 +173,9 @@ typedef struct nvllm_metrics {
     uint64_t active_batch_size, waiting_queue_depth, kv_cache_used_blocks, kv_cache_total_blocks;
     double kv_cache_utilization_pct, avg_ttft_ms, avg_iteration_latency_ms;
     uint64_t total_preemptions, total_iterations;
+    /* beyond the reference's snapshot: flattened rows computed, bytes copied
+     * host->device / device->host, launches of this library's kernels */
+    uint64_t total_tokens_computed, h2d_bytes, d2h_bytes, kernel_launches;
 } nvllm_metrics;
 
 int nvllm_generator_create(nvllm_engine* engine, nvllm_model* model,

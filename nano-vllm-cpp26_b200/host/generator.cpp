@@ -59,7 +59,10 @@ Generator::Generator(AttentionEngine& eng, DeviceModel& model, const SchedulerCo
       model_(model),
       sched_(cfg, std::size_t(eng.config().layout.block_size)),
       precision_(precision),
-      start_(Clock::now()) {}
+      start_(Clock::now()),
+      launches0_(model.kernel_launches()),
+      h2d0_(model.h2d_bytes()),
+      d2h0_(model.d2h_bytes()) {}
 
 Generator::~Generator() {
     if (trace_ != nullptr) std::fclose(trace_);
@@ -140,6 +143,7 @@ std::expected<StepSummary, EngineError> Generator::step() {
         ++ttft_samples_;
     }
     tokens_generated_ += n;
+    tokens_computed_ += tokens_.size();
     ++iterations_;
     step_us_ += std::chrono::duration<double, std::micro>(Clock::now() - t0).count();
     return sum;
@@ -185,6 +189,10 @@ Metrics Generator::metrics() const {
     m.avg_iteration_latency_ms = iterations_ > 0 ? step_us_ / double(iterations_) / 1000.0 : 0.0;
     m.total_preemptions = sched_.total_preemptions();
     m.total_iterations = iterations_;
+    m.total_tokens_computed = tokens_computed_;
+    m.h2d_bytes = model_.h2d_bytes() - h2d0_;
+    m.d2h_bytes = model_.d2h_bytes() - d2h0_;
+    m.kernel_launches = model_.kernel_launches() - launches0_;
     return m;
 }
 

@@ -39,6 +39,8 @@ struct Metrics {
     double avg_iteration_latency_ms = 0.0;
     uint64_t total_preemptions = 0;
     uint64_t total_iterations = 0;
+    uint64_t total_tokens_computed = 0;  // flattened rows through the forward pass
+    uint64_t h2d_bytes = 0, d2h_bytes = 0, kernel_launches = 0;
 
     // The reference's MetricsSnapshot::to_json layout (src/engine.cpp:8-38).
     std::string to_json() const;
@@ -90,6 +92,8 @@ private:
     int64_t step_index_ = 0;
     // telemetry
     uint64_t received_ = 0, tokens_generated_ = 0, iterations_ = 0, ttft_samples_ = 0;
+    uint64_t tokens_computed_ = 0;
+    uint64_t launches0_ = 0, h2d0_ = 0, d2h0_ = 0;  // model counters at construction
     double step_us_ = 0.0, ttft_us_ = 0.0;
 };
 

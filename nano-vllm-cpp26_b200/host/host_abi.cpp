@@ -435,7 +435,8 @@ int nvllm_generator_metrics(const nvllm_generator* g, nvllm_metrics* out) {
                          m.total_tokens_generated, m.throughput_tokens_per_sec,
                          m.active_batch_size, m.waiting_queue_depth, m.kv_cache_used_blocks,
                          m.kv_cache_total_blocks, m.kv_cache_utilization_pct, m.avg_ttft_ms,
-                         m.avg_iteration_latency_ms, m.total_preemptions, m.total_iterations};
+                         m.avg_iteration_latency_ms, m.total_preemptions, m.total_iterations,
+                         m.total_tokens_computed, m.h2d_bytes, m.d2h_bytes, m.kernel_launches};
     return NVLLM_OK;
 }
 

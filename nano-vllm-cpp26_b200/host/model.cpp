@@ -219,6 +219,10 @@ std::expected<void, EngineError> DeviceModel::enqueue(std::span<const int64_t> t
     NVLLM_OP_TRY(nvllm_gather_rows(d_last_, d_hidden_, last_idx, S, T, D, st));
     const float* lm = d_w_ + V * D + std::size_t(cfg_.layers) * layer_floats_;
     if (auto r = gemm(d_last_, lm, d_logits_, S, D, V, 0.0f); !r) return r;
+    // embedding, last-token gather, sampler; per layer two RMSNorms, SiLU, the
+    // KV write and the attention's plan, decode and merge (+ prefill)
+    launches_ += 3 + uint64_t(cfg_.layers) * (3 + 4 + (step.max_query_len > 1 ? 1 : 0));
+    h2d_bytes_ += io_in_bytes_ + step.bytes;
     NVLLM_OP_TRY(nvllm_penalized_argmax(d_logits_, d_prev_, S, V, kRepeatPenalty, d_sampled_,
                                         top_k > 0 ? d_margin_ : nullptr,
                                         top_k > 0 ? d_top_idx_ : nullptr,
@@ -239,6 +243,7 @@ std::expected<void, EngineError> DeviceModel::forward(std::span<const int64_t> t
     unsigned char* h_out = h_io_ + io_in_bytes_;
     const std::size_t bytes = top_k > 0 ? io_out_bytes_ : std::size_t(S) * 4;
     NVLLM_CUDA_TRY(cudaMemcpyAsync(h_out, d_io_ + io_in_bytes_, bytes, cudaMemcpyDeviceToHost, st));
+    d2h_bytes_ += bytes;
     NVLLM_CUDA_TRY(cudaStreamSynchronize(st));
     const int32_t status = nvllm_get_last_error(st);
     if (status != NVLLM_OK) return kernel_error(status);

@@ -73,6 +73,13 @@ public:
                                              int32_t precision, int32_t top_k = 0);
     const int32_t* device_sampled() const noexcept { return d_sampled_; }
 
+    // Totals over every forward so far: launches of this library's kernels
+    // (cuBLAS GEMMs not counted) and bytes copied host->device (token ids,
+    // previous tokens, the engine's metadata) and device->host (results).
+    uint64_t kernel_launches() const noexcept { return launches_; }
+    uint64_t h2d_bytes() const noexcept { return h2d_bytes_; }
+    uint64_t d2h_bytes() const noexcept { return d2h_bytes_; }
+
 private:
     DeviceModel(const ModelConfig& cfg, AttentionEngine& eng) : cfg_(cfg), eng_(eng) {}
     std::expected<void, EngineError> init();
@@ -106,6 +113,7 @@ private:
     float* d_top_val_ = nullptr;    // [S, 32]
     cudaEvent_t io_done_ = nullptr;
     int32_t last_rows_ = 0;
+    uint64_t launches_ = 0, h2d_bytes_ = 0, d2h_bytes_ = 0;
 };
 
 }  // namespace nvllm

@@ -57,7 +57,9 @@ class Metrics(ctypes.Structure):
                 ("kv_cache_total_blocks", ctypes.c_uint64),
                 ("kv_cache_utilization_pct", ctypes.c_double), ("avg_ttft_ms", ctypes.c_double),
                 ("avg_iteration_latency_ms", ctypes.c_double),
-                ("total_preemptions", ctypes.c_uint64), ("total_iterations", ctypes.c_uint64)]
+                ("total_preemptions", ctypes.c_uint64), ("total_iterations", ctypes.c_uint64),
+                ("total_tokens_computed", ctypes.c_uint64), ("h2d_bytes", ctypes.c_uint64),
+                ("d2h_bytes", ctypes.c_uint64), ("kernel_launches", ctypes.c_uint64)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}

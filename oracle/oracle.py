@@ -168,7 +168,8 @@ class RefPath:
         lib.ref_engine_create.argtypes = [ctypes.c_int32] * 4
         lib.ref_generate.restype = ctypes.c_int64
         lib.ref_generate.argtypes = [ctypes.c_int64] * 12 + [_i64p, _i64p, _i64p, ctypes.c_int32,
-                                                             ctypes.c_int64, ctypes.c_char_p]
+                                                             ctypes.c_int64, ctypes.c_char_p,
+                                                             ctypes.POINTER(ctypes.c_double)]
         lib.ref_inv_sqrt.restype = ctypes.c_float
         lib.ref_inv_sqrt.argtypes = [ctypes.c_float]
         lib.ref_model_operands.restype = ctypes.c_int64
@@ -262,10 +263,28 @@ class RefPath:
                                   model["head_dim"], model["ffn"], num_blocks, block_size,
                                   max_batch, max_tokens_per_step, watermark, len(prompts),
                                   _ptr(lens, _i64p), _ptr(np.ascontiguousarray(toks), _i64p),
-                                  _ptr(mnt, _i64p), num_threads, max_steps, path.encode())
+                                  _ptr(mnt, _i64p), num_threads, max_steps, path.encode(), None)
         if n < 0:
             raise RuntimeError("ref_generate failed")
         return read_trace(path)
+
+    def generate_timed(self, model: dict, num_blocks: int, block_size: int, max_batch: int,
+                       max_tokens_per_step: int, watermark: int, prompts, max_new_tokens,
+                       num_threads: int = 0) -> tuple[int, float]:
+        """The same run without a trace: (steps, seconds of the scheduling
+        loop, model construction excluded)."""
+        lens = np.array([len(p) for p in prompts], np.int64)
+        toks = np.ascontiguousarray(np.concatenate([np.asarray(p, np.int64) for p in prompts]))
+        mnt = np.asarray(max_new_tokens, np.int64)
+        secs = ctypes.c_double(0.0)
+        n = self.lib.ref_generate(model["vocab"], model["hidden"], model["layers"], model["heads"],
+                                  model["head_dim"], model["ffn"], num_blocks, block_size,
+                                  max_batch, max_tokens_per_step, watermark, len(prompts),
+                                  _ptr(lens, _i64p), _ptr(toks, _i64p), _ptr(mnt, _i64p),
+                                  num_threads, 0, None, ctypes.byref(secs))
+        if n < 0:
+            raise RuntimeError("ref_generate failed")
+        return int(n), float(secs.value)
 
     def inv_sqrt(self, x: float) -> np.float32:
         """1.0f / std::sqrt(x) as the reference build evaluates it."""

@@ -32,6 +32,7 @@
 
 #include <algorithm>
 #include <array>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -314,17 +315,22 @@ int64_t ref_forward_attention(void* engine, void* cache, int32_t num_seqs,
 //     top-2 margin of the penalised logits (src/model.cpp:294-309) and the 8
 //     largest raw logits as (index, value) pairs; float values are stored as
 //     their 32-bit patterns
+// path NULL: no trace (timing runs). loop_seconds (may be NULL) receives the
+// wall time of the scheduling loop alone, model construction excluded.
 // Returns the number of steps, or -1 (cannot open path / bad arguments).
 int64_t ref_generate(int64_t vocab, int64_t hidden, int64_t layers, int64_t heads, int64_t head_dim,
                      int64_t ffn, int64_t num_blocks, int64_t block_size, int64_t max_batch,
                      int64_t max_tokens_per_step, int64_t watermark, int64_t num_requests,
                      const int64_t* prompt_lens, const int64_t* prompt_tokens,
                      const int64_t* max_new_tokens, int32_t num_threads, int64_t max_steps,
-                     const char* path) {
+                     const char* path, double* loop_seconds) {
     if (num_requests < 0 || hidden != heads * head_dim) return -1;
-    std::FILE* f = std::fopen(path, "wb");
-    if (f == nullptr) return -1;
-    auto put = [f](int64_t v) { std::fwrite(&v, sizeof(v), 1, f); };
+    std::FILE* f = path != nullptr ? std::fopen(path, "wb") : nullptr;
+    if (path != nullptr && f == nullptr) return -1;
+    const bool tracing = f != nullptr;
+    auto put = [f](int64_t v) {
+        if (f != nullptr) std::fwrite(&v, sizeof(v), 1, f);
+    };
     nano_vllm::ModelConfig mc{.vocab_size = std::size_t(vocab), .hidden_dim = std::size_t(hidden),
                               .num_layers = std::size_t(layers), .num_heads = std::size_t(heads),
                               .head_dim = std::size_t(head_dim), .ffn_dim = std::size_t(ffn)};
@@ -349,6 +355,7 @@ int64_t ref_generate(int64_t vocab, int64_t hidden, int64_t layers, int64_t head
     }
     int64_t step = 0;
     g_plan.active = false;
+    const auto t_loop = std::chrono::steady_clock::now();
     while (sched.has_pending_work() && (max_steps <= 0 || step < max_steps)) {
         (void)sched.schedule_step(cache);
         const auto running = sched.running();
@@ -366,13 +373,14 @@ int64_t ref_generate(int64_t vocab, int64_t hidden, int64_t layers, int64_t head
             put(int64_t(unc.size()));
             for (const std::size_t t : unc) put(int64_t(t));
         }
-        g_lm = LogitsCapture{.active = true, .call = 0, .target = std::size_t(6 * layers), .logits = {}};
+        g_lm = LogitsCapture{.active = tracing, .call = 0, .target = std::size_t(6 * layers),
+                             .logits = {}};
         const auto sampled = model.forward_batch(running, cache, pool);
         g_lm.active = false;
         put(-2);
         for (const std::size_t t : sampled) put(int64_t(t));
         auto bits = [](float x) { uint32_t u; std::memcpy(&u, &x, 4); return int64_t(u); };
-        for (std::size_t i = 0; i < running.size(); ++i) {
+        for (std::size_t i = 0; tracing && i < running.size(); ++i) {
             const float* row = g_lm.logits.data() + i * std::size_t(vocab);
             const std::size_t prev = running[i].tokens.empty() ? 0 : running[i].tokens.back();
             float b1 = -INFINITY, b2 = -INFINITY;
@@ -393,7 +401,11 @@ int64_t ref_generate(int64_t vocab, int64_t hidden, int64_t layers, int64_t head
         (void)sched.process_step_outputs(sampled, cache, model.vocab());
         ++step;
     }
-    std::fclose(f);
+    if (loop_seconds != nullptr) {
+        *loop_seconds =
+            std::chrono::duration<double>(std::chrono::steady_clock::now() - t_loop).count();
+    }
+    if (f != nullptr) std::fclose(f);
     return step;
 }
 
