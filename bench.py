@@ -674,7 +674,7 @@ def serve_main(args):
                          spec.model["heads"], spec.model["head_dim"])
     eng = Engine(lay, device=local, **spec.engine_limits())
     gemm = GEMM_BF16X9 if args.gemm == "bf16x9" else GEMM_FP32
-    model = Model(spec.model, eng, gemm_math=gemm)
+    model = Model(spec.model, eng, gemm_math=gemm, graph_max_tokens=args.graph_max_tokens)
     precision = nvllm.PRECISION_TF32 if args.precision == "tf32" else nvllm.PRECISION_FP32
     estream = torch.cuda.ExternalStream(eng.stream(), device=dev)
 
@@ -740,6 +740,7 @@ def serve_main(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded prompts; LCG weights of the reference model)",
         "config": {**serve_config(spec), "gemm": args.gemm, "prefill_precision": args.precision,
+                   "graph_max_tokens": args.graph_max_tokens,
                    "parallelism": f"sequence-partitioned x{world}",
                    "engine_iterations_per_step": iters / args.steps,
                    "tokens_computed_per_step": computed / args.steps,
@@ -793,6 +794,11 @@ def main() -> int:
                     default="decode")
     ap.add_argument("--gemm", choices=["fp32", "bf16x9"], default="fp32",
                     help="projection arithmetic of the serving workloads")
+    ap.add_argument("--graph-max-tokens", type=int, default=None,
+                    help="serving: engine iterations of at most this many new tokens replay a "
+                         "CUDA graph per padded bucket (0: eager; default 512 for the toy "
+                         "workloads, 0 for serve, whose cuBLAS GEMMs run slower on padded "
+                         "shapes than the launches they save)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32",
                     help="prefill tile arithmetic (decode is always fp32)")
@@ -806,6 +812,8 @@ def main() -> int:
     if args.workload in SERVE_WORKLOADS:
         if args.steps is None:
             args.steps = SERVE_DEFAULT_STEPS[args.workload]
+        if args.graph_max_tokens is None:
+            args.graph_max_tokens = 0 if args.workload == "serve" else 512
         return reference_serve_main(args) if args.impl == "reference" else serve_main(args)
     if args.steps is None:
         args.steps = 1000

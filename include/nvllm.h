@@ -162,6 +162,13 @@ int nvllm_paged_attention_head_split(const nvllm_head_split* hs, const float* qu
  * assert()s for these (src/kv_cache.cpp:50-51, :63-64). */
 int nvllm_get_last_error(void* stream);
 
+/* Device address of that status word on the current device (nonzero = some
+ * kernel raised a status since it was last cleared), so that a caller can read
+ * it with an asynchronous copy in the same stream as its results instead of
+ * the synchronous read of nvllm_get_last_error; call nvllm_get_last_error to
+ * decode and clear a nonzero word. */
+int nvllm_device_status_word(const uint32_t** word);
+
 /* Static string for a status code. */
 const char* nvllm_status_string(int status);
 

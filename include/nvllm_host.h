@@ -59,6 +59,15 @@ int nvllm_pack_metadata(int32_t num_seqs, const int32_t* num_computed, const int
                         const int64_t* block_ids, const int32_t* table_lens, int32_t block_size,
                         int32_t max_blocks, void* buf, size_t buf_bytes,
                         nvllm_metadata_offsets* out);
+/* The same batch laid out as pad_seqs sequences and pad_tokens token rows
+ * (at least the batch's own): extra sequences empty (cu_seqlens repeats the
+ * token count, context 0, last_token_idx 0, zero table row), extra token rows
+ * with slot -1; sizes from nvllm_metadata_bytes(pad_seqs, pad_tokens, ...). */
+int nvllm_pack_metadata_padded(int32_t num_seqs, const int32_t* num_computed,
+                               const int32_t* total_len, const int64_t* block_ids,
+                               const int32_t* table_lens, int32_t block_size, int32_t max_blocks,
+                               int32_t pad_seqs, int32_t pad_tokens, void* buf,
+                               size_t buf_bytes, nvllm_metadata_offsets* out);
 
 /* ---- engine --------------------------------------------------------------- */
 typedef struct nvllm_engine nvllm_engine;
@@ -79,6 +88,15 @@ int64_t nvllm_engine_num_free_blocks(const nvllm_engine* e);
 int nvllm_engine_begin_step(nvllm_engine* e, int32_t num_seqs, const int32_t* num_computed,
                             const int32_t* total_len, const int64_t* block_ids,
                             const int32_t* table_lens);
+/* begin_step laid out as pad_seqs sequences and pad_tokens token rows (at
+ * least the batch's own; at most max_seqs / max_tokens): the extra sequences
+ * are empty and the extra rows have slot -1, and the step's attention bounds
+ * become those of the bucket, so that every batch of a bucket issues the same
+ * launches. */
+int nvllm_engine_begin_step_padded(nvllm_engine* e, int32_t num_seqs, const int32_t* num_computed,
+                                   const int32_t* total_len, const int64_t* block_ids,
+                                   const int32_t* table_lens, int32_t pad_seqs,
+                                   int32_t pad_tokens);
 /* One layer, host rows [num_tokens, H*hd]; returns when out holds the result. */
 int nvllm_engine_attention(nvllm_engine* e, int32_t layer, const float* q, const float* k,
                            const float* v, float* out, int32_t precision);
@@ -108,6 +126,10 @@ typedef struct nvllm_model_config {
     int64_t vocab, hidden, layers, heads, head_dim, ffn;
     float emb_scale, ffn_scale; /* weight scales; 0 = 1/sqrt(hidden), 1/sqrt(ffn) */
     int32_t gemm_math;          /* nvllm_gemm_math */
+    /* Steps begun padded (nvllm_engine_begin_step_padded; the generator pads
+     * every step of at most this many new tokens to power-of-two buckets) run
+     * as one CUDA graph per bucket, captured on first use. 0: always eager. */
+    int32_t graph_max_tokens;
 } nvllm_model_config;
 
 int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvllm_model** out);

@@ -270,6 +270,14 @@ int nvllm_get_last_error(void* stream) {
     return NVLLM_ERR_INVALID;
 }
 
+int nvllm_device_status_word(const uint32_t** word) {
+    if (word == nullptr) return NVLLM_ERR_INVALID;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return NVLLM_ERR_CUDA;
+    *word = static_cast<const uint32_t*>(p);
+    return NVLLM_OK;
+}
+
 const char* nvllm_status_string(int status) {
     switch (status) {
         case NVLLM_OK: return "ok";

@@ -1,5 +1,6 @@
 #include "engine.hpp"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 
@@ -91,8 +92,10 @@ AttentionEngine::~AttentionEngine() {
     if (stream_) cudaStreamDestroy(stream_);
 }
 
-std::expected<void, EngineError> AttentionEngine::begin_step(std::span<const SequenceView> seqs) {
-    if (seqs.size() > std::size_t(cfg_.max_seqs)) {
+std::expected<void, EngineError> AttentionEngine::begin_step(std::span<const SequenceView> seqs,
+                                                            int32_t pad_seqs, int32_t pad_tokens) {
+    if (seqs.size() > std::size_t(cfg_.max_seqs) || pad_seqs > cfg_.max_seqs ||
+        pad_tokens > cfg_.max_tokens) {
         return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
     }
     NVLLM_CUDA_TRY(cudaSetDevice(cfg_.device));
@@ -100,7 +103,8 @@ std::expected<void, EngineError> AttentionEngine::begin_step(std::span<const Seq
     NVLLM_CUDA_TRY(cudaEventSynchronize(meta_done_[meta_slot_]));
     auto packed = pack_metadata(
         seqs, cfg_.layout.block_size, cfg_.max_blocks_per_seq,
-        std::span<std::byte>(reinterpret_cast<std::byte*>(h_meta_[meta_slot_]), meta_capacity_));
+        std::span<std::byte>(reinterpret_cast<std::byte*>(h_meta_[meta_slot_]), meta_capacity_),
+        pad_seqs, pad_tokens);
     if (!packed) return std::unexpected(EngineError{EngineError::Kind::Pack, int(packed.error())});
     if (packed->num_tokens > cfg_.max_tokens) {
         return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
@@ -109,6 +113,11 @@ std::expected<void, EngineError> AttentionEngine::begin_step(std::span<const Seq
                                    cudaMemcpyHostToDevice, stream_));
     NVLLM_CUDA_TRY(cudaEventRecord(meta_done_[meta_slot_], stream_));
     meta_slot_ ^= 1;
+    if (packed->padded) {
+        const int32_t cap = cfg_.max_blocks_per_seq * cfg_.layout.block_size;
+        packed->max_query_len = packed->max_query_len <= 1 ? 1 : std::min(packed->num_tokens, cap);
+        packed->max_context_len = cap;
+    }
     step_ = *packed;
     have_step_ = true;
     return {};

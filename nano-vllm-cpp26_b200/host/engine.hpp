@@ -68,8 +68,15 @@ public:
     // the step's packed metadata on the device (offsets in step())
     const unsigned char* device_metadata() const noexcept { return d_meta_; }
 
-    // Flattens the batch and uploads its metadata (one cudaMemcpyAsync).
-    std::expected<void, EngineError> begin_step(std::span<const SequenceView> seqs);
+    // Flattens the batch and uploads its metadata (one cudaMemcpyAsync). With
+    // pad_seqs / pad_tokens the batch is laid out as that many sequences and
+    // token rows (empty sequences, slot -1 rows) and the step's attention
+    // bounds become those of the bucket: max_query_len 1 for decode-only
+    // batches, else min(pad_tokens, max context); max_context_len the table
+    // capacity. Every batch of a bucket then issues identical launches, which
+    // is what lets the device model replay one captured CUDA graph per bucket.
+    std::expected<void, EngineError> begin_step(std::span<const SequenceView> seqs,
+                                                int32_t pad_seqs = 0, int32_t pad_tokens = 0);
 
     // One layer with host rows: H2D of Q/K/V, KV write, attention, D2H of the
     // output; returns once `out` holds the result. Rows that already live in

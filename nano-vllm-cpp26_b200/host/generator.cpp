@@ -1,5 +1,6 @@
 #include "generator.hpp"
 
+#include <algorithm>
 #include <bit>
 #include <cstring>
 #include <format>
@@ -10,6 +11,12 @@ namespace {
 constexpr int32_t kTraceTopK = 8;
 
 int64_t float_bits(float x) { return int64_t(std::bit_cast<uint32_t>(x)); }
+
+// the power of two at or above x (x >= 1), at most cap
+int32_t bucket(std::size_t x, int32_t cap) {
+    const std::size_t b = std::bit_ceil(std::max<std::size_t>(x, 1));
+    return int32_t(std::min<std::size_t>(b, std::size_t(cap)));
+}
 }  // namespace
 
 std::string Metrics::to_json() const {
@@ -103,7 +110,17 @@ std::expected<StepSummary, EngineError> Generator::step() {
         tokens_.insert(tokens_.end(), unc.begin(), unc.end());
         prev_[i] = seq.tokens.back();  // tokens is never empty
     }
-    if (auto r = eng_.begin_step(views_); !r) return std::unexpected(r.error());
+    // small steps are padded to a (sequences, tokens) bucket so that the model
+    // replays one captured CUDA graph per bucket
+    int32_t pad_seqs = 0, pad_tokens = 0;
+    const int32_t graph_max = model_.config().graph_max_tokens;
+    if (graph_max > 0 && tokens_.size() <= std::size_t(graph_max)) {
+        pad_seqs = bucket(n, eng_.config().max_seqs);
+        pad_tokens = bucket(tokens_.size(), eng_.config().max_tokens);
+    }
+    if (auto r = eng_.begin_step(views_, pad_seqs, pad_tokens); !r) {
+        return std::unexpected(r.error());
+    }
     sampled_.resize(n);
     const int32_t top_k = trace_ != nullptr ? kTraceTopK : 0;
     if (top_k > 0) {

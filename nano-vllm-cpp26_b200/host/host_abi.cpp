@@ -200,6 +200,25 @@ int nvllm_pack_metadata(int32_t num_seqs, const int32_t* num_computed, const int
     return NVLLM_OK;
 }
 
+int nvllm_pack_metadata_padded(int32_t num_seqs, const int32_t* num_computed,
+                               const int32_t* total_len, const int64_t* block_ids,
+                               const int32_t* table_lens, int32_t block_size, int32_t max_blocks,
+                               int32_t pad_seqs, int32_t pad_tokens, void* buf,
+                               size_t buf_bytes, nvllm_metadata_offsets* out) {
+    std::vector<nvllm::BlockId> storage;
+    std::vector<nvllm::SequenceView> views;
+    if (!make_views(num_seqs, num_computed, total_len, block_ids, table_lens, storage, views) ||
+        buf == nullptr || out == nullptr || pad_seqs < 1 || pad_tokens < 1) {
+        return NVLLM_ERR_INVALID;
+    }
+    auto r = nvllm::pack_metadata(views, block_size, max_blocks,
+                                  std::span<std::byte>(static_cast<std::byte*>(buf), buf_bytes),
+                                  pad_seqs, pad_tokens);
+    if (!r) return NVLLM_HOST_PACK_ERROR;
+    fill_offsets(*r, out);
+    return NVLLM_OK;
+}
+
 int nvllm_engine_create(const nvllm_engine_config* cfg, nvllm_engine** out) {
     if (cfg == nullptr || out == nullptr) return NVLLM_ERR_INVALID;
     *out = nullptr;
@@ -242,6 +261,20 @@ int nvllm_engine_begin_step(nvllm_engine* e, int32_t num_seqs, const int32_t* nu
     return r ? NVLLM_OK : engine_status(r.error());
 }
 
+int nvllm_engine_begin_step_padded(nvllm_engine* e, int32_t num_seqs, const int32_t* num_computed,
+                                   const int32_t* total_len, const int64_t* block_ids,
+                                   const int32_t* table_lens, int32_t pad_seqs,
+                                   int32_t pad_tokens) {
+    if (e == nullptr || pad_seqs < 1 || pad_tokens < 1) return NVLLM_ERR_INVALID;
+    std::vector<nvllm::BlockId> storage;
+    std::vector<nvllm::SequenceView> views;
+    if (!make_views(num_seqs, num_computed, total_len, block_ids, table_lens, storage, views)) {
+        return NVLLM_ERR_INVALID;
+    }
+    auto r = e->impl->begin_step(views, pad_seqs, pad_tokens);
+    return r ? NVLLM_OK : engine_status(r.error());
+}
+
 int nvllm_engine_attention(nvllm_engine* e, int32_t layer, const float* q, const float* k,
                            const float* v, float* out, int32_t precision) {
     if (e == nullptr) return NVLLM_ERR_INVALID;
@@ -277,7 +310,8 @@ int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvll
     nvllm::ModelConfig mc{.vocab = cfg->vocab, .hidden = cfg->hidden, .layers = cfg->layers,
                           .heads = cfg->heads, .head_dim = cfg->head_dim, .ffn = cfg->ffn,
                           .emb_scale = cfg->emb_scale, .ffn_scale = cfg->ffn_scale,
-                          .gemm_math = cfg->gemm_math};
+                          .gemm_math = cfg->gemm_math,
+                          .graph_max_tokens = cfg->graph_max_tokens};
     auto r = nvllm::DeviceModel::create(mc, *engine->impl);
     if (!r) return engine_status(r.error());
     auto* m = new (std::nothrow) nvllm_model{std::move(*r)};

@@ -33,8 +33,11 @@ MetadataLayout metadata_layout(int32_t num_seqs, int32_t num_tokens, int32_t max
 
 std::expected<MetadataLayout, PackError> pack_metadata(std::span<const SequenceView> seqs,
                                                        int32_t block_size, int32_t max_blocks,
-                                                       std::span<std::byte> buf) {
-    if (block_size <= 0 || max_blocks <= 0) return std::unexpected(PackError::Invalid);
+                                                       std::span<std::byte> buf,
+                                                       int32_t pad_seqs, int32_t pad_tokens) {
+    if (block_size <= 0 || max_blocks <= 0 || pad_seqs < 0 || pad_tokens < 0) {
+        return std::unexpected(PackError::Invalid);
+    }
     int64_t n_tokens = 0;
     int32_t max_q = 0, max_ctx = 0;
     for (const auto& sv : seqs) {
@@ -49,11 +52,18 @@ std::expected<MetadataLayout, PackError> pack_metadata(std::span<const SequenceV
         max_ctx = std::max(max_ctx, sv.total_len);
     }
     if (n_tokens > std::numeric_limits<int32_t>::max()) return std::unexpected(PackError::TooWide);
-    MetadataLayout m =
-        metadata_layout(int32_t(seqs.size()), int32_t(n_tokens), max_blocks);
+    const bool padded = pad_seqs > 0 || pad_tokens > 0;
+    const int32_t S = int32_t(seqs.size());
+    const int32_t S_out = std::max(S, pad_seqs);
+    const int32_t T_out = std::max(int32_t(n_tokens), pad_tokens);
+    if (padded && (pad_seqs < S || pad_tokens < n_tokens)) return std::unexpected(PackError::Invalid);
+    MetadataLayout m = metadata_layout(S_out, T_out, max_blocks);
     if (buf.size() < m.bytes) return std::unexpected(PackError::BufferTooSmall);
     m.max_query_len = max_q;
     m.max_context_len = max_ctx;
+    m.real_seqs = S;
+    m.real_tokens = int32_t(n_tokens);
+    m.padded = padded;
 
     auto* base = reinterpret_cast<unsigned char*>(buf.data());
     auto* cu = reinterpret_cast<int32_t*>(base + m.cu_off);
@@ -84,6 +94,14 @@ std::expected<MetadataLayout, PackError> pack_metadata(std::span<const SequenceV
         ctx[s] = sv.total_len;
         last[s] = t - 1;
     }
+    for (int32_t s = S; s < S_out; ++s) {
+        std::fill(tables + std::size_t(s) * std::size_t(max_blocks),
+                  tables + std::size_t(s + 1) * std::size_t(max_blocks), 0);
+        cu[s + 1] = t;
+        ctx[s] = 0;
+        last[s] = 0;
+    }
+    std::fill(slots + t, slots + T_out, -1);
     return m;
 }
 

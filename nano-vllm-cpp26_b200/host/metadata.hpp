@@ -30,8 +30,10 @@ struct SequenceView {
 
 struct MetadataLayout {
     std::size_t cu_off = 0, ctx_off = 0, last_off = 0, slot_off = 0, table_off = 0, bytes = 0;
-    int32_t num_seqs = 0, num_tokens = 0, max_blocks = 0;
+    int32_t num_seqs = 0, num_tokens = 0, max_blocks = 0;  // as laid out (padding included)
     int32_t max_query_len = 0, max_context_len = 0;
+    int32_t real_seqs = 0, real_tokens = 0;  // the batch's own sequences and new tokens
+    bool padded = false;
 };
 
 enum class PackError {
@@ -45,9 +47,15 @@ enum class PackError {
 MetadataLayout metadata_layout(int32_t num_seqs, int32_t num_tokens, int32_t max_blocks);
 
 // Packs the batch into buf; returns the layout actually used (max_blocks is the
-// caller's table width).
+// caller's table width). pad_seqs / pad_tokens (0: none) lay the batch out as
+// pad_seqs sequences and pad_tokens token rows, so that every batch of a
+// bucket has the same layout: the extra sequences are empty (no new tokens,
+// context 0, zero table row, last_token_idx 0) and the extra token rows have
+// slot -1, which the KV write skips.
 std::expected<MetadataLayout, PackError> pack_metadata(std::span<const SequenceView> seqs,
                                                        int32_t block_size, int32_t max_blocks,
-                                                       std::span<std::byte> buf);
+                                                       std::span<std::byte> buf,
+                                                       int32_t pad_seqs = 0,
+                                                       int32_t pad_tokens = 0);
 
 }  // namespace nvllm

@@ -56,7 +56,7 @@ std::expected<std::unique_ptr<DeviceModel>, EngineError> DeviceModel::create(
         cfg.hidden != cfg.heads * cfg.head_dim || cfg.hidden > INT32_MAX ||
         cfg.ffn > INT32_MAX || L.num_layers != cfg.layers || L.num_heads != cfg.heads ||
         L.head_dim != cfg.head_dim || cfg.emb_scale < 0.0f || cfg.ffn_scale < 0.0f ||
-        cfg.gemm_math < 0 || cfg.gemm_math > 1) {
+        cfg.gemm_math < 0 || cfg.gemm_math > 1 || cfg.graph_max_tokens < 0) {
         return invalid();
     }
     std::unique_ptr<DeviceModel> m(new DeviceModel(cfg, eng));
@@ -123,7 +123,9 @@ std::expected<void, EngineError> DeviceModel::init() {
     d_logits_ = d_last_ + S * D;
 
     io_in_bytes_ = align16(std::size_t(T) * 4) + align16(std::size_t(S) * 8);
-    io_out_bytes_ = 2 * align16(std::size_t(S) * 4) + 2 * std::size_t(S) * kMaxTopK * 4;
+    // sampled ids, margins, top-k indices and values, then 16 bytes for the
+    // status word
+    io_out_bytes_ = 2 * align16(std::size_t(S) * 4) + 2 * std::size_t(S) * kMaxTopK * 4 + 16;
     NVLLM_CUDA_TRY(cudaMalloc(&d_io_, io_in_bytes_ + io_out_bytes_));
     NVLLM_CUDA_TRY(cudaMallocHost(&h_io_, io_in_bytes_ + io_out_bytes_));
     d_tokens_ = reinterpret_cast<int32_t*>(d_io_);
@@ -133,6 +135,13 @@ std::expected<void, EngineError> DeviceModel::init() {
     d_margin_ = reinterpret_cast<float*>(out + align16(std::size_t(S) * 4));
     d_top_idx_ = reinterpret_cast<int32_t*>(out + 2 * align16(std::size_t(S) * 4));
     d_top_val_ = reinterpret_cast<float*>(d_top_idx_ + S * kMaxTopK);
+    // a fixed cuBLAS workspace: captured GEMMs must not allocate
+    constexpr std::size_t kBlasWorkspace = std::size_t(32) << 20;
+    NVLLM_CUDA_TRY(cudaMalloc(&d_blas_ws_, kBlasWorkspace));
+    NVLLM_BLAS_TRY(cublasSetWorkspace(blas_, d_blas_ws_, kBlasWorkspace));
+    NVLLM_OP_TRY(nvllm_device_status_word(&d_status_));
+    // activations start finite: padded rows of a bucket read rows no step wrote
+    NVLLM_CUDA_TRY(cudaMemsetAsync(d_act_, 0, act * sizeof(float), st));
     NVLLM_CUDA_TRY(cudaEventCreateWithFlags(&io_done_, cudaEventDisableTiming));
     NVLLM_CUDA_TRY(cudaEventRecord(io_done_, st));
     NVLLM_CUDA_TRY(cudaStreamSynchronize(st));
@@ -142,7 +151,9 @@ std::expected<void, EngineError> DeviceModel::init() {
 DeviceModel::~DeviceModel() {
     cudaSetDevice(eng_.config().device);
     cudaStreamSynchronize(eng_.stream());
+    for (auto& [key, exec] : graphs_) cudaGraphExecDestroy(exec);
     if (blas_) cublasDestroy(blas_);
+    if (d_blas_ws_) cudaFree(d_blas_ws_);
     if (io_done_) cudaEventDestroy(io_done_);
     if (h_io_) cudaFreeHost(h_io_);
     if (d_io_) cudaFree(d_io_);
@@ -165,30 +176,65 @@ std::expected<void, EngineError> DeviceModel::enqueue(std::span<const int64_t> t
                                                       std::span<const int64_t> prev_tokens,
                                                       int32_t precision, int32_t top_k) {
     const MetadataLayout& step = eng_.step();
-    if (!eng_.has_step() || token_ids.size() != std::size_t(step.num_tokens) ||
-        prev_tokens.size() != std::size_t(step.num_seqs) || top_k < 0 || top_k > kMaxTopK) {
+    if (!eng_.has_step() || token_ids.size() != std::size_t(step.real_tokens) ||
+        prev_tokens.size() != std::size_t(step.real_seqs) || top_k < 0 || top_k > kMaxTopK) {
         return invalid();
     }
-    const int64_t V = cfg_.vocab, D = cfg_.hidden, F = cfg_.ffn;
-    const int64_t T = step.num_tokens, S = step.num_seqs;
-    last_rows_ = int32_t(S);
-    if (S == 0) return {};
+    const int64_t V = cfg_.vocab;
+    const int64_t T = step.num_tokens, S = step.num_seqs;  // as laid out (padded or not)
+    last_rows_ = step.real_seqs;
+    if (step.real_seqs == 0) return {};
     cudaStream_t st = eng_.stream();
     NVLLM_CUDA_TRY(cudaSetDevice(eng_.config().device));
 
     // inputs: token ids modulo the vocabulary (src/model.cpp:152) and the
-    // previous tokens, one upload from pinned staging
+    // previous tokens, one upload from pinned staging; padded rows get token 0
     NVLLM_CUDA_TRY(cudaEventSynchronize(io_done_));
     auto* h_tok = reinterpret_cast<int32_t*>(h_io_);
     auto* h_prev = reinterpret_cast<int64_t*>(h_io_ + align16(std::size_t(eng_.config().max_tokens) * 4));
-    for (int64_t t = 0; t < T; ++t) {
+    for (std::size_t t = 0; t < token_ids.size(); ++t) {
         if (token_ids[t] < 0) return invalid();
         h_tok[t] = int32_t(token_ids[t] % V);
     }
-    for (int64_t s = 0; s < S; ++s) h_prev[s] = prev_tokens[s];
+    for (int64_t t = int64_t(token_ids.size()); t < T; ++t) h_tok[t] = 0;
+    for (std::size_t s = 0; s < prev_tokens.size(); ++s) h_prev[s] = prev_tokens[s];
+    for (int64_t s = int64_t(prev_tokens.size()); s < S; ++s) h_prev[s] = 0;
     NVLLM_CUDA_TRY(cudaMemcpyAsync(d_io_, h_io_, io_in_bytes_, cudaMemcpyHostToDevice, st));
     NVLLM_CUDA_TRY(cudaEventRecord(io_done_, st));
+    // embedding, last-token gather, sampler; per layer two RMSNorms, SiLU, the
+    // KV write and the attention's plan, decode and merge (+ prefill)
+    launches_ += 3 + uint64_t(cfg_.layers) * (3 + 4 + (step.max_query_len > 1 ? 1 : 0));
+    h2d_bytes_ += io_in_bytes_ + step.bytes;
 
+    if (!(step.padded && cfg_.graph_max_tokens > 0)) return body(step, precision, top_k);
+    const auto key = std::make_tuple(int32_t(T), int32_t(S), step.max_query_len, precision, top_k);
+    auto it = graphs_.find(key);
+    if (it == graphs_.end()) {
+        NVLLM_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        auto r = body(step, precision, top_k);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (!r || e != cudaSuccess) {
+            if (graph != nullptr) cudaGraphDestroy(graph);
+            if (!r) return r;
+            return cuda_error(e);
+        }
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) return cuda_error(ie);
+        it = graphs_.emplace(key, exec).first;
+    }
+    NVLLM_CUDA_TRY(cudaGraphLaunch(it->second, st));
+    ++graph_launches_;
+    return {};
+}
+
+std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, int32_t precision,
+                                                   int32_t top_k) {
+    const int64_t V = cfg_.vocab, D = cfg_.hidden, F = cfg_.ffn;
+    const int64_t T = step.num_tokens, S = step.num_seqs;
+    cudaStream_t st = eng_.stream();
     const float* emb = d_w_;
     NVLLM_OP_TRY(nvllm_embedding_gather(d_hidden_, emb, d_tokens_, T, V, D, st));
     const float one = 1.0f, zero = 0.0f;
@@ -219,10 +265,6 @@ std::expected<void, EngineError> DeviceModel::enqueue(std::span<const int64_t> t
     NVLLM_OP_TRY(nvllm_gather_rows(d_last_, d_hidden_, last_idx, S, T, D, st));
     const float* lm = d_w_ + V * D + std::size_t(cfg_.layers) * layer_floats_;
     if (auto r = gemm(d_last_, lm, d_logits_, S, D, V, 0.0f); !r) return r;
-    // embedding, last-token gather, sampler; per layer two RMSNorms, SiLU, the
-    // KV write and the attention's plan, decode and merge (+ prefill)
-    launches_ += 3 + uint64_t(cfg_.layers) * (3 + 4 + (step.max_query_len > 1 ? 1 : 0));
-    h2d_bytes_ += io_in_bytes_ + step.bytes;
     NVLLM_OP_TRY(nvllm_penalized_argmax(d_logits_, d_prev_, S, V, kRepeatPenalty, d_sampled_,
                                         top_k > 0 ? d_margin_ : nullptr,
                                         top_k > 0 ? d_top_idx_ : nullptr,
@@ -241,12 +283,17 @@ std::expected<void, EngineError> DeviceModel::forward(std::span<const int64_t> t
     if (sampled == nullptr) return invalid();
     cudaStream_t st = eng_.stream();
     unsigned char* h_out = h_io_ + io_in_bytes_;
-    const std::size_t bytes = top_k > 0 ? io_out_bytes_ : std::size_t(S) * 4;
+    const std::size_t bytes = top_k > 0 ? io_out_bytes_ - 16 : std::size_t(S) * 4;
     NVLLM_CUDA_TRY(cudaMemcpyAsync(h_out, d_io_ + io_in_bytes_, bytes, cudaMemcpyDeviceToHost, st));
-    d2h_bytes_ += bytes;
+    // the kernels' status word rides along with the results (4 bytes)
+    auto* h_status = reinterpret_cast<uint32_t*>(h_out + io_out_bytes_ - 16);
+    NVLLM_CUDA_TRY(cudaMemcpyAsync(h_status, d_status_, 4, cudaMemcpyDeviceToHost, st));
+    d2h_bytes_ += bytes + 4;
     NVLLM_CUDA_TRY(cudaStreamSynchronize(st));
-    const int32_t status = nvllm_get_last_error(st);
-    if (status != NVLLM_OK) return kernel_error(status);
+    if (*h_status != 0) {
+        const int32_t status = nvllm_get_last_error(st);  // decodes and clears it
+        if (status != NVLLM_OK) return kernel_error(status);
+    }
     const int64_t S_cap = eng_.config().max_seqs;
     const auto* h_sampled = reinterpret_cast<const int32_t*>(h_out);
     for (int64_t s = 0; s < S; ++s) sampled[s] = h_sampled[s];

@@ -25,8 +25,10 @@
 #include <cstddef>
 #include <cstdint>
 #include <expected>
+#include <map>
 #include <memory>
 #include <span>
+#include <tuple>
 
 #include "engine.hpp"
 
@@ -38,6 +40,9 @@ struct ModelConfig {
     float emb_scale = 0.0f, ffn_scale = 0.0f;
     // 0: fp32 FFMA; 1: fp32 emulated with bf16x9 on the tensor cores
     int32_t gemm_math = 0;
+    // Steps of at most this many new tokens run as one CUDA graph per padded
+    // (tokens, sequences) bucket, captured on first use (0: always eager).
+    int32_t graph_max_tokens = 0;
 };
 
 class DeviceModel {
@@ -60,6 +65,10 @@ public:
     // sequence's last token (src/model.cpp:297-298). Writes sampled[s]; with
     // top_k > 0 also the top-2 margin of the penalised logits and the top_k
     // largest raw logits of every row. Returns once the results are on the host.
+    // A step begun padded (begin_step with pad_seqs / pad_tokens) runs the
+    // padded shapes; with graph_max_tokens > 0 it replays the bucket's CUDA
+    // graph (captured the first time the bucket is seen). Padded rows compute
+    // values nobody reads; they never reach the arena or the results.
     std::expected<void, EngineError> forward(std::span<const int64_t> token_ids,
                                              std::span<const int64_t> prev_tokens,
                                              int64_t* sampled, int32_t precision,
@@ -77,6 +86,8 @@ public:
     // (cuBLAS GEMMs not counted) and bytes copied host->device (token ids,
     // previous tokens, the engine's metadata) and device->host (results).
     uint64_t kernel_launches() const noexcept { return launches_; }
+    uint64_t graph_launches() const noexcept { return graph_launches_; }
+    std::size_t graphs_captured() const noexcept { return graphs_.size(); }
     uint64_t h2d_bytes() const noexcept { return h2d_bytes_; }
     uint64_t d2h_bytes() const noexcept { return d2h_bytes_; }
 
@@ -85,6 +96,9 @@ private:
     std::expected<void, EngineError> init();
     std::expected<void, EngineError> gemm(const float* a, const float* w, float* c, int64_t m,
                                           int64_t k, int64_t n, float beta);
+    // the device work of one step (everything after the input upload)
+    std::expected<void, EngineError> body(const MetadataLayout& step, int32_t precision,
+                                          int32_t top_k);
 
     ModelConfig cfg_;
     AttentionEngine& eng_;
@@ -113,7 +127,11 @@ private:
     float* d_top_val_ = nullptr;    // [S, 32]
     cudaEvent_t io_done_ = nullptr;
     int32_t last_rows_ = 0;
-    uint64_t launches_ = 0, h2d_bytes_ = 0, d2h_bytes_ = 0;
+    uint64_t launches_ = 0, h2d_bytes_ = 0, d2h_bytes_ = 0, graph_launches_ = 0;
+    void* d_blas_ws_ = nullptr;           // cuBLAS workspace (graph capture needs a fixed one)
+    const uint32_t* d_status_ = nullptr;  // libnvllm's device status word
+    // (tokens, sequences, max query rows, precision, top_k) -> instantiated graph
+    std::map<std::tuple<int32_t, int32_t, int32_t, int32_t, int32_t>, cudaGraphExec_t> graphs_;
 };
 
 }  // namespace nvllm

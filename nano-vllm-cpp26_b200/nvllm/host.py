@@ -69,7 +69,7 @@ class ModelConfig(ctypes.Structure):
     _fields_ = [("vocab", ctypes.c_int64), ("hidden", ctypes.c_int64), ("layers", ctypes.c_int64),
                 ("heads", ctypes.c_int64), ("head_dim", ctypes.c_int64), ("ffn", ctypes.c_int64),
                 ("emb_scale", ctypes.c_float), ("ffn_scale", ctypes.c_float),
-                ("gemm_math", ctypes.c_int32)]
+                ("gemm_math", ctypes.c_int32), ("graph_max_tokens", ctypes.c_int32)]
 
 
 GEMM_FP32 = 0
@@ -97,6 +97,10 @@ def host_lib() -> ctypes.CDLL:
     L.nvllm_block_allocator_num_free.argtypes = [_vp]
     L.nvllm_metadata_bytes.restype = ctypes.c_size_t
     L.nvllm_metadata_bytes.argtypes = [ctypes.c_int32] * 3
+    L.nvllm_pack_metadata_padded.argtypes = [ctypes.c_int32, _i32p, _i32p, _i64p, _i32p,
+                                             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                             ctypes.c_int32, _vp, ctypes.c_size_t,
+                                             ctypes.POINTER(MetadataOffsets)]
     L.nvllm_pack_metadata.argtypes = [ctypes.c_int32, _i32p, _i32p, _i64p, _i32p, ctypes.c_int32,
                                       ctypes.c_int32, _vp, ctypes.c_size_t,
                                       ctypes.POINTER(MetadataOffsets)]
@@ -107,6 +111,8 @@ def host_lib() -> ctypes.CDLL:
     L.nvllm_engine_num_free_blocks.restype = ctypes.c_int64
     L.nvllm_engine_num_free_blocks.argtypes = [_vp]
     L.nvllm_engine_begin_step.argtypes = [_vp, ctypes.c_int32, _i32p, _i32p, _i64p, _i32p]
+    L.nvllm_engine_begin_step_padded.argtypes = [_vp, ctypes.c_int32, _i32p, _i32p, _i64p,
+                                                 _i32p, ctypes.c_int32, ctypes.c_int32]
     L.nvllm_engine_attention.argtypes = [_vp, ctypes.c_int32, _f32p, _f32p, _f32p, _f32p,
                                          ctypes.c_int32]
     L.nvllm_engine_host_buffers.argtypes = [_vp] + [ctypes.POINTER(_f32p)] * 4
@@ -192,20 +198,29 @@ class BlockAllocator:
         return self.L.nvllm_block_allocator_num_free(self.h)
 
 
-def pack_metadata(num_computed, total_len, tables, block_size: int, max_blocks: int) -> dict:
-    """Host packer (no GPU): returns the int32 sections of the packed buffer."""
+def pack_metadata(num_computed, total_len, tables, block_size: int, max_blocks: int,
+                  pad_seqs: int = 0, pad_tokens: int = 0) -> dict:
+    """Host packer (no GPU): returns the int32 sections of the packed buffer
+    (laid out as pad_seqs sequences / pad_tokens rows when they are given)."""
     L = host_lib()
     nc = np.ascontiguousarray(num_computed, np.int32)
     tl = np.ascontiguousarray(total_len, np.int32)
     ids, lens = _tables(tables)
-    S = len(tl)
-    n = int((tl - nc).sum()) if S else 0
-    nbytes = L.nvllm_metadata_bytes(S, max(n, 0), max_blocks)
+    n = int((tl - nc).sum()) if len(tl) else 0
+    padded = pad_seqs > 0 or pad_tokens > 0
+    S = max(len(tl), pad_seqs)
+    nbytes = L.nvllm_metadata_bytes(S, max(n, pad_tokens, 0), max_blocks)
     buf = np.zeros(max(nbytes, 16) // 4, np.int32)
     off = MetadataOffsets()
-    rc = L.nvllm_pack_metadata(S, _ptr(nc, _i32p), _ptr(tl, _i32p), _ptr(ids, _i64p),
-                               _ptr(lens, _i32p), block_size, max_blocks, buf.ctypes.data,
-                               buf.nbytes, ctypes.byref(off))
+    if padded:
+        rc = L.nvllm_pack_metadata_padded(len(tl), _ptr(nc, _i32p), _ptr(tl, _i32p),
+                                          _ptr(ids, _i64p), _ptr(lens, _i32p), block_size,
+                                          max_blocks, pad_seqs, pad_tokens, buf.ctypes.data,
+                                          buf.nbytes, ctypes.byref(off))
+    else:
+        rc = L.nvllm_pack_metadata(len(tl), _ptr(nc, _i32p), _ptr(tl, _i32p), _ptr(ids, _i64p),
+                                   _ptr(lens, _i32p), block_size, max_blocks, buf.ctypes.data,
+                                   buf.nbytes, ctypes.byref(off))
     if rc != OK:
         raise NvllmError(rc, "nvllm_pack_metadata")
 
@@ -270,6 +285,17 @@ class Engine:
         if rc != OK:
             raise NvllmError(rc, "nvllm_engine_begin_step")
 
+    def begin_step_padded(self, num_computed, total_len, tables, pad_seqs: int,
+                          pad_tokens: int) -> None:
+        nc = np.ascontiguousarray(num_computed, np.int32)
+        tl = np.ascontiguousarray(total_len, np.int32)
+        ids, lens = _tables(tables)
+        rc = self.L.nvllm_engine_begin_step_padded(self.h, len(tl), _ptr(nc, _i32p),
+                                                   _ptr(tl, _i32p), _ptr(ids, _i64p),
+                                                   _ptr(lens, _i32p), pad_seqs, pad_tokens)
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_engine_begin_step_padded")
+
     def prepare_tables(self, tables):
         """Pre-flattened (ids, lens) for begin_step_raw."""
         return _tables(tables)
@@ -309,13 +335,14 @@ class Model:
     optional [emb_scale, ffn_scale] of the weights; ``gemm_math`` GEMM_FP32
     (FFMA) or GEMM_BF16X9 (fp32 emulated on the tensor cores)."""
 
-    def __init__(self, cfg: dict, engine: Engine, scales=None, gemm_math: int = GEMM_FP32):
+    def __init__(self, cfg: dict, engine: Engine, scales=None, gemm_math: int = GEMM_FP32,
+                 graph_max_tokens: int = 0):
         self.L = host_lib()
         self.engine = engine  # the model uses the engine's arenas and stream
         self.cfg = dict(cfg)
         es, fs = (0.0, 0.0) if scales is None else (float(scales[0]), float(scales[1]))
         mc = ModelConfig(cfg["vocab"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["head_dim"],
-                         cfg["ffn"], es, fs, gemm_math)
+                         cfg["ffn"], es, fs, gemm_math, graph_max_tokens)
         h = _vp()
         rc = self.L.nvllm_model_create(ctypes.byref(mc), engine.h, ctypes.byref(h))
         if rc != OK:

@@ -109,3 +109,35 @@ def test_packer_rejects_bad_batches(host):
         host.pack_metadata([5], [4], [[0]], 16, 4)
     m = host.pack_metadata([], [], [], 16, 4)  # empty batch
     assert m["cu_seqlens_q"].tolist() == [0]
+
+
+def test_packer_padding_to_a_bucket(host, oracle):
+    """A batch laid out as a bigger bucket: the real part is the unpadded
+    packing unchanged, the extra sequences are empty and the extra rows have
+    slot -1 (which the KV write skips)."""
+    from nvllm import NvllmError
+    for seed in range(10):
+        S = int(det_ints(seed, 1, 1, 1, 9)[0])
+        total = det_ints(seed, 2, S, 1, 200)
+        comp = np.minimum(total, det_ints(seed, 3, S, 0, 200))
+        B = [4, 8, 16][seed % 3]
+        case = make_case("p", seed, num_heads=1, head_dim=32, block_size=B, num_layers=1,
+                         num_computed=comp, total_len=total)
+        W = case.block_tables.shape[1]
+        plain = host.pack_metadata(case.num_computed, case.total_len, _tables_of(case), B, W)
+        T = len(plain["slot_mapping"])
+        pS, pT = S + 3, T + 5
+        m = host.pack_metadata(case.num_computed, case.total_len, _tables_of(case), B, W,
+                               pad_seqs=pS, pad_tokens=pT)
+        assert np.array_equal(m["cu_seqlens_q"][:S + 1], plain["cu_seqlens_q"])
+        assert (m["cu_seqlens_q"][S + 1:] == T).all()
+        assert np.array_equal(m["context_lens"][:S], plain["context_lens"])
+        assert (m["context_lens"][S:] == 0).all()
+        assert np.array_equal(m["last_token_idx"][:S], plain["last_token_idx"])
+        assert (m["last_token_idx"][S:] == 0).all()
+        assert np.array_equal(m["slot_mapping"][:T], plain["slot_mapping"])
+        assert (m["slot_mapping"][T:] == -1).all() and len(m["slot_mapping"]) == pT
+        assert np.array_equal(m["block_tables"][:S], plain["block_tables"])
+        assert (m["block_tables"][S:] == 0).all()
+    with pytest.raises(NvllmError):  # a bucket smaller than the batch
+        host.pack_metadata([0, 0], [3, 3], [[1], [2]], 16, 2, pad_seqs=1, pad_tokens=8)
