@@ -6,31 +6,35 @@
 // Geometry: head_dim 128, block size 16 (one TMA box = the 16 rows of one
 // physical block and 32 columns of one head).
 //
-// One CTA per SM (persistent), 5 warps:
+// One CTA per SM (persistent), 13 warps:
 //   warps 0-3  softmax / epilogue: thread t owns query row t of a 128-row tile
 //              and TMEM lane t. Per key tile (32 keys) it reads its row of S
 //              from TMEM (tcgen05.ld), applies the causal mask, updates the
-//              online max and sum, writes P (tf32) to shared memory, writes
-//              column t of V transposed (tf32, zero past the visible keys) to
-//              shared memory, and folds the previous tile's P.V from TMEM into
-//              an fp32 register accumulator with the usual rescale.
+//              online max and sum, rescales its row of the O accumulator in
+//              TMEM by exp(m_old - m_new) (skipped when no row of the warp saw
+//              its maximum grow: the factor is then exactly 1), and stores P as
+//              tf32 hi / lo parts into its own TMEM lane (the A operand of P.V).
 //   warp 4     producer: one thread issues the TMA gathers of the K and V
 //              tiles (2 physical blocks x 4 swizzle atoms per tensor) into a
 //              3-stage ring and all tcgen05.mma: S(t+1) = Q K(t+1)^T is issued
 //              while the softmax warps work on S(t); O(t) = P(t) V(t) once P(t)
-//              and V(t)^T are in shared memory.
-// Both products run as 3xTF32 (A_hi B_hi + A_lo B_hi + A_hi B_lo, every part
-// rounded to nearest), which keeps them at fp32 accuracy: a single tf32 pass
-// errs by ~1e-3 in the output at these magnitudes (one visible key => the
-// output is that key's V row, carried at tf32 precision). Q_hi and Q_lo live
-// in TMEM as the A operand of S; K_hi (rounded in place) and K_lo are written
-// by the producer warp next to the TMA-loaded K tile; P and V^T hi / lo parts
-// by the softmax warps.
-// The shared-memory operands (K, P, V^T parts) are K-major in the 128-byte
-// swizzled layout (TMA writes K that way; P and V^T are written by the softmax
-// threads in the same pattern). V must be transposed on chip: a tf32 operand
-// can only be consumed K-major here, and V arrives key-major. TMEM holds S
-// twice (2 x 32 columns), O (128 columns) and Q_hi, Q_lo (128 columns each).
+//              is in TMEM, accumulating into O in TMEM.
+//   warps 5-12 converters, working ahead of the MMAs: write the lo part of the
+//              landed K tile, and transpose V into the K-major V^T hi / lo
+//              operand (zero past the visible keys) in one of two V^T buffers.
+// Both products run as 3xTF32 (A_hi B_hi + A_lo B_hi + A_hi B_lo), which keeps
+// them at fp32 accuracy: a single tf32 pass errs by ~1e-3 in the output at
+// these magnitudes (one visible key => the output is that key's V row, carried
+// at tf32 precision). The tensor core reads a tf32 operand as the top 19 bits
+// of its fp32 container, so hi is the value itself and lo = x - (x with its low
+// 13 bits cleared), exact in fp32; the terms left out (lo*lo and lo's own low
+// bits) are ~2^-20 of the product. Q_hi and Q_lo live in TMEM as the A operand
+// of S, P_hi and P_lo in TMEM as the A operand of O.
+// The shared-memory operands (K and V^T parts) are K-major in the 128-byte
+// swizzled layout (TMA writes K that way; the converters write V^T in the same
+// pattern). V must be transposed on chip: a tf32 operand can only be consumed
+// K-major here, and V arrives key-major. TMEM (512 columns): S twice (2 x 32),
+// P_hi and P_lo (32 each), O (128), Q_hi and Q_lo (128 each).
 // Every wait is bounded; on a timeout the CTA records NVLLM_ERR_TIMEOUT, lets
 // its outstanding copies and MMAs finish and frees its TMEM.
 #include <cuda.h>
@@ -50,32 +54,40 @@ constexpr int kQT = 128;  // query rows per tile (= TMEM lanes)
 constexpr int kKT = 32;   // keys per tile
 constexpr int kHD = 128;
 constexpr int kStages = 3;
-constexpr int kThreads = 160;
-// TMEM columns: S[0] 0..31, S[1] 32..63, O 128..255, Q_hi 256..383, Q_lo 384..511
+constexpr int kSoftmaxThreads = 128;  // warps 0-3
+constexpr int kProducerWarp = 4;
+constexpr int kConvThreads = 256;     // warps 5-12
+constexpr int kThreads = kSoftmaxThreads + 32 + kConvThreads;
+// TMEM columns: S[0] 0..31, S[1] 32..63, P_hi 64..95, P_lo 96..127, O 128..255,
+// Q_hi 256..383, Q_lo 384..511
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColPhi = 64;
+constexpr uint32_t kColPlo = 96;
 constexpr uint32_t kColO = 128;
 constexpr uint32_t kColQhi = 256;
 constexpr uint32_t kColQlo = 384;
 
 constexpr uint32_t kKVAtom = kKT * 128;         // 32 rows x 32 fp32
 constexpr uint32_t kKBytes = 4 * kKVAtom;       // 16 KiB per tensor tile
-constexpr uint32_t kStageBytes = 3 * kKBytes;   // K_hi, K_lo, V
-constexpr uint32_t kPBytes = kQT * 128;         // 128 rows x 32 keys (one of hi / lo)
+constexpr uint32_t kStageBytes = 3 * kKBytes;   // K (= K_hi), K_lo, V
 constexpr uint32_t kVtBytes = kHD * 128;        // 128 dims x 32 keys (one of hi / lo)
+constexpr uint32_t kVtBufBytes = 2 * kVtBytes;  // hi + lo
 constexpr uint32_t kOffKV = 0;
-constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;
-constexpr uint32_t kOffVt = kOffP + 2 * kPBytes;
-constexpr uint32_t kOffBar = kOffVt + 2 * kVtBytes;
+constexpr uint32_t kOffVt = kOffKV + kStages * kStageBytes;
+constexpr uint32_t kOffBar = kOffVt + 2 * kVtBufBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + control block + alignment slack
+static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
 
 constexpr uint32_t kIdescS = tc::tf32_idesc(kQT, kKT, false, false);
 constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, false);
 
 struct Control {
-    uint64_t kv_full[kStages];
-    uint64_t pv_done[kStages];
+    uint64_t kv_full[kStages];   // TMA landed (transaction count)
+    uint64_t cv_full[kStages];   // converters done: K_lo and V^T written (256 arrivals)
+    uint64_t pv_done[kStages];   // O of the stage's tile complete: stage reusable
+    uint64_t vt_free[2];         // O complete: V^T buffer reusable
     uint64_t s_full[2];
-    uint64_t p_full;
+    uint64_t p_full;             // P in TMEM, previous O folded (128 arrivals)
     uint64_t o_full;
     uint64_t drain;
     uint32_t tmem_base;
@@ -99,6 +111,12 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Co
     }
 }
 
+// x = x_hi + lo exactly, with x_hi = x with its low 13 bits cleared (what the
+// tensor core reads of a tf32 operand)
+__device__ __forceinline__ float tf32_lo(float x) {
+    return x - __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+}
+
 __device__ __forceinline__ uint32_t stage_of(uint32_t n) { return n % kStages; }
 __device__ __forceinline__ uint32_t stage_parity(uint32_t n) { return (n / kStages) & 1u; }
 
@@ -109,7 +127,6 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* sKV = base + kOffKV;
-    unsigned char* sP = base + kOffP;
     unsigned char* sVt = base + kOffVt;
     Control* ctl = reinterpret_cast<Control*>(base + kOffBar);
     const int tid = threadIdx.x;
@@ -119,16 +136,20 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&ctl->kv_full[i], 1);
+            mbar_init(&ctl->cv_full[i], kConvThreads);
             mbar_init(&ctl->pv_done[i], 1);
         }
-        for (int i = 0; i < 2; ++i) mbar_init(&ctl->s_full[i], 1);
-        mbar_init(&ctl->p_full, kQT);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&ctl->vt_free[i], 1);
+            mbar_init(&ctl->s_full[i], 1);
+        }
+        mbar_init(&ctl->p_full, kSoftmaxThreads);
         mbar_init(&ctl->o_full, 1);
         mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
     }
     fence_barrier_init();
-    if (warp == 4) {
+    if (warp == kProducerWarp) {
         tc::tmem_alloc(&ctl->tmem_base, kTmemCols);
         tc::tmem_relinquish();
     }
@@ -143,7 +164,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     const int total = p.counters->prefill_items * H;
     uint32_t tile_seq = 0;   // key tiles processed by this CTA (ring position)
     uint32_t next_load = 0;  // producer: ring index of the next K/V load to issue
-    uint32_t next_wait = 0;  // producer: ring index of the next K/V load to wait for
+    uint32_t next_wait = 0;  // producer: ring index of the next load not known to have landed
     bool issued_mma = false;
 
     for (;;) {
@@ -166,9 +187,9 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
         const int ntiles = (nk + kKT - 1) / kKT;
         const uint32_t n0 = tile_seq;
 
-        if (warp < 4) {
-            // Q tile -> TMEM as the A operand of S = Q K^T, split for 3xTF32:
-            // q = q_hi + q_lo with both parts tf32 (round to nearest).
+        if (tid < kSoftmaxThreads) {
+            // Q tile -> TMEM as the A operand of S = Q K^T, split for 3xTF32
+            // (q_hi = q as read by the tensor core, q_lo = the rest).
             const int row = tid;
             const uint32_t lane_off = uint32_t(warp * 32) << 16;
             const float4* qrow = reinterpret_cast<const float4*>(
@@ -183,8 +204,8 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     const float x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        hi[4 * i + e] = tc::to_tf32(x[e]);
-                        lo[4 * i + e] = tc::to_tf32(x[e] - hi[4 * i + e]);
+                        hi[4 * i + e] = x[e];
+                        lo[4 * i + e] = tf32_lo(x[e]);
                     }
                 }
                 tc::tmem_st32(tmem + kColQhi + c * 32u + lane_off, hi);
@@ -195,11 +216,10 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
         }
         __syncthreads();
 
-        if (warp == 4) {
+        if (warp == kProducerWarp) {
             // ---------------------------------------------------------------- producer
-            // The whole warp waits and rounds each K tile to tf32 in place (the
-            // tensor core would otherwise truncate it); lane 0 alone issues the
-            // TMA copies, the MMAs and their commits.
+            // Lane 0 issues the TMA copies, the MMAs and their commits; the whole
+            // warp takes part in the waits.
             const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
             auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
                 const bool got = wait_or_abort(bar, parity, ctl);
@@ -241,23 +261,11 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 next_load = n + 1;
                 return true;
             };
-            // wait for tile n's K/V, split its K into tf32 hi (in place) and lo
-            // parts, then S(n) = Q_hi K_hi^T + Q_lo K_hi^T + Q_hi K_lo^T
-            auto stage_and_issue_s = [&](uint32_t n) -> bool {
-                if (!wait_all(&ctl->kv_full[stage_of(n)], stage_parity(n))) return false;
+            // once the converters have split tile n's K:
+            // S(n) = Q_hi K_hi^T + Q_lo K_hi^T + Q_hi K_lo^T
+            auto issue_s = [&](uint32_t n) -> bool {
+                if (!wait_all(&ctl->cv_full[stage_of(n)], stage_parity(n))) return false;
                 next_wait = n + 1;
-                float4* kp = reinterpret_cast<float4*>(sKV + stage_of(n) * kStageBytes);
-                float4* klp = kp + kKBytes / 16;
-                for (uint32_t i = lane; i < kKBytes / 16; i += 32) {
-                    const float4 v = kp[i];
-                    const float4 hi = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y),
-                                                  tc::to_tf32(v.z), tc::to_tf32(v.w));
-                    kp[i] = hi;
-                    klp[i] = make_float4(tc::to_tf32(v.x - hi.x), tc::to_tf32(v.y - hi.y),
-                                         tc::to_tf32(v.z - hi.z), tc::to_tf32(v.w - hi.w));
-                }
-                tc::fence_async_smem();
-                __syncwarp();
                 if (lane == 0) {
                     tc::fence_after_sync();
                     const uint32_t ka = smem_addr(sKV + stage_of(n) * kStageBytes);
@@ -278,52 +286,93 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 __syncwarp();
                 return true;
             };
-            auto issue_o = [&](uint32_t n) {
+            // O(n) = P_hi V_hi + P_lo V_hi + P_hi V_lo, P from TMEM, V^T from the
+            // buffer the converters filled for tile n
+            auto issue_o = [&](uint32_t n, bool first) {
                 if (lane == 0) {
                     tc::fence_after_sync();
-                    const uint32_t pa = smem_addr(sP);
-                    const uint32_t va = smem_addr(sVt);
+                    const uint32_t va = smem_addr(sVt + (n & 1u) * kVtBufBytes);
 #pragma unroll
                     for (int k = 0; k < kKT / 8; ++k) {
-                        const uint64_t phi = tc::sw128_desc(pa + k * 32u, 16, 1024);
-                        const uint64_t plo = tc::sw128_desc(pa + kPBytes + k * 32u, 16, 1024);
                         const uint64_t vhi = tc::sw128_desc(va + k * 32u, 16, 1024);
                         const uint64_t vlo = tc::sw128_desc(va + kVtBytes + k * 32u, 16, 1024);
-                        tc::mma_tf32(tO, plo, vhi, kIdescO, k > 0);
-                        tc::mma_tf32(tO, phi, vlo, kIdescO, true);
-                        tc::mma_tf32(tO, phi, vhi, kIdescO, true);
+                        tc::mma_tf32_ts(tO, tmem + kColPlo + 8u * k, vhi, kIdescO, k > 0 || !first);
+                        tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vlo, kIdescO, true);
+                        tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vhi, kIdescO, true);
                     }
                     tc::commit(&ctl->o_full);
                     tc::commit(&ctl->pv_done[stage_of(n)]);
+                    tc::commit(&ctl->vt_free[n & 1u]);
                 }
                 __syncwarp();
             };
 
             bool ok = true;
             for (int t = 0; ok && t < min(ntiles, kStages); ++t) ok = load(n0 + t, t);
-            if (ok) ok = stage_and_issue_s(n0);
+            if (ok) ok = issue_s(n0);
             for (int t = 0; ok && t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
                 if (t + 1 < ntiles) {
-                    ok = stage_and_issue_s(n + 1);
+                    ok = issue_s(n + 1);
                     if (!ok) break;
                 }
                 ok = wait_all(&ctl->p_full, n & 1u);
                 if (!ok) break;
-                issue_o(n);
+                issue_o(n, t == 0);
                 if (t + kStages < ntiles) ok = load(n + kStages, t + kStages);
+            }
+        } else if (warp > kProducerWarp) {
+            // -------------------------------------------------------------- converters
+            // thread c: 4 float4 of K_lo, then keys 16*(c/128) .. +15 of V^T row c%128
+            const int c = tid - (kSoftmaxThreads + 32);
+            const int d = c & (kHD - 1);  // dimension = V^T row
+            const int kh = c >> 7;        // which 16 keys of the tile
+            const int vt_dd = d & 31;     // dimension within its V atom
+            for (int t = 0; t < ntiles; ++t) {
+                const uint32_t n = n0 + t;
+                if (!wait_or_abort(&ctl->kv_full[stage_of(n)], stage_parity(n), ctl)) break;
+                unsigned char* stage = sKV + stage_of(n) * kStageBytes;
+                {
+                    const float4* kp = reinterpret_cast<const float4*>(stage);
+                    float4* klp = reinterpret_cast<float4*>(stage + kKBytes);
+#pragma unroll
+                    for (int i = 0; i < int(kKBytes / 16) / kConvThreads; ++i) {
+                        const int j = c + i * kConvThreads;
+                        const float4 v = kp[j];
+                        klp[j] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+                    }
+                }
+                if (n >= 2 && !wait_or_abort(&ctl->vt_free[n & 1u], ((n >> 1) - 1) & 1u, ctl)) break;
+                unsigned char* vt = sVt + (n & 1u) * kVtBufBytes;
+                const int nvk = nk - t * kKT;
+                const unsigned char* sV = stage + 2 * kKBytes + (d >> 5) * kKVAtom + (vt_dd & 3) * 4;
+#pragma unroll
+                for (int q = 4 * kh; q < 4 * kh + 4; ++q) {
+                    float hi[4], lo[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int k = 4 * q + e;
+                        const float x = k < nvk ? *reinterpret_cast<const float*>(
+                                                      sV + k * 128 + (((vt_dd >> 2) ^ (k & 7)) * 16))
+                                                : 0.f;
+                        hi[e] = x;
+                        lo[e] = tf32_lo(x);
+                    }
+                    const int pos = q ^ (d & 7);
+                    *reinterpret_cast<float4*>(vt + d * 128 + pos * 16) =
+                        make_float4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<float4*>(vt + kVtBytes + d * 128 + pos * 16) =
+                        make_float4(lo[0], lo[1], lo[2], lo[3]);
+                }
+                tc::fence_async_smem();
+                mbar_arrive(&ctl->cv_full[stage_of(n)]);
             }
         } else {
             // ------------------------------------------------------------ softmax warps
-            const int row = tid;  // query row, TMEM lane, and (for V^T) head dimension
+            const int row = tid;  // query row and TMEM lane
             const int qpos = first_pos + r0 + row;
             const uint32_t lane_off = uint32_t(warp * 32) << 16;
-            const int vt_atom = row >> 5;   // V atom holding dimension `row`
-            const int vt_dd = row & 31;     // dimension within the atom
-            float o[kHD];
-#pragma unroll
-            for (int j = 0; j < kHD; ++j) o[j] = 0.f;
-            float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
+            float m_run = -INFINITY, l_run = 0.f;
             bool ok = true;
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
@@ -354,88 +403,55 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 l_run = fmaf(l_run, alpha, ps);
                 m_run = m_new;
                 if (t > 0) {
-                    // previous tile's P.V: also frees the P and V^T buffers
+                    // previous tile's P.V is in O: P's TMEM columns are free, and O
+                    // can be rescaled to the new maximum before this tile's P.V
                     if (!wait_or_abort(&ctl->o_full, (n - 1) & 1u, ctl)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
+                    if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+                        for (int c = 0; c < kHD / 32; ++c) {
+                            float ov[32];
+                            tc::tmem_ld32(tO + c * 32u + lane_off, ov);
+                            tc::tmem_ld_wait();
 #pragma unroll
-                    for (int c = 0; c < kHD / 32; ++c) {
-                        float ov[32];
-                        tc::tmem_ld32(tO + c * 32u + lane_off, ov);
-                        tc::tmem_ld_wait();
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) o[c * 32 + j] = fmaf(o[c * 32 + j], alpha_prev, ov[j]);
-                    }
-                }
-                // P -> shared memory as tf32 hi / lo parts, 128B-swizzled K-major
-#pragma unroll
-                for (int c = 0; c < kKT / 4; ++c) {
-                    float hi[4], lo[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        hi[e] = tc::to_tf32(sc[4 * c + e]);
-                        lo[e] = tc::to_tf32(sc[4 * c + e] - hi[e]);
-                    }
-                    const int pos = c ^ (row & 7);
-                    *reinterpret_cast<float4*>(sP + row * 128 + pos * 16) =
-                        make_float4(hi[0], hi[1], hi[2], hi[3]);
-                    *reinterpret_cast<float4*>(sP + kPBytes + row * 128 + pos * 16) =
-                        make_float4(lo[0], lo[1], lo[2], lo[3]);
-                }
-                // V^T row `row` (tf32; zero past the visible keys)
-                if (!wait_or_abort(&ctl->kv_full[stage_of(n)], stage_parity(n), ctl)) {
-                    ok = false;
-                    break;
-                }
-                {
-                    const unsigned char* sV = sKV + stage_of(n) * kStageBytes + 2 * kKBytes +
-                                              vt_atom * kKVAtom + (vt_dd & 3) * 4;
-                    const int nvk = nk - kbase;
-#pragma unroll
-                    for (int c = 0; c < kKT / 4; ++c) {
-                        float hi[4], lo[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int k = 4 * c + e;
-                            const float x = *reinterpret_cast<const float*>(
-                                sV + k * 128 + (((vt_dd >> 2) ^ (k & 7)) * 16));
-                            hi[e] = k < nvk ? tc::to_tf32(x) : 0.f;
-                            lo[e] = k < nvk ? tc::to_tf32(x - hi[e]) : 0.f;
+                            for (int j = 0; j < 32; ++j) ov[j] *= alpha;
+                            tc::tmem_st32(tO + c * 32u + lane_off, ov);
                         }
-                        const int pos = c ^ (row & 7);
-                        *reinterpret_cast<float4*>(sVt + row * 128 + pos * 16) =
-                            make_float4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<float4*>(sVt + kVtBytes + row * 128 + pos * 16) =
-                            make_float4(lo[0], lo[1], lo[2], lo[3]);
                     }
                 }
-                tc::fence_async_smem();
+                // P -> this row's TMEM lane as tf32 hi / lo parts (A operand of O)
+                {
+                    float lo[kKT];
+#pragma unroll
+                    for (int j = 0; j < kKT; ++j) lo[j] = tf32_lo(sc[j]);
+                    tc::tmem_st32(tmem + kColPhi + lane_off, sc);
+                    tc::tmem_st32(tmem + kColPlo + lane_off, lo);
+                    tc::tmem_st_wait();
+                }
                 tc::fence_before_sync();
                 mbar_arrive(&ctl->p_full);
-                alpha_prev = alpha;
             }
             if (ok && ntiles > 0) {
                 const uint32_t n = n0 + ntiles - 1;
                 if (wait_or_abort(&ctl->o_full, n & 1u, ctl)) {
                     tc::fence_after_sync();
-#pragma unroll
+                    const float inv = 1.0f / fmaxf(l_run, 1e-12f);
+                    float4* op = reinterpret_cast<float4*>(p.out + int64_t(q0 + r0 + row) * g.row +
+                                                           int64_t(h) * kHD);
+#pragma unroll 1
                     for (int c = 0; c < kHD / 32; ++c) {
                         float ov[32];
                         tc::tmem_ld32(tO + c * 32u + lane_off, ov);
                         tc::tmem_ld_wait();
+                        if (row < nrows) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) o[c * 32 + j] = fmaf(o[c * 32 + j], alpha_prev, ov[j]);
-                    }
-                    if (row < nrows) {
-                        const float inv = 1.0f / fmaxf(l_run, 1e-12f);
-                        float4* op = reinterpret_cast<float4*>(p.out + int64_t(q0 + r0 + row) * g.row +
-                                                               int64_t(h) * kHD);
-#pragma unroll
-                        for (int c = 0; c < kHD / 4; ++c) {
-                            op[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv,
-                                                o[4 * c + 3] * inv);
+                            for (int j = 0; j < 8; ++j) {
+                                op[c * 8 + j] = make_float4(ov[4 * j] * inv, ov[4 * j + 1] * inv,
+                                                            ov[4 * j + 2] * inv, ov[4 * j + 3] * inv);
+                            }
                         }
                     }
                 }
@@ -447,7 +463,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
 
     // Teardown: on an abort, let this CTA's copies and MMAs finish (bounded)
     // before its shared memory and TMEM are released.
-    if (warp == 4 && lane == 0) {
+    if (warp == kProducerWarp && lane == 0) {
         for (uint32_t n = next_wait; n < next_load; ++n) {
             mbar_wait(&ctl->kv_full[stage_of(n)], stage_parity(n));
         }
@@ -458,7 +474,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == kProducerWarp) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, kTmemCols);
     }
