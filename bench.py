@@ -652,7 +652,7 @@ def serve_main(args):
     # The host library is loaded before torch so that its cuBLAS references bind
     # to the CUDA toolkit's cuBLAS it was linked against (which has the bf16x9
     # mode) rather than to the copy torch brings.
-    from nvllm.host import GEMM_BF16X9, GEMM_FP32, Engine, Generator, Model, host_lib
+    from nvllm.host import GEMM_BF16X9, GEMM_FP32, GEMM_TF32X3, Engine, Generator, Model, host_lib
     host_lib()
     import torch
     import nvllm
@@ -673,7 +673,7 @@ def serve_main(args):
     lay = nvllm.KVLayout(spec.num_blocks, spec.model["layers"], spec.block_size,
                          spec.model["heads"], spec.model["head_dim"])
     eng = Engine(lay, device=local, **spec.engine_limits())
-    gemm = GEMM_BF16X9 if args.gemm == "bf16x9" else GEMM_FP32
+    gemm = {"fp32": GEMM_FP32, "bf16x9": GEMM_BF16X9, "tf32x3": GEMM_TF32X3}[args.gemm]
     model = Model(spec.model, eng, gemm_math=gemm, graph_max_tokens=args.graph_max_tokens)
     precision = nvllm.PRECISION_TF32 if args.precision == "tf32" else nvllm.PRECISION_FP32
     estream = torch.cuda.ExternalStream(eng.stream(), device=dev)
@@ -792,8 +792,11 @@ def main() -> int:
     ap.add_argument("--workload", choices=["decode", "mixed", "longctx", "decode_small",
                                            "mixed_small", *SERVE_WORKLOADS],
                     default="decode")
-    ap.add_argument("--gemm", choices=["fp32", "bf16x9"], default="fp32",
-                    help="projection arithmetic of the serving workloads")
+    ap.add_argument("--gemm", choices=["fp32", "bf16x9", "tf32x3"], default=None,
+                    help="projection arithmetic of the serving workloads: cuBLAS FFMA, cuBLAS "
+                         "bf16x9, or the tcgen05 3xTF32 GEMM (rows > 32; FFMA below); default "
+                         "tf32x3 for serve, fp32 for the toy model (whose 128-wide "
+                         "projections give the tensor-core GEMM one to three tiles)")
     ap.add_argument("--graph-max-tokens", type=int, default=None,
                     help="serving: engine iterations of at most this many new tokens replay a "
                          "CUDA graph per padded bucket (0: eager; default 512 for the toy "
@@ -814,6 +817,8 @@ def main() -> int:
             args.steps = SERVE_DEFAULT_STEPS[args.workload]
         if args.graph_max_tokens is None:
             args.graph_max_tokens = 0 if args.workload == "serve" else 512
+        if args.gemm is None:
+            args.gemm = "tf32x3" if args.workload == "serve" else "fp32"
         return reference_serve_main(args) if args.impl == "reference" else serve_main(args)
     if args.steps is None:
         args.steps = 1000

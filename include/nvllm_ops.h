@@ -23,6 +23,10 @@ extern "C" {
 int nvllm_lcg_fill(float* out, int64_t rows, int64_t cols, int64_t ld, uint64_t stream_offset,
                    float scale, void* stream);
 
+/* out[c * rows + r] = in[r * cols + c]: out = in^T for a rows x cols row-major
+ * matrix (out of place). */
+int nvllm_transpose(const float* in, int64_t rows, int64_t cols, float* out, void* stream);
+
 /* out[t] = table[token_ids[t] % vocab] (src/model.cpp:161-166). */
 int nvllm_embedding_gather(float* out, const float* table, const int32_t* token_ids, int64_t n,
                            int64_t vocab, int64_t dim, void* stream);
@@ -51,6 +55,34 @@ int nvllm_gather_rows(float* out, const float* in, const int32_t* rows, int64_t 
 int nvllm_penalized_argmax(const float* logits, const int64_t* prev_tokens, int64_t rows,
                            int64_t vocab, float penalty, int32_t* sampled, float* margin,
                            int32_t* top_idx, float* top_val, int32_t top_k, void* stream);
+
+/* Dense fp32 GEMM on the tcgen05 tensor cores (3xTF32: W_hi X_hi + W_lo X_hi +
+ * W_hi X_lo, fp32 quality) for the projections of src/model.cpp:42-62:
+ *   C[t, c] = epi(sum_k x[t * lda + k] * wt[c * k + k'])   t < m, c < n
+ * i.e. x [m, k] row-major (row stride lda) times W = wt^T, with the weights
+ * stored transposed (wt [n, k] row-major). Column c of the product goes to
+ * outs[c / out_block][t * ldc + c % out_block] (n_outs = n / out_block <= 3:
+ * one output, or the Q/K/V split). n and out_block multiples of 128, k of 32,
+ * lda of 4; x and wt 16-byte aligned. When fewer output tiles than SMs exist
+ * (small m) K is split over CTAs and the partials, kept in `workspace`
+ * (nvllm_gemm_workspace_size bytes), are summed in a fixed order. The products
+ * accumulate on the tensor core in chunks of 128 of K, which are summed in fp32
+ * registers with round-to-nearest adds. */
+enum nvllm_gemm_epilogue {
+    NVLLM_GEMM_STORE = 0,      /* C = product */
+    NVLLM_GEMM_ACCUMULATE = 1, /* C += product (the residual adds) */
+    NVLLM_GEMM_SILU = 2        /* C = silu(product) (the FFN up projection) */
+};
+size_t nvllm_gemm_workspace_size(int64_t m, int64_t n, int64_t k);
+/* wt_lo NULL: wt holds W^T and every tile is split on chip; else wt = W_hi^T and
+ * wt_lo = W_lo^T as written by nvllm_tf32_split (static weights split once). */
+int nvllm_gemm_tf32x3(const float* x, int64_t lda, int64_t m, int64_t k, const float* wt,
+                      const float* wt_lo, int64_t n, float* const* outs, int32_t n_outs,
+                      int64_t out_block, int64_t ldc, int32_t epilogue, void* workspace,
+                      size_t workspace_bytes, void* stream);
+/* hi[i] = in[i] rounded to tf32 (nearest, in an fp32 container), lo[i] = in[i] - hi[i]
+ * (exact): the operand parts of nvllm_gemm_tf32x3. */
+int nvllm_tf32_split(const float* in, float* hi, float* lo, int64_t count, void* stream);
 
 #ifdef __cplusplus
 }

@@ -306,6 +306,23 @@ __global__ void penalized_argmax_kernel(const float* __restrict__ logits,
     }
 }
 
+// out[c * rows + r] = in[r * cols + c]: 32 x 32 tiles through shared memory
+// (padded rows: no bank conflicts), coalesced on both sides.
+__global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                 int64_t rows, int64_t cols) {
+    __shared__ float tile[32][33];
+    const int64_t r0 = int64_t(blockIdx.y) * 32, c0 = int64_t(blockIdx.x) * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[i][threadIdx.x] = in[r * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) out[c * rows + r] = tile[threadIdx.x][i];
+    }
+}
+
 }  // namespace
 }  // namespace nvllm
 
@@ -324,6 +341,19 @@ int nvllm_lcg_fill(float* out, int64_t rows, int64_t cols, int64_t ld, uint64_t 
     lcg_fill_kernel<<<grid_for(groups * 32, threads), threads, 0,
                       static_cast<cudaStream_t>(stream)>>>(out, rows, cols, ld, stream_offset,
                                                            scale);
+    return launch_status();
+}
+
+int nvllm_transpose(const float* in, int64_t rows, int64_t cols, float* out, void* stream) {
+    if (rows < 0 || cols < 0 || rows > (int64_t(1) << 36) / 32 || cols > (int64_t(1) << 36) / 32) {
+        return NVLLM_ERR_INVALID;
+    }
+    if (rows == 0 || cols == 0) return NVLLM_OK;
+    if (!in || !out || in == out) return NVLLM_ERR_INVALID;
+    const int64_t gy = (rows + 31) / 32, gx = (cols + 31) / 32;
+    if (gy > 65535 || gx > 2147483647) return NVLLM_ERR_INVALID;
+    transpose_kernel<<<dim3(unsigned(gx), unsigned(gy)), dim3(32, 8), 0,
+                       static_cast<cudaStream_t>(stream)>>>(in, out, rows, cols);
     return launch_status();
 }
 

@@ -84,7 +84,8 @@ constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, false);
 struct Control {
     uint64_t kv_full[kStages];   // TMA landed (transaction count)
     uint64_t cv_full[kStages];   // converters done: K_lo and V^T written (256 arrivals)
-    uint64_t pv_done[kStages];   // O of the stage's tile complete: stage reusable
+    uint64_t pv_done[kStages];   // S of the stage's tile complete: stage reusable (K read
+                                 // by S, V already turned into V^T by the converters)
     uint64_t vt_free[2];         // O complete: V^T buffer reusable
     uint64_t s_full[2];
     uint64_t p_full;             // P in TMEM, previous O folded (128 arrivals)
@@ -281,6 +282,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                         tc::mma_tf32_ts(ts, tmem + kColQhi + 8u * k, bhi, kIdescS, true);
                     }
                     tc::commit(&ctl->s_full[n & 1u]);
+                    tc::commit(&ctl->pv_done[stage_of(n)]);
                     issued_mma = true;
                 }
                 __syncwarp();
@@ -301,7 +303,6 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                         tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vhi, kIdescO, true);
                     }
                     tc::commit(&ctl->o_full);
-                    tc::commit(&ctl->pv_done[stage_of(n)]);
                     tc::commit(&ctl->vt_free[n & 1u]);
                 }
                 __syncwarp();

@@ -2,7 +2,9 @@
 
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <climits>
+#include <utility>
 #include <cmath>
 
 #include "../../include/nvllm_ops.h"
@@ -56,7 +58,9 @@ std::expected<std::unique_ptr<DeviceModel>, EngineError> DeviceModel::create(
         cfg.hidden != cfg.heads * cfg.head_dim || cfg.hidden > INT32_MAX ||
         cfg.ffn > INT32_MAX || L.num_layers != cfg.layers || L.num_heads != cfg.heads ||
         L.head_dim != cfg.head_dim || cfg.emb_scale < 0.0f || cfg.ffn_scale < 0.0f ||
-        cfg.gemm_math < 0 || cfg.gemm_math > 1 || cfg.graph_max_tokens < 0) {
+        cfg.gemm_math < 0 || cfg.gemm_math > 2 || cfg.graph_max_tokens < 0 ||
+        (cfg.gemm_math == 2 &&
+         (cfg.hidden % 128 != 0 || cfg.ffn % 128 != 0 || cfg.vocab % 128 != 0))) {
         return invalid();
     }
     std::unique_ptr<DeviceModel> m(new DeviceModel(cfg, eng));
@@ -112,6 +116,44 @@ std::expected<void, EngineError> DeviceModel::init() {
     NVLLM_OP_TRY(fill(D, V, emb_scale));  // LM head
     if (draw != w_floats_) return invalid();
 
+    if (cfg_.gemm_math == 2) {
+        // transposed, tf32-split copies of every [k, n] weight after the embedding
+        const std::size_t t_floats = w_floats_ - std::size_t(V * D);
+        NVLLM_CUDA_TRY(cudaMalloc(&d_wt_hi_, t_floats * sizeof(float)));
+        NVLLM_CUDA_TRY(cudaMalloc(&d_wt_lo_, t_floats * sizeof(float)));
+        float* scratch = nullptr;
+        NVLLM_CUDA_TRY(cudaMalloc(&scratch, std::size_t(std::max(D * V, D * F)) * sizeof(float)));
+        std::size_t off = std::size_t(V * D);
+        auto prep = [&](int64_t rows, int64_t cols) -> int {
+            int rc = nvllm_transpose(d_w_ + off, rows, cols, scratch, st);
+            const std::size_t t = off - std::size_t(V * D);
+            if (rc == NVLLM_OK) {
+                rc = nvllm_tf32_split(scratch, d_wt_hi_ + t, d_wt_lo_ + t, rows * cols, st);
+            }
+            off += std::size_t(rows * cols);
+            return rc;
+        };
+        int rc = NVLLM_OK;
+        for (int64_t l = 0; l < cfg_.layers && rc == NVLLM_OK; ++l) {
+            for (int i = 0; i < 4 && rc == NVLLM_OK; ++i) rc = prep(D, D);
+            if (rc == NVLLM_OK) rc = prep(D, F);
+            if (rc == NVLLM_OK) rc = prep(F, D);
+        }
+        if (rc == NVLLM_OK) rc = prep(D, V);
+        cudaStreamSynchronize(st);
+        cudaFree(scratch);
+        if (rc != NVLLM_OK) return kernel_error(rc);
+        // split-K partials: the largest any projection of more than 32 rows asks for
+        const int64_t tmax = eng_.config().max_tokens;
+        for (int64_t m = 33; m <= tmax; ++m) {
+            for (const auto& [k, n] : {std::pair{D, 3 * D}, std::pair{D, D}, std::pair{D, F},
+                                       std::pair{F, D}, std::pair{D, V}}) {
+                gemm_ws_bytes_ = std::max(gemm_ws_bytes_, nvllm_gemm_workspace_size(m, n, k));
+            }
+        }
+        if (gemm_ws_bytes_ > 0) NVLLM_CUDA_TRY(cudaMalloc(&d_gemm_ws_, gemm_ws_bytes_));
+    }
+
     const std::size_t act = std::size_t(T * D * 6 + T * F + S * D + S * V);
     NVLLM_CUDA_TRY(cudaMalloc(&d_act_, act * sizeof(float)));
     d_hidden_ = d_act_;
@@ -159,6 +201,9 @@ DeviceModel::~DeviceModel() {
     if (d_io_) cudaFree(d_io_);
     if (d_act_) cudaFree(d_act_);
     if (d_w_) cudaFree(d_w_);
+    if (d_wt_hi_) cudaFree(d_wt_hi_);
+    if (d_wt_lo_) cudaFree(d_wt_lo_);
+    if (d_gemm_ws_) cudaFree(d_gemm_ws_);
 }
 
 // Row-major C[m, n] = A[m, k] . W[k, n] + beta * C: the column-major product
@@ -170,6 +215,39 @@ std::expected<void, EngineError> DeviceModel::gemm(const float* a, const float* 
     NVLLM_BLAS_TRY(cublasSgemm(blas_, CUBLAS_OP_N, CUBLAS_OP_N, int(n), int(m), int(k), &one, w,
                                int(n), a, int(k), &beta, c, int(n)));
     return {};
+}
+
+std::expected<void, EngineError> DeviceModel::gemm_tc(const float* a, int64_t m, int64_t k,
+                                                      std::size_t w_off, int64_t n,
+                                                      float* const* outs, int32_t n_outs,
+                                                      int64_t out_block, int64_t ldc,
+                                                      int32_t epilogue) {
+    const std::size_t t = w_off - std::size_t(cfg_.vocab * cfg_.hidden);
+    NVLLM_OP_TRY(nvllm_gemm_tf32x3(a, k, m, k, d_wt_hi_ + t, d_wt_lo_ + t, n, outs, n_outs,
+                                   out_block, ldc, epilogue, d_gemm_ws_, gemm_ws_bytes_,
+                                   eng_.stream()));
+    return {};
+}
+
+// Launches of this library's kernels in one step: embedding, last-token gather
+// and sampler; per layer two RMSNorms, the KV write and the attention's plan,
+// decode and merge (+ prefill), and either the SiLU (cuBLAS projections) or the
+// four tcgen05 GEMMs (+ their split-K sums).
+uint64_t DeviceModel::step_launches(const MetadataLayout& step) const {
+    const int64_t D = cfg_.hidden, F = cfg_.ffn, V = cfg_.vocab;
+    const int64_t T = step.num_tokens, S = step.num_seqs;
+    uint64_t per_layer = 2 + 4 + (step.max_query_len > 1 ? 1 : 0);
+    if (use_tc(T)) {
+        for (const auto& [k, n] : {std::pair{D, 3 * D}, std::pair{D, D}, std::pair{D, F},
+                                   std::pair{F, D}}) {
+            per_layer += 1 + (nvllm_gemm_workspace_size(T, n, k) > 0 ? 1 : 0);
+        }
+    } else {
+        per_layer += 1;
+    }
+    uint64_t total = 3 + uint64_t(cfg_.layers) * per_layer;
+    if (use_tc(S)) total += 1 + (nvllm_gemm_workspace_size(S, V, D) > 0 ? 1 : 0);
+    return total;
 }
 
 std::expected<void, EngineError> DeviceModel::enqueue(std::span<const int64_t> token_ids,
@@ -201,9 +279,7 @@ std::expected<void, EngineError> DeviceModel::enqueue(std::span<const int64_t> t
     for (int64_t s = int64_t(prev_tokens.size()); s < S; ++s) h_prev[s] = 0;
     NVLLM_CUDA_TRY(cudaMemcpyAsync(d_io_, h_io_, io_in_bytes_, cudaMemcpyHostToDevice, st));
     NVLLM_CUDA_TRY(cudaEventRecord(io_done_, st));
-    // embedding, last-token gather, sampler; per layer two RMSNorms, SiLU, the
-    // KV write and the attention's plan, decode and merge (+ prefill)
-    launches_ += 3 + uint64_t(cfg_.layers) * (3 + 4 + (step.max_query_len > 1 ? 1 : 0));
+    launches_ += step_launches(step);
     h2d_bytes_ += io_in_bytes_ + step.bytes;
 
     if (!(step.padded && cfg_.graph_max_tokens > 0)) return body(step, precision, top_k);
@@ -244,27 +320,72 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
         const float* w_o = lw + 3 * D * D;
         const float* w_up = lw + 4 * D * D;
         const float* w_down = w_up + D * F;
+        const std::size_t l_off = std::size_t(V * D) + std::size_t(l) * layer_floats_;
+        float* q = d_qkv_;
+        float* k = d_qkv_ + T * D;
+        float* v = d_qkv_ + 2 * T * D;
         NVLLM_OP_TRY(nvllm_rms_norm(d_norm_, d_hidden_, nullptr, T, D, kRmsEps, st));
-        // Q, K, V = norm . {w_q, w_k, w_v} as one batched GEMM (src/model.cpp:184-186)
-        NVLLM_BLAS_TRY(cublasSgemmStridedBatched(blas_, CUBLAS_OP_N, CUBLAS_OP_N, int(D), int(T),
-                                                 int(D), &one, w_q, int(D), D * D, d_norm_,
-                                                 int(D), 0, &zero, d_qkv_, int(D), T * D, 3));
-        const float* q = d_qkv_;
-        const float* k = d_qkv_ + T * D;
-        const float* v = d_qkv_ + 2 * T * D;
+        // Q, K, V = norm . {w_q, w_k, w_v} (src/model.cpp:184-186): one GEMM over the
+        // stacked transposed weights with a three-way output, or one batched SGEMM
+        if (use_tc(T)) {
+            float* const outs[3] = {q, k, v};
+            if (auto r = gemm_tc(d_norm_, T, D, l_off, 3 * D, outs, 3, D, D, NVLLM_GEMM_STORE); !r) {
+                return r;
+            }
+        } else {
+            NVLLM_BLAS_TRY(cublasSgemmStridedBatched(blas_, CUBLAS_OP_N, CUBLAS_OP_N, int(D),
+                                                     int(T), int(D), &one, w_q, int(D), D * D,
+                                                     d_norm_, int(D), 0, &zero, d_qkv_, int(D),
+                                                     T * D, 3));
+        }
         if (auto r = eng_.attention_device(int32_t(l), q, k, v, d_attn_, precision); !r) return r;
         // hidden += attn . w_o (src/model.cpp:263-266)
-        if (auto r = gemm(d_attn_, w_o, d_hidden_, T, D, D, 1.0f); !r) return r;
+        if (use_tc(T)) {
+            float* const outs[1] = {d_hidden_};
+            if (auto r = gemm_tc(d_attn_, T, D, l_off + 3 * D * D, D, outs, 1, D, D,
+                                 NVLLM_GEMM_ACCUMULATE);
+                !r) {
+                return r;
+            }
+        } else if (auto r = gemm(d_attn_, w_o, d_hidden_, T, D, D, 1.0f); !r) {
+            return r;
+        }
         NVLLM_OP_TRY(nvllm_rms_norm(d_norm_, d_hidden_, nullptr, T, D, kRmsEps, st));
-        if (auto r = gemm(d_norm_, w_up, d_up_, T, D, F, 0.0f); !r) return r;
-        NVLLM_OP_TRY(nvllm_silu(d_up_, T * F, st));
-        // hidden += silu(up) . w_down (src/model.cpp:274-277)
-        if (auto r = gemm(d_up_, w_down, d_hidden_, T, F, D, 1.0f); !r) return r;
+        // up = silu(norm . w_up) (src/model.cpp:270-273)
+        if (use_tc(T)) {
+            float* const outs[1] = {d_up_};
+            if (auto r = gemm_tc(d_norm_, T, D, l_off + 4 * D * D, F, outs, 1, F, F,
+                                 NVLLM_GEMM_SILU);
+                !r) {
+                return r;
+            }
+        } else {
+            if (auto r = gemm(d_norm_, w_up, d_up_, T, D, F, 0.0f); !r) return r;
+            NVLLM_OP_TRY(nvllm_silu(d_up_, T * F, st));
+        }
+        // hidden += up . w_down (src/model.cpp:274-277)
+        if (use_tc(T)) {
+            float* const outs[1] = {d_hidden_};
+            if (auto r = gemm_tc(d_up_, T, F, l_off + 4 * D * D + D * F, D, outs, 1, D, D,
+                                 NVLLM_GEMM_ACCUMULATE);
+                !r) {
+                return r;
+            }
+        } else if (auto r = gemm(d_up_, w_down, d_hidden_, T, F, D, 1.0f); !r) {
+            return r;
+        }
     }
     const auto* last_idx = reinterpret_cast<const int32_t*>(eng_.device_metadata() + step.last_off);
     NVLLM_OP_TRY(nvllm_gather_rows(d_last_, d_hidden_, last_idx, S, T, D, st));
-    const float* lm = d_w_ + V * D + std::size_t(cfg_.layers) * layer_floats_;
-    if (auto r = gemm(d_last_, lm, d_logits_, S, D, V, 0.0f); !r) return r;
+    const std::size_t lm_off = std::size_t(V * D) + std::size_t(cfg_.layers) * layer_floats_;
+    if (use_tc(S)) {
+        float* const outs[1] = {d_logits_};
+        if (auto r = gemm_tc(d_last_, S, D, lm_off, V, outs, 1, V, V, NVLLM_GEMM_STORE); !r) {
+            return r;
+        }
+    } else if (auto r = gemm(d_last_, d_w_ + lm_off, d_logits_, S, D, V, 0.0f); !r) {
+        return r;
+    }
     NVLLM_OP_TRY(nvllm_penalized_argmax(d_logits_, d_prev_, S, V, kRepeatPenalty, d_sampled_,
                                         top_k > 0 ? d_margin_ : nullptr,
                                         top_k > 0 ? d_top_idx_ : nullptr,

@@ -13,10 +13,12 @@
 // adjacent), KV write + paged attention (the engine), W_o GEMM accumulating
 // into the residual, RMSNorm, up GEMM, SiLU, down GEMM accumulating into the
 // residual; then the last-token gather, the LM-head GEMM and the penalised
-// argmax. The projections are cuBLAS SGEMMs on fp32 data: FFMA on the CUDA
-// cores, or (gemm_math 1) cuBLAS's bf16x9 emulation of fp32 on the tensor
-// cores (each fp32 operand split into three bf16 terms, fp32 accumulation);
-// never TF32.
+// argmax. The projections run on fp32 data: cuBLAS SGEMMs (FFMA on the CUDA
+// cores, or with gemm_math 1 cuBLAS's bf16x9 emulation of fp32 on the tensor
+// cores), or with gemm_math 2 nvllm_gemm_tf32x3 (tcgen05, 3xTF32 at fp32
+// quality, weights kept transposed and pre-split into tf32 hi / lo parts) for
+// every projection of more than 32 rows, its epilogue doing the residual add
+// (W_o, down), the SiLU (up) and the Q/K/V split; never single-pass TF32.
 #pragma once
 
 #include <cublas_v2.h>
@@ -38,7 +40,9 @@ struct ModelConfig {
     int64_t vocab = 0, hidden = 0, layers = 0, heads = 0, head_dim = 0, ffn = 0;
     // weight scales of src/model.cpp:81-82; 0 = 1/sqrt(hidden), 1/sqrt(ffn)
     float emb_scale = 0.0f, ffn_scale = 0.0f;
-    // 0: fp32 FFMA; 1: fp32 emulated with bf16x9 on the tensor cores
+    // 0: fp32 FFMA (cuBLAS); 1: fp32 emulated with bf16x9 (cuBLAS); 2: this
+    // library's tcgen05 3xTF32 GEMM for projections of more than 32 rows (with
+    // the residual add, SiLU and Q/K/V split in its epilogue), cuBLAS FFMA below
     int32_t gemm_math = 0;
     // Steps of at most this many new tokens run as one CUDA graph per padded
     // (tokens, sequences) bucket, captured on first use (0: always eager).
@@ -96,6 +100,13 @@ private:
     std::expected<void, EngineError> init();
     std::expected<void, EngineError> gemm(const float* a, const float* w, float* c, int64_t m,
                                           int64_t k, int64_t n, float beta);
+    // the tcgen05 GEMM on the transposed hi / lo weights at draw offset w_off
+    std::expected<void, EngineError> gemm_tc(const float* a, int64_t m, int64_t k,
+                                             std::size_t w_off, int64_t n, float* const* outs,
+                                             int32_t n_outs, int64_t out_block, int64_t ldc,
+                                             int32_t epilogue);
+    bool use_tc(int64_t rows) const noexcept { return cfg_.gemm_math == 2 && rows > 32; }
+    uint64_t step_launches(const MetadataLayout& step) const;
     // the device work of one step (everything after the input upload)
     std::expected<void, EngineError> body(const MetadataLayout& step, int32_t precision,
                                           int32_t top_k);
@@ -105,6 +116,12 @@ private:
     cublasHandle_t blas_ = nullptr;
     float* d_w_ = nullptr;
     std::size_t w_floats_ = 0;
+    // gemm_math 2: every projection and the LM head transposed ([n, k]) and split
+    // into tf32 hi / lo parts, at their draw offsets minus the embedding's
+    float* d_wt_hi_ = nullptr;
+    float* d_wt_lo_ = nullptr;
+    void* d_gemm_ws_ = nullptr;
+    std::size_t gemm_ws_bytes_ = 0;
     std::size_t layer_floats_ = 0;
     // activations, sized for the engine's max_tokens (T) and max_seqs (S)
     float* d_act_ = nullptr;

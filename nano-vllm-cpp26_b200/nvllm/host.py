@@ -74,6 +74,7 @@ class ModelConfig(ctypes.Structure):
 
 GEMM_FP32 = 0
 GEMM_BF16X9 = 1
+GEMM_TF32X3 = 2
 
 
 _HOST: ctypes.CDLL | None = None

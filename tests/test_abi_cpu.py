@@ -147,3 +147,15 @@ def test_model_ops_validate_on_the_host(nvlib, nvmod):
     assert nvlib.nvllm_penalized_argmax(vp(256), vp(256), i64(1), i64(10), f32(1.5), vp(256),
                                         None, None, None, ctypes.c_int32(4),
                                         st) == nvmod.ERR_INVALID  # top-k outputs missing
+    # the tensor-core GEMM: shapes it does not tile are refused on the host
+    outs = (ctypes.c_void_p * 1)(256)
+    assert nvlib.nvllm_gemm_tf32x3(vp(256), i64(64), i64(4), i64(64), vp(256), None, i64(100), outs,
+                                   ctypes.c_int32(1), i64(100), i64(100), ctypes.c_int32(0),
+                                   None, ctypes.c_size_t(0), st) == nvmod.ERR_INVALID
+    assert nvlib.nvllm_gemm_tf32x3(vp(256), i64(40), i64(4), i64(40), vp(256), None, i64(128), outs,
+                                   ctypes.c_int32(1), i64(128), i64(128), ctypes.c_int32(3),
+                                   None, ctypes.c_size_t(0), st) == nvmod.ERR_INVALID
+    assert nvlib.nvllm_gemm_tf32x3(None, i64(64), i64(0), i64(64), None, None, i64(128), outs,
+                                   ctypes.c_int32(1), i64(128), i64(128), ctypes.c_int32(0),
+                                   None, ctypes.c_size_t(0), st) == nvmod.OK  # m = 0
+    assert nvlib.nvllm_gemm_workspace_size(i64(4), i64(100), i64(64)) == 0

@@ -14,7 +14,7 @@ from helpers import LOGIT_RTOL, load_trace, trace_requests
 pytestmark = pytest.mark.gpu
 
 
-def build(name, precision=0, graph_max_tokens=0):
+def build(name, precision=0, graph_max_tokens=0, gemm_math=0):
     import nvllm
     from nvllm.host import Engine, Generator, Model
     cfg, z, steps = load_trace(name)
@@ -26,21 +26,24 @@ def build(name, precision=0, graph_max_tokens=0):
     B = int(z["block_size"])
     eng = Engine(lay, max_seqs=max_batch, max_tokens=max(max_tokens, longest),
                  max_blocks_per_seq=(longest + B - 1) // B)
-    model = Model(cfg, eng, scales=z["scales"][:2], graph_max_tokens=graph_max_tokens)
+    model = Model(cfg, eng, scales=z["scales"][:2], graph_max_tokens=graph_max_tokens,
+                  gemm_math=gemm_math)
     gen = Generator(eng, model, max_batch, max_tokens, watermark, precision=precision)
     for i, (p, m) in enumerate(zip(prompts, max_new)):
         gen.add_request(i + 1, p, m)
     return cfg, z, steps, (eng, model, gen), prompts
 
 
+@pytest.mark.parametrize("gemm", [0, 2], ids=["ffma", "tcgen05"])
 @pytest.mark.parametrize("graphs", [0, 512], ids=["eager", "graphs"])
 @pytest.mark.parametrize("name", ["tokens_toy_seeded", "tokens_toy_bench", "tokens_wide"])
-def test_generator_reproduces_reference_run(name, graphs, tmp_path):
+def test_generator_reproduces_reference_run(name, graphs, gemm, tmp_path):
     """graphs 512: every step of at most 512 new tokens is padded to a
-    power-of-two bucket and replayed as that bucket's CUDA graph."""
+    power-of-two bucket and replayed as that bucket's CUDA graph; gemm 2: the
+    projections of more than 32 rows on the tcgen05 GEMM."""
     from nvllm.host import metrics_json
     from oracle.oracle import read_trace
-    cfg, z, steps, objs, prompts = build(name, graph_max_tokens=graphs)
+    cfg, z, steps, objs, prompts = build(name, graph_max_tokens=graphs, gemm_math=gemm)
     eng, model, gen = objs
     try:
         path = str(tmp_path / "run.trace")

@@ -211,6 +211,14 @@ def test_device_model_tf32_attention_wide():
     assert replay("tokens_wide", precision=1) > 0
 
 
+@pytest.mark.parametrize("name", ["tokens_toy_seeded", "tokens_toy_bench", "tokens_wide"])
+def test_device_model_tcgen05_gemms(name):
+    """Projections of more than 32 rows on nvllm_gemm_tf32x3 (3xTF32, fused
+    residual / SiLU / Q-K-V epilogues): the reference's tokens and logits."""
+    from nvllm.host import GEMM_TF32X3
+    assert replay(name, gemm_math=GEMM_TF32X3) > 0
+
+
 @pytest.mark.parametrize("name", ["tokens_toy_seeded", "tokens_wide"])
 def test_device_model_bf16x9_gemms(name):
     """Projections in cuBLAS's bf16x9 emulation of fp32 on the tensor cores:
