@@ -121,10 +121,12 @@ enum nvllm_gemm_math {
     NVLLM_GEMM_BF16X9 = 1, /* fp32 emulated on the tensor cores: each operand split into three
                               bf16 terms, products accumulated in fp32 (cuBLAS's bf16x9 mode;
                               NVLLM_ERR_UNSUPPORTED when the cuBLAS in the process lacks it) */
-    NVLLM_GEMM_TF32X3 = 2  /* nvllm_gemm_tf32x3 (tcgen05, 3xTF32, fp32 quality) for every
-                              projection of more than 32 rows, with the residual add, SiLU and
-                              Q/K/V split in its epilogue; FFMA below. hidden, ffn and vocab
-                              must be multiples of 128. */
+    NVLLM_GEMM_TF32X3 = 2  /* this library's kernels, fp32 quality: nvllm_gemm_tf32x3
+                              (tcgen05, 3xTF32) for every projection of more than 32 rows,
+                              nvllm_gemm_decode_tc (tcgen05, 3xTF32) for 17-32 rows and
+                              nvllm_gemm_skinny (FFMA) for at most 16, the LM head included,
+                              each with the residual add, SiLU and Q/K/V split in its epilogue.
+                              hidden, ffn and vocab must be multiples of 128. */
 };
 typedef struct nvllm_model_config {
     int64_t vocab, hidden, layers, heads, head_dim, ffn;

@@ -84,6 +84,33 @@ int nvllm_gemm_tf32x3(const float* x, int64_t lda, int64_t m, int64_t k, const f
  * (exact): the operand parts of nvllm_gemm_tf32x3. */
 int nvllm_tf32_split(const float* in, float* hi, float* lo, int64_t count, void* stream);
 
+/* Dense fp32 GEMM (FFMA) for projections of few rows, the decode steps of
+ * src/model.cpp:42-62, with the weights in the reference's row-major layout:
+ *   outs[b][t * ldc + c] = epi(sum_k x[t * lda + k] * w[b * w_batch_stride + k * ldw + c])
+ * for t < m <= 256, c < n, b < batch <= 3 (Q, K and V from one launch). lda and
+ * ldw multiples of 4, x and w 16-byte aligned; w_batch_stride >= k * ldw when
+ * batch > 1. K is split over CTAs when the columns alone do not fill the GPU;
+ * the partials, kept in `workspace` (nvllm_gemm_skinny_workspace_size bytes,
+ * 16-byte aligned), are summed in a fixed order, so results are reproducible
+ * run to run. */
+size_t nvllm_gemm_skinny_workspace_size(int64_t m, int64_t n, int64_t k, int32_t batch);
+int nvllm_gemm_skinny(const float* x, int64_t lda, int64_t m, int64_t k, const float* w,
+                      int64_t ldw, int64_t n, int32_t batch, int64_t w_batch_stride,
+                      float* const* outs, int64_t ldc, int32_t epilogue, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* The same product, arguments and rules as nvllm_gemm_skinny for m <= 32, on the
+ * tcgen05 tensor cores in 3xTF32 (fp32 quality): W streamed from HBM once and
+ * split into tf32 hi / lo parts on chip, accumulated in chunks of 128 of K that
+ * are summed in fp32 registers. K is dealt to persistent CTAs in equal ranges
+ * (stream-K); the pieces of output tiles that CTAs share, kept in `workspace`
+ * (nvllm_gemm_decode_tc_workspace_size bytes), are summed in a fixed order. */
+size_t nvllm_gemm_decode_tc_workspace_size(int64_t m, int64_t n, int64_t k, int32_t batch);
+int nvllm_gemm_decode_tc(const float* x, int64_t lda, int64_t m, int64_t k, const float* w,
+                         int64_t ldw, int64_t n, int32_t batch, int64_t w_batch_stride,
+                         float* const* outs, int64_t ldc, int32_t epilogue, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <tuple>
 #include <utility>
 #include <cmath>
 
@@ -151,6 +152,16 @@ std::expected<void, EngineError> DeviceModel::init() {
                 gemm_ws_bytes_ = std::max(gemm_ws_bytes_, nvllm_gemm_workspace_size(m, n, k));
             }
         }
+        // and what the decode-size GEMMs ask for at <= 32 rows
+        for (int64_t m = 1; m <= std::min<int64_t>(tmax, 32); ++m) {
+            for (const auto& [k, n, b] : {std::tuple{D, D, 3}, std::tuple{D, D, 1},
+                                          std::tuple{D, F, 1}, std::tuple{F, D, 1},
+                                          std::tuple{D, V, 1}}) {
+                gemm_ws_bytes_ = std::max(
+                    {gemm_ws_bytes_, nvllm_gemm_skinny_workspace_size(m, n, k, int32_t(b)),
+                     nvllm_gemm_decode_tc_workspace_size(m, n, k, int32_t(b))});
+            }
+        }
         if (gemm_ws_bytes_ > 0) NVLLM_CUDA_TRY(cudaMalloc(&d_gemm_ws_, gemm_ws_bytes_));
     }
 
@@ -229,10 +240,32 @@ std::expected<void, EngineError> DeviceModel::gemm_tc(const float* a, int64_t m,
     return {};
 }
 
+std::expected<void, EngineError> DeviceModel::gemm_small(const float* a, int64_t m, int64_t k,
+                                                         const float* w, int64_t n,
+                                                         int32_t batch, int64_t w_stride,
+                                                         float* const* outs, int32_t epilogue) {
+    if (use_decode_tc(m)) {
+        NVLLM_OP_TRY(nvllm_gemm_decode_tc(a, k, m, k, w, n, n, batch, w_stride, outs, n, epilogue,
+                                          d_gemm_ws_, gemm_ws_bytes_, eng_.stream()));
+    } else {
+        NVLLM_OP_TRY(nvllm_gemm_skinny(a, k, m, k, w, n, n, batch, w_stride, outs, n, epilogue,
+                                       d_gemm_ws_, gemm_ws_bytes_, eng_.stream()));
+    }
+    return {};
+}
+
+// The workspace of the decode-size GEMM that gemm_small picks for m rows (a
+// second, summing kernel runs when it is not 0).
+std::size_t DeviceModel::small_workspace(int64_t m, int64_t n, int64_t k, int32_t batch) const {
+    return use_decode_tc(m) ? nvllm_gemm_decode_tc_workspace_size(m, n, k, batch)
+                            : nvllm_gemm_skinny_workspace_size(m, n, k, batch);
+}
+
 // Launches of this library's kernels in one step: embedding, last-token gather
 // and sampler; per layer two RMSNorms, the KV write and the attention's plan,
 // decode and merge (+ prefill), and either the SiLU (cuBLAS projections) or the
-// four tcgen05 GEMMs (+ their split-K sums).
+// four tcgen05 / skinny GEMMs (+ their split-K sums); the LM head's own GEMM
+// (+ its split-K sum) unless cuBLAS runs it.
 uint64_t DeviceModel::step_launches(const MetadataLayout& step) const {
     const int64_t D = cfg_.hidden, F = cfg_.ffn, V = cfg_.vocab;
     const int64_t T = step.num_tokens, S = step.num_seqs;
@@ -242,11 +275,20 @@ uint64_t DeviceModel::step_launches(const MetadataLayout& step) const {
                                    std::pair{F, D}}) {
             per_layer += 1 + (nvllm_gemm_workspace_size(T, n, k) > 0 ? 1 : 0);
         }
+    } else if (use_small(T)) {
+        for (const auto& [k, n, b] : {std::tuple{D, D, 3}, std::tuple{D, D, 1},
+                                      std::tuple{D, F, 1}, std::tuple{F, D, 1}}) {
+            per_layer += 1 + (small_workspace(T, n, k, int32_t(b)) > 0 ? 1 : 0);
+        }
     } else {
         per_layer += 1;
     }
     uint64_t total = 3 + uint64_t(cfg_.layers) * per_layer;
-    if (use_tc(S)) total += 1 + (nvllm_gemm_workspace_size(S, V, D) > 0 ? 1 : 0);
+    if (use_tc(S)) {
+        total += 1 + (nvllm_gemm_workspace_size(S, V, D) > 0 ? 1 : 0);
+    } else if (use_small(S)) {
+        total += 1 + (small_workspace(S, V, D, 1) > 0 ? 1 : 0);
+    }
     return total;
 }
 
@@ -332,6 +374,11 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
             if (auto r = gemm_tc(d_norm_, T, D, l_off, 3 * D, outs, 3, D, D, NVLLM_GEMM_STORE); !r) {
                 return r;
             }
+        } else if (use_small(T)) {
+            float* const outs[3] = {q, k, v};
+            if (auto r = gemm_small(d_norm_, T, D, w_q, D, 3, D * D, outs, NVLLM_GEMM_STORE); !r) {
+                return r;
+            }
         } else {
             NVLLM_BLAS_TRY(cublasSgemmStridedBatched(blas_, CUBLAS_OP_N, CUBLAS_OP_N, int(D),
                                                      int(T), int(D), &one, w_q, int(D), D * D,
@@ -347,6 +394,11 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
                 !r) {
                 return r;
             }
+        } else if (use_small(T)) {
+            float* const outs[1] = {d_hidden_};
+            if (auto r = gemm_small(d_attn_, T, D, w_o, D, 1, 0, outs, NVLLM_GEMM_ACCUMULATE); !r) {
+                return r;
+            }
         } else if (auto r = gemm(d_attn_, w_o, d_hidden_, T, D, D, 1.0f); !r) {
             return r;
         }
@@ -357,6 +409,11 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
             if (auto r = gemm_tc(d_norm_, T, D, l_off + 4 * D * D, F, outs, 1, F, F,
                                  NVLLM_GEMM_SILU);
                 !r) {
+                return r;
+            }
+        } else if (use_small(T)) {
+            float* const outs[1] = {d_up_};
+            if (auto r = gemm_small(d_norm_, T, D, w_up, F, 1, 0, outs, NVLLM_GEMM_SILU); !r) {
                 return r;
             }
         } else {
@@ -371,6 +428,11 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
                 !r) {
                 return r;
             }
+        } else if (use_small(T)) {
+            float* const outs[1] = {d_hidden_};
+            if (auto r = gemm_small(d_up_, T, F, w_down, D, 1, 0, outs, NVLLM_GEMM_ACCUMULATE); !r) {
+                return r;
+            }
         } else if (auto r = gemm(d_up_, w_down, d_hidden_, T, F, D, 1.0f); !r) {
             return r;
         }
@@ -381,6 +443,11 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
     if (use_tc(S)) {
         float* const outs[1] = {d_logits_};
         if (auto r = gemm_tc(d_last_, S, D, lm_off, V, outs, 1, V, V, NVLLM_GEMM_STORE); !r) {
+            return r;
+        }
+    } else if (use_small(S)) {
+        float* const outs[1] = {d_logits_};
+        if (auto r = gemm_small(d_last_, S, D, d_w_ + lm_off, V, 1, 0, outs, NVLLM_GEMM_STORE); !r) {
             return r;
         }
     } else if (auto r = gemm(d_last_, d_w_ + lm_off, d_logits_, S, D, V, 0.0f); !r) {

@@ -105,7 +105,21 @@ private:
                                              std::size_t w_off, int64_t n, float* const* outs,
                                              int32_t n_outs, int64_t out_block, int64_t ldc,
                                              int32_t epilogue);
+    // nvllm_gemm_skinny (rows <= 16) or nvllm_gemm_decode_tc (17-32) on the
+    // row-major weights (batch matrices at stride w_stride)
+    std::expected<void, EngineError> gemm_small(const float* a, int64_t m, int64_t k,
+                                                const float* w, int64_t n, int32_t batch,
+                                                int64_t w_stride, float* const* outs,
+                                                int32_t epilogue);
+    bool use_small(int64_t rows) const noexcept { return use_skinny(rows) || use_decode_tc(rows); }
+    std::size_t small_workspace(int64_t m, int64_t n, int64_t k, int32_t batch) const;
     bool use_tc(int64_t rows) const noexcept { return cfg_.gemm_math == 2 && rows > 32; }
+    // decode-size projections (<= 32 rows): the FFMA skinny GEMM up to 16 rows,
+    // the tcgen05 decode GEMM above (measured crossover on the 4096-wide shapes)
+    bool use_skinny(int64_t rows) const noexcept { return cfg_.gemm_math == 2 && rows <= 16; }
+    bool use_decode_tc(int64_t rows) const noexcept {
+        return cfg_.gemm_math == 2 && rows > 16 && rows <= 32;
+    }
     uint64_t step_launches(const MetadataLayout& step) const;
     // the device work of one step (everything after the input upload)
     std::expected<void, EngineError> body(const MetadataLayout& step, int32_t precision,
