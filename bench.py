@@ -794,17 +794,20 @@ def main() -> int:
                     default="decode")
     ap.add_argument("--gemm", choices=["fp32", "bf16x9", "tf32x3"], default=None,
                     help="projection arithmetic of the serving workloads: cuBLAS FFMA, cuBLAS "
-                         "bf16x9, or the tcgen05 3xTF32 GEMM (rows > 32; FFMA below); default "
-                         "tf32x3 for serve, fp32 for the toy model (whose 128-wide "
-                         "projections give the tensor-core GEMM one to three tiles)")
+                         "bf16x9, or this library's GEMMs (tcgen05 3xTF32 above 32 rows and at "
+                         "17-32, FFMA at <= 16); default tf32x3 for serve, fp32 for the toy "
+                         "model (whose 128-wide projections give the tensor-core GEMMs one to "
+                         "three tiles)")
     ap.add_argument("--graph-max-tokens", type=int, default=None,
                     help="serving: engine iterations of at most this many new tokens replay a "
-                         "CUDA graph per padded bucket (0: eager; default 512 for the toy "
-                         "workloads, 0 for serve, whose cuBLAS GEMMs run slower on padded "
-                         "shapes than the launches they save)")
+                         "CUDA graph per padded bucket (0: eager; default 512, or 0 for serve "
+                         "with cuBLAS projections, which run slower on padded shapes than the "
+                         "launches a graph saves)")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32",
-                    help="prefill tile arithmetic (decode is always fp32)")
+    ap.add_argument("--precision", choices=["fp32", "tf32"], default=None,
+                    help="prefill tile arithmetic (decode is always fp32): fp32 FFMA, or tcgen05 "
+                         "3xTF32 (fp32 quality); default tf32 for a serving workload whose "
+                         "projections run on the tcgen05 GEMMs, else fp32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--head-split", action="store_true",
                     help="split the batch's heads over the ranks (long-context decode)")
@@ -815,13 +818,17 @@ def main() -> int:
     if args.workload in SERVE_WORKLOADS:
         if args.steps is None:
             args.steps = SERVE_DEFAULT_STEPS[args.workload]
-        if args.graph_max_tokens is None:
-            args.graph_max_tokens = 0 if args.workload == "serve" else 512
         if args.gemm is None:
             args.gemm = "tf32x3" if args.workload == "serve" else "fp32"
+        if args.graph_max_tokens is None:
+            args.graph_max_tokens = 0 if args.workload == "serve" and args.gemm != "tf32x3" else 512
+        if args.precision is None:
+            args.precision = "tf32" if args.gemm == "tf32x3" else "fp32"
         return reference_serve_main(args) if args.impl == "reference" else serve_main(args)
     if args.steps is None:
         args.steps = 1000
+    if args.precision is None:
+        args.precision = "fp32"
     from nvllm.workload import make_batch
     spec = make_batch(args.workload, seed=args.seed)
     if args.impl == "reference":

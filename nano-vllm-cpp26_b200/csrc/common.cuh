@@ -12,11 +12,31 @@ enum : uint32_t {
     kStatusBounds = 1u,    // block id / slot outside the arena (access skipped)
     kStatusTimeout = 2u,   // a bounded mbarrier wait gave up
     kStatusMetadata = 4u,  // cu_seqlens / context_lens inconsistent with the bounds
+    // which kernel's wait gave up (with kStatusTimeout)
+    kStatusInDecode = 1u << 8,
+    kStatusInPrefillTc = 1u << 9,
+    kStatusInGemmTf32x3 = 1u << 10,
+    kStatusInGemmSkinny = 1u << 11,
+    kStatusInGemmDecodeTc = 1u << 12,
+    kStatusInPrefill = 1u << 13,
 };
 
 extern __device__ uint32_t g_status;
+// Where the first bounded wait that gave up was: {site bits, where code (set by
+// the kernel: role, barrier, unit), block index, raw mbarrier word}; word 0 is 0
+// until then. Cleared with the status word.
+extern __device__ uint32_t g_timeout_info[4];
 
 __device__ __forceinline__ void raise_status(uint32_t bits) { atomicOr(&g_status, bits); }
+
+__device__ __forceinline__ void record_timeout(uint32_t site, uint32_t where, const uint64_t* bar) {
+    if (atomicCAS(&g_timeout_info[0], 0u, site | 1u) == 0u) {
+        g_timeout_info[1] = where;
+        g_timeout_info[2] = blockIdx.x;
+        g_timeout_info[3] = static_cast<uint32_t>(*reinterpret_cast<const volatile uint64_t*>(bar));
+        __threadfence();
+    }
+}
 
 // Geometry of the reference arena [num_blocks, L, B, H*hd] in floats.
 struct ArenaGeom {
@@ -79,15 +99,15 @@ __device__ __forceinline__ uint64_t global_ns() {
 // launch ends by itself.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-// Bounded wait: returns false (and raises kStatusTimeout) if the phase does
-// not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait: returns false (and raises kStatusTimeout | site) if the phase
+// does not complete within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
         if (global_ns() - t0 > kWaitLimitNs) {
-            raise_status(kStatusTimeout);
+            raise_status(kStatusTimeout | site);
             return false;
         }
     }

@@ -113,18 +113,27 @@ __host__ __device__ __forceinline__ int64_t owner(int64_t u, int64_t units, int6
     return c;
 }
 
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Control* ctl) {
+// where: role << 24 | barrier << 16 | unit, recorded if this wait gives up first
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Control* ctl,
+                                              uint32_t where = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*reinterpret_cast<volatile int32_t*>(&ctl->abort)) return false;
         if (global_ns() - t0 > kWaitLimitNs) {
-            raise_status(kStatusTimeout);
+            raise_status(kStatusTimeout | kStatusInGemmDecodeTc);
+            record_timeout(kStatusInGemmDecodeTc, where | (parity << 15), bar);
             atomicExch(&ctl->abort, 1);
             return false;
         }
     }
+}
+// roles and barriers of the where code
+enum : uint32_t { kWhoProducer = 1, kWhoIssuer = 2, kWhoConverter = 4 };
+enum : uint32_t { kBarFull = 1, kBarConv = 2, kBarEmpty = 3, kBarDFull = 4, kBarDFree = 5 };
+__device__ __forceinline__ uint32_t where_code(uint32_t who, uint32_t bar, uint32_t g) {
+    return (who << 24) | (bar << 16) | (g & 0x7fffu);
 }
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
@@ -208,7 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t g = 0; g < nu; ++g) {
                 const uint32_t s = g % kStages;
                 if (g >= uint32_t(kStages) &&
-                    !wait_or_abort(&ctl->empty[s], ((g / kStages) - 1) & 1u, ctl)) {
+                    !wait_or_abort(&ctl->empty[s], ((g / kStages) - 1) & 1u, ctl,
+                                   where_code(kWhoProducer, kBarEmpty, g))) {
                     break;
                 }
                 unsigned char* st = smem + s * kStageBytes;
@@ -224,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // copies in flight land before the CTA ends (bounded waits)
             for (uint32_t h = loaded > uint32_t(kStages) ? loaded - kStages : 0; h < loaded; ++h) {
-                mbar_wait(&ctl->full[h % kStages], (h / kStages) & 1u);
+                mbar_wait(&ctl->full[h % kStages], (h / kStages) & 1u, kStatusInGemmDecodeTc);
             }
         }
     } else if (warp == kMmaWarp0 || warp == kMmaWarp0 + 1) {
@@ -249,9 +259,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool chunk_first = ji % kChunk == 0;
                 const bool chunk_last = ji % kChunk == kChunk - 1 || jj + 2 >= len;
                 const uint32_t s = g % kStages, ab = g % kABufs, buf = q & 1u;
-                if (!wait_or_abort(&ctl->conv[s], (g / kStages) & 1u, ctl)) break;
+                if (!wait_or_abort(&ctl->conv[s], (g / kStages) & 1u, ctl,
+                                   where_code(kWhoIssuer + uint32_t(me), kBarConv, g))) {
+                    break;
+                }
                 if (chunk_first && q >= 2 &&
-                    !wait_or_abort(&ctl->d_free[me][buf], ((q >> 1) - 1) & 1u, ctl)) {
+                    !wait_or_abort(&ctl->d_free[me][buf], ((q >> 1) - 1) & 1u, ctl,
+                                   where_code(kWhoIssuer + uint32_t(me), kBarDFree, g))) {
                     break;
                 }
                 tc::fence_after_sync();
@@ -278,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // issued MMAs complete before the TMEM is freed (bounded wait)
             if (issued_mma) {
                 tc::commit(&ctl->drain[me]);
-                mbar_wait(&ctl->drain[me], 0);
+                mbar_wait(&ctl->drain[me], 0, kStatusInGemmDecodeTc);
             }
         }
     } else {
@@ -294,7 +308,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // which they end, a fixed order)
         auto fold = [&](int i) -> bool {
             const uint32_t q = qf[i], buf = q & 1u;
-            if (!wait_or_abort(&ctl->d_full[i][buf], (q >> 1) & 1u, ctl)) return false;
+            if (!wait_or_abort(&ctl->d_full[i][buf], (q >> 1) & 1u, ctl,
+                               where_code(kWhoConverter, kBarDFull, (uint32_t(i) << 14) | q))) {
+                return false;
+            }
             tc::fence_after_sync();
             float v[32];
             tc::tmem_ld32(tmem + kColD + uint32_t(i * 2 + int(buf)) * uint32_t(kBT) + lane_off, v);
@@ -370,9 +387,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // A buffer ab was last read by the MMAs of unit g - kABufs, whose
                 // completion is that of its stage
                 const uint32_t h = g - uint32_t(kABufs);
-                if (!wait_or_abort(&ctl->full[s], (g / kStages) & 1u, ctl) ||
+                if (!wait_or_abort(&ctl->full[s], (g / kStages) & 1u, ctl,
+                                   where_code(kWhoConverter + uint32_t(grp), kBarFull, g)) ||
                     (g >= uint32_t(kABufs) &&
-                     !wait_or_abort(&ctl->empty[h % kStages], (h / kStages) & 1u, ctl))) {
+                     !wait_or_abort(&ctl->empty[h % kStages], (h / kStages) & 1u, ctl,
+                                    where_code(kWhoConverter + uint32_t(grp), kBarEmpty, g)))) {
                     ok = false;
                     break;
                 }

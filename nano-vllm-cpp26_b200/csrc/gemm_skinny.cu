@@ -96,7 +96,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Co
         if (mbar_try_wait(bar, parity)) return true;
         if (*reinterpret_cast<volatile int32_t*>(&ctl->abort)) return false;
         if (global_ns() - t0 > kWaitLimitNs) {
-            raise_status(kStatusTimeout);
+            raise_status(kStatusTimeout | kStatusInGemmSkinny);
             atomicExch(&ctl->abort, 1);
             return false;
         }
@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(Layout<MP>::kThreads, MP <= 16 ? 3 : 2)
     // copies still in flight (only after an abort) land before the CTA ends
     if (issuer) {
         for (int h = max(0, issued - kStages); h < issued; ++h) {
-            mbar_wait(&ctl->full[h % kStages], uint32_t(h / kStages) & 1u);
+            mbar_wait(&ctl->full[h % kStages], uint32_t(h / kStages) & 1u, kStatusInGemmSkinny);
         }
     }
     __syncthreads();

@@ -100,7 +100,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Co
         if (mbar_try_wait(bar, parity)) return true;
         if (*reinterpret_cast<volatile int32_t*>(&ctl->abort)) return false;
         if (global_ns() - t0 > kWaitLimitNs) {
-            raise_status(kStatusTimeout);
+            raise_status(kStatusTimeout | kStatusInGemmTf32x3);
             atomicExch(&ctl->abort, 1);
             return false;
         }
@@ -249,10 +249,10 @@ gemm_kernel(const GemmParams p, const __grid_constant__ CUtensorMap wmap,
         }
         // teardown: copies in flight land, MMAs complete (bounded waits)
         if (lane == 0) {
-            for (uint32_t g = g_mma; g < g_load; ++g) mbar_wait(&ctl->kv_full[g % S], (g / S) & 1u);
+            for (uint32_t g = g_mma; g < g_load; ++g) mbar_wait(&ctl->kv_full[g % S], (g / S) & 1u, kStatusInGemmTf32x3);
             if (issued_mma) {
                 tc::commit(&ctl->drain);
-                mbar_wait(&ctl->drain, 0);
+                mbar_wait(&ctl->drain, 0, kStatusInGemmTf32x3);
             }
         }
     } else {

@@ -1,7 +1,9 @@
 // The extern "C" boundary of libnvllm.so (declared in include/nvllm.h):
 // argument validation, workspace carve-up and kernel dispatch.
+#include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/nvllm.h"
 #include "common.cuh"
@@ -256,6 +258,12 @@ int nvllm_paged_attention_head_split(const nvllm_head_split* hs, const float* qu
     return e == cudaSuccess ? NVLLM_OK : NVLLM_ERR_CUDA;
 }
 
+namespace {
+std::atomic<uint32_t> g_last_status{0};  // the last nonzero word nvllm_get_last_error cleared
+uint32_t g_last_timeout[4] = {0, 0, 0, 0};  // and the timeout record cleared with it
+std::mutex g_last_timeout_mu;
+}  // namespace
+
 int nvllm_get_last_error(void* stream) {
     if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) {
         return NVLLM_ERR_CUDA;
@@ -263,11 +271,31 @@ int nvllm_get_last_error(void* stream) {
     uint32_t v = 0;
     if (cudaMemcpyFromSymbol(&v, g_status, sizeof(v)) != cudaSuccess) return NVLLM_ERR_CUDA;
     if (v == 0) return NVLLM_OK;
+    g_last_status.store(v);
+    if (v & kStatusTimeout) {
+        uint32_t info[4] = {0, 0, 0, 0};
+        const uint32_t zeros[4] = {0, 0, 0, 0};
+        if (cudaMemcpyFromSymbol(info, g_timeout_info, sizeof(info)) != cudaSuccess ||
+            cudaMemcpyToSymbol(g_timeout_info, zeros, sizeof(zeros)) != cudaSuccess) {
+            return NVLLM_ERR_CUDA;
+        }
+        std::lock_guard<std::mutex> lk(g_last_timeout_mu);
+        std::memcpy(g_last_timeout, info, sizeof(info));
+    }
     const uint32_t zero = 0;
     if (cudaMemcpyToSymbol(g_status, &zero, sizeof(zero)) != cudaSuccess) return NVLLM_ERR_CUDA;
     if (v & kStatusTimeout) return NVLLM_ERR_TIMEOUT;
     if (v & kStatusBounds) return NVLLM_ERR_BOUNDS;
     return NVLLM_ERR_INVALID;
+}
+
+uint32_t nvllm_last_status_word(void) { return g_last_status.load(); }
+
+int nvllm_last_timeout_info(uint32_t* info) {
+    if (info == nullptr) return NVLLM_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_last_timeout_mu);
+    std::memcpy(info, g_last_timeout, sizeof(g_last_timeout));
+    return NVLLM_OK;
 }
 
 int nvllm_device_status_word(const uint32_t** word) {

@@ -40,6 +40,7 @@
 namespace nvllm {
 
 __device__ uint32_t g_status = 0;
+__device__ uint32_t g_timeout_info[4] = {0, 0, 0, 0};
 
 namespace {
 
@@ -285,9 +286,9 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const AttnParams p) 
         if (consumed == issued) break;
 
         const int stage = int(consumed % NS);
-        if (!mbar_wait(&bars[stage], (consumed / NS) & 1u)) {
+        if (!mbar_wait(&bars[stage], (consumed / NS) & 1u, kStatusInDecode)) {
             // let this warp's other copies land (bounded), then stop
-            for (uint32_t n = consumed + 1; n < issued; ++n) mbar_wait(&bars[n % NS], (n / NS) & 1u);
+            for (uint32_t n = consumed + 1; n < issued; ++n) mbar_wait(&bars[n % NS], (n / NS) & 1u, kStatusInDecode);
             return;
         }
         if (cc == 0) {
@@ -494,7 +495,7 @@ __global__ void flag_wait_kernel(const uint32_t* flag, uint32_t target) {
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
         if (int32_t(v - target) >= 0) return;
         if (global_ns() - t0 > kWaitLimitNs) {
-            raise_status(kStatusTimeout);
+            raise_status(kStatusTimeout | kStatusInDecode);
             return;
         }
         __nanosleep(200);

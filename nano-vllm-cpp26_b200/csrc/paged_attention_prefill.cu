@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_fp32_kernel(const 
             if (warp == 0 && t + 1 < ntiles) issue(t + 1);
             const uint32_t n = tile_seq + t;
             const int stage = int(n & 1u);
-            if (!mbar_wait(&bars[stage], (n >> 1) & 1u)) timed_out = true;
+            if (!mbar_wait(&bars[stage], (n >> 1) & 1u, kStatusInPrefill)) timed_out = true;
             if (__syncthreads_or(timed_out)) {
                 timed_out = true;
                 break;
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_fp32_kernel(const 
             // issued) land, bounded, before the CTA's shared memory is released.
             if (t + 1 < ntiles) {
                 const uint32_t n = tile_seq + t + 1;
-                mbar_wait(&bars[n & 1u], (n >> 1) & 1u);
+                mbar_wait(&bars[n & 1u], (n >> 1) & 1u, kStatusInPrefill);
             }
             return;
         }

@@ -105,7 +105,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Co
         if (mbar_try_wait(bar, parity)) return true;
         if (*reinterpret_cast<volatile int32_t*>(&ctl->abort)) return false;
         if (global_ns() - t0 > kWaitLimitNs) {
-            raise_status(kStatusTimeout);
+            raise_status(kStatusTimeout | kStatusInPrefillTc);
             atomicExch(&ctl->abort, 1);
             return false;
         }
@@ -466,11 +466,11 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     // before its shared memory and TMEM are released.
     if (warp == kProducerWarp && lane == 0) {
         for (uint32_t n = next_wait; n < next_load; ++n) {
-            mbar_wait(&ctl->kv_full[stage_of(n)], stage_parity(n));
+            mbar_wait(&ctl->kv_full[stage_of(n)], stage_parity(n), kStatusInPrefillTc);
         }
         if (issued_mma) {
             tc::commit(&ctl->drain);
-            mbar_wait(&ctl->drain, 0);
+            mbar_wait(&ctl->drain, 0, kStatusInPrefillTc);
         }
     }
     tc::fence_before_sync();

@@ -97,9 +97,15 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
                  : "memory");
 }
 
+// The tcgen05 ld / st / wait instructions below are .sync.aligned: every lane
+// of the warp executes them together. Each follows a __syncwarp(), so that a
+// warp whose lanes left a spin wait (an mbarrier poll) at different
+// iterations is converged again first.
+
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes (one row per thread).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     uint32_t r[32];
+    __syncwarp();
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -116,6 +122,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 }
 // Stores 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+    __syncwarp();
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
         "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -134,10 +141,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
         : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() {
+    __syncwarp();
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_ld_wait() {
+    __syncwarp();
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 

@@ -34,16 +34,20 @@ def build(name, precision=0, graph_max_tokens=0, gemm_math=0):
     return cfg, z, steps, (eng, model, gen), prompts
 
 
-@pytest.mark.parametrize("gemm", [0, 2], ids=["ffma", "tcgen05"])
+@pytest.mark.parametrize("gemm,precision", [(0, 0), (2, 0), (2, 1)],
+                         ids=["ffma", "tcgen05", "tcgen05-tf32attn"])
 @pytest.mark.parametrize("graphs", [0, 512], ids=["eager", "graphs"])
 @pytest.mark.parametrize("name", ["tokens_toy_seeded", "tokens_toy_bench", "tokens_wide"])
-def test_generator_reproduces_reference_run(name, graphs, gemm, tmp_path):
+def test_generator_reproduces_reference_run(name, graphs, gemm, precision, tmp_path):
     """graphs 512: every step of at most 512 new tokens is padded to a
-    power-of-two bucket and replayed as that bucket's CUDA graph; gemm 2: the
-    projections of more than 32 rows on the tcgen05 GEMM."""
+    power-of-two bucket and replayed as that bucket's CUDA graph; gemm 2: every
+    projection on this library's GEMMs (tcgen05 above 32 rows, the decode-size
+    kernels below); precision 1: the prefill attention tiles on the tcgen05
+    3xTF32 kernel where the geometry has it (the FFMA kernel elsewhere)."""
     from nvllm.host import metrics_json
     from oracle.oracle import read_trace
-    cfg, z, steps, objs, prompts = build(name, graph_max_tokens=graphs, gemm_math=gemm)
+    cfg, z, steps, objs, prompts = build(name, precision=precision, graph_max_tokens=graphs,
+                                         gemm_math=gemm)
     eng, model, gen = objs
     try:
         path = str(tmp_path / "run.trace")
