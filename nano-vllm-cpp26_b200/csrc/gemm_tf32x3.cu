@@ -48,10 +48,11 @@ namespace {
 
 constexpr int kBN = 128;  // output features per tile (MMA M, TMEM lanes)
 constexpr int kBK = 32;   // K columns per stage (one 128-byte swizzle atom)
-constexpr int kThreads = 256;
+constexpr int kThreads = 288;      // producer, 7 converter warps, MMA issuer
 constexpr int kConvThreads = 224;  // warps 1-7
 constexpr int kEpiThreads = 128;   // warps 4-7 (also converters)
 constexpr int kEpiWarp0 = 4;
+constexpr int kMmaWarp = 8;
 constexpr int kMaxSplits = 16;
 constexpr int kMaxOuts = 3;
 constexpr int kChunkSteps = 4;  // stages (of 32 K) per TMEM accumulation chunk
@@ -64,10 +65,13 @@ struct Cfg {
     static constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBBytes;  // W, W_lo, X, X_lo
     static constexpr uint32_t kOffBar = kStages * kStageBytes;
     static constexpr uint32_t kSmem = kOffBar + 256 + 1024;
-    static constexpr uint32_t kTmemCols = 2 * BT;  // two accumulators of BT columns
+    // two accumulators of BT columns (MMA targets) and the fp32 sum of the tile's
+    // folded chunks (BT columns)
+    static constexpr uint32_t kColSum = 2 * BT;
+    static constexpr uint32_t kTmemCols = BT <= 32 ? 128 : 512;
     static constexpr uint32_t kIdesc = tc::tf32_idesc(kBN, BT, false, false);
     static_assert(kSmem <= 227u * 1024u, "shared memory");
-    static_assert(kTmemCols >= 32 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation");
+    static_assert(kTmemCols >= 3 * BT && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation");
 };
 
 struct GemmParams {
@@ -172,54 +176,52 @@ gemm_kernel(const GemmParams p, const __grid_constant__ CUtensorMap wmap,
     const uint32_t tmem = ctl->tmem_base;
 
     if (warp == 0) {
-        // ------------------------------------------------------------------ producer
-        uint32_t g_mma = 0, g_load = 0;
-        bool issued_mma = false;
-        bool ok = true;
-        auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-            return __all_sync(0xffffffffu, wait_or_abort(bar, parity, ctl));
-        };
-        uint32_t q = 0;  // accumulation chunks issued
-        // the load of step g into ring slot g % S, once the MMAs of step g - S are done
-        auto load = [&](const Item& im, uint32_t g_first) -> bool {
-            const uint32_t g = g_load;
-            if (g >= uint32_t(S) && !wait_all(&ctl->st_free[g % S], ((g / S) - 1) & 1u)) return false;
-            if (lane == 0) {
-                unsigned char* st = stage_ptr(g);
-                mbar_arrive_expect_tx(&ctl->kv_full[g % S],
-                                      (p.w_split ? 2 : 1) * C::kABytes + C::kBBytes);
-                const int x = (im.step0 + int(g - g_first)) * kBK;
-                tc::tma_load_2d(st, &wmap, x, int(im.n0), &ctl->kv_full[g % S]);
-                if (p.w_split) {
-                    tc::tma_load_2d(st + C::kABytes, &wlomap, x, int(im.n0), &ctl->kv_full[g % S]);
+        // ------------------------------------------------- producer (TMA copies)
+        if (lane == 0) {
+            uint32_t g = 0;  // steps loaded (ring slot g % S)
+            bool ok = true;
+            for (int64_t it = blockIdx.x; ok && it < p.items; it += gridDim.x) {
+                const Item im = item_of(p, it, BT);
+                for (int s = 0; s < im.nsteps; ++s, ++g) {
+                    // the slot's previous step (g - S) has been read by its MMAs
+                    if (g >= uint32_t(S) &&
+                        !wait_or_abort(&ctl->st_free[g % S], ((g / S) - 1) & 1u, ctl)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* st = stage_ptr(g);
+                    mbar_arrive_expect_tx(&ctl->kv_full[g % S],
+                                          (p.w_split ? 2 : 1) * C::kABytes + C::kBBytes);
+                    const int x = (im.step0 + s) * kBK;
+                    tc::tma_load_2d(st, &wmap, x, int(im.n0), &ctl->kv_full[g % S]);
+                    if (p.w_split) {
+                        tc::tma_load_2d(st + C::kABytes, &wlomap, x, int(im.n0), &ctl->kv_full[g % S]);
+                    }
+                    tc::tma_load_2d(st + 2 * C::kABytes, &xmap, x, int(im.t0), &ctl->kv_full[g % S]);
                 }
-                tc::tma_load_2d(st + 2 * C::kABytes, &xmap, x, int(im.t0), &ctl->kv_full[g % S]);
             }
-            __syncwarp();
-            ++g_load;
-            return true;
-        };
-        for (int64_t it = blockIdx.x; ok && it < p.items; it += gridDim.x) {
-            const Item im = item_of(p, it, BT);
-            const uint32_t g_first = g_mma;
-            const uint32_t g_end = g_first + uint32_t(im.nsteps);
-            // S - 1 steps in flight ahead of the MMAs; the S-th slot is the one the
-            // MMAs are reading, so a refill never waits on the MMAs just issued
-            while (ok && g_load < g_end && g_load < g_mma + S - 1) ok = load(im, g_first);
-            for (int s = 0; ok && s < im.nsteps; ++s) {
-                const uint32_t g = g_mma;
-                if (!wait_all(&ctl->cv_full[g % S], (g / S) & 1u)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t buf = q & 1u;
-                const bool chunk_first = s % kChunkSteps == 0;
-                const bool chunk_last = s % kChunkSteps == kChunkSteps - 1 || s + 1 == im.nsteps;
-                if (chunk_first && q >= 2 && !wait_all(&ctl->d_free[buf], ((q >> 1) - 1) & 1u)) {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0) {
+            // copies in flight land before the CTA ends (bounded waits)
+            for (uint32_t h = g > uint32_t(S) ? g - S : 0; h < g; ++h) {
+                mbar_wait(&ctl->kv_full[h % S], (h / S) & 1u, kStatusInGemmTf32x3);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------------------------ MMAs
+        if (lane == 0) {
+            uint32_t g = 0, q = 0;  // steps issued, accumulation chunks issued
+            bool ok = true, issued_mma = false;
+            for (int64_t it = blockIdx.x; ok && it < p.items; it += gridDim.x) {
+                const Item im = item_of(p, it, BT);
+                for (int s = 0; s < im.nsteps; ++s, ++g) {
+                    const uint32_t buf = q & 1u;
+                    const bool chunk_first = s % kChunkSteps == 0;
+                    const bool chunk_last = s % kChunkSteps == kChunkSteps - 1 || s + 1 == im.nsteps;
+                    if (!wait_or_abort(&ctl->cv_full[g % S], (g / S) & 1u, ctl) ||
+                        (chunk_first && q >= 2 &&
+                         !wait_or_abort(&ctl->d_free[buf], ((q >> 1) - 1) & 1u, ctl))) {
+                        ok = false;
+                        break;
+                    }
                     tc::fence_after_sync();
                     const uint32_t a = smem_addr(stage_ptr(g));
                     const uint32_t alo = a + C::kABytes;
@@ -238,18 +240,14 @@ gemm_kernel(const GemmParams p, const __grid_constant__ CUtensorMap wmap,
                         tc::mma_tf32(d, da, db, C::kIdesc, true);
                     }
                     tc::commit(&ctl->st_free[g % S]);
-                    if (chunk_last) tc::commit(&ctl->d_full[buf]);
+                    if (chunk_last) {
+                        tc::commit(&ctl->d_full[buf]);
+                        ++q;
+                    }
                     issued_mma = true;
                 }
-                __syncwarp();
-                if (chunk_last) ++q;
-                ++g_mma;
-                while (ok && g_load < g_end && g_load < g_mma + S - 1) ok = load(im, g_first);
             }
-        }
-        // teardown: copies in flight land, MMAs complete (bounded waits)
-        if (lane == 0) {
-            for (uint32_t g = g_mma; g < g_load; ++g) mbar_wait(&ctl->kv_full[g % S], (g / S) & 1u, kStatusInGemmTf32x3);
+            // issued MMAs complete before the TMEM is freed (bounded wait)
             if (issued_mma) {
                 tc::commit(&ctl->drain);
                 mbar_wait(&ctl->drain, 0, kStatusInGemmTf32x3);
@@ -261,14 +259,85 @@ gemm_kernel(const GemmParams p, const __grid_constant__ CUtensorMap wmap,
         const bool drains = warp >= kEpiWarp0;
         const int e = tid - kEpiWarp0 * 32;  // TMEM lane = output feature within the tile
         const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+        const uint32_t sum = tmem + C::kColSum + lane_off;
+        // Chunks wait to be folded in the order they end: a chunk that ends at step
+        // g is folded into the tile's sum (in TMEM) once step g + 2 is converted, so
+        // that the wait on the chunk's MMAs never holds up the next conversions. At
+        // most two are pending (one chunk ends per step).
+        struct Pending {
+            int64_t n0, t0;
+            uint32_t step;
+            int32_t split;
+            bool first, last;  // the tile's first / last chunk
+        };
+        Pending pend[2];
+        int n_pend = 0;
+        uint32_t qf = 0;  // chunks folded
+        auto fold = [&](const Pending& pc) -> bool {
+            const uint32_t buf = qf & 1u;
+            if (!wait_or_abort(&ctl->d_full[buf], (qf >> 1) & 1u, ctl)) return false;
+            tc::fence_after_sync();
+            int64_t col = 0, ld = 0;
+            float* out = nullptr;
+            if (pc.last) {
+                col = pc.n0 + e;
+                if (p.splits > 1) {
+                    out = p.partial + int64_t(pc.split) * p.m * p.n + col;
+                    ld = p.n;
+                } else {
+                    out = p.outs[col / p.out_block] + (col % p.out_block);
+                    ld = p.ldc;
+                }
+            }
+#pragma unroll 1
+            for (int cc = 0; cc < BT / 32; ++cc) {
+                float v[32];
+                tc::tmem_ld32(tmem + buf * uint32_t(BT) + uint32_t(cc * 32) + lane_off, v);
+                tc::tmem_ld_wait();
+                if (!pc.first) {
+                    float a[32];
+                    tc::tmem_ld32(sum + uint32_t(cc * 32), a);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) v[jj] = a[jj] + v[jj];
+                }
+                if (!pc.last) {
+                    tc::tmem_st32(sum + uint32_t(cc * 32), v);
+                    continue;
+                }
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int64_t t = pc.t0 + cc * 32 + jj;
+                    if (t < p.m) {
+                        float* o = out + t * ld;
+                        if (p.splits > 1 || p.epilogue == NVLLM_GEMM_STORE) {
+                            *o = v[jj];
+                        } else if (p.epilogue == NVLLM_GEMM_ACCUMULATE) {
+                            *o += v[jj];
+                        } else {
+                            *o = silu(v[jj]);
+                        }
+                    }
+                }
+            }
+            if (!pc.last) tc::tmem_st_wait();
+            tc::fence_before_sync();
+            mbar_arrive(&ctl->d_free[buf]);
+            ++qf;
+            return true;
+        };
+        auto fold_pending = [&](uint32_t upto) -> bool {
+            while (n_pend > 0 && pend[0].step + 2 <= upto) {
+                if (!fold(pend[0])) return false;
+                pend[0] = pend[1];
+                --n_pend;
+            }
+            return true;
+        };
         uint32_t g = 0;  // stages converted
-        uint32_t q = 0;  // accumulation chunks drained
         bool ok = true;
         for (int64_t it = blockIdx.x; ok && it < p.items; it += gridDim.x) {
             const Item im = item_of(p, it, BT);
-            float acc[BT];
-#pragma unroll
-            for (int jj = 0; jj < BT; ++jj) acc[jj] = 0.f;
             for (int s = 0; s < im.nsteps; ++s, ++g) {
                 if (!wait_or_abort(&ctl->kv_full[g % S], (g / S) & 1u, ctl)) {
                     ok = false;
@@ -295,53 +364,19 @@ gemm_kernel(const GemmParams p, const __grid_constant__ CUtensorMap wmap,
                 }
                 tc::fence_async_smem();
                 mbar_arrive(&ctl->cv_full[g % S]);
-                const bool chunk_last = s % kChunkSteps == kChunkSteps - 1 || s + 1 == im.nsteps;
-                if (drains && chunk_last) {
-                    const uint32_t buf = q & 1u;
-                    if (!wait_or_abort(&ctl->d_full[buf], (q >> 1) & 1u, ctl)) {
-                        ok = false;
-                        break;
-                    }
-                    tc::fence_after_sync();
-#pragma unroll
-                    for (int cc = 0; cc < BT / 32; ++cc) {
-                        float v[32];
-                        tc::tmem_ld32(tmem + buf * uint32_t(BT) + uint32_t(cc * 32) + lane_off, v);
-                        tc::tmem_ld_wait();
-#pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) acc[cc * 32 + jj] += v[jj];
-                    }
-                    tc::fence_before_sync();
-                    mbar_arrive(&ctl->d_free[buf]);
-                    ++q;
+                if (!drains) continue;
+                if (!fold_pending(g)) {
+                    ok = false;
+                    break;
                 }
-            }
-            if (!ok || !drains) continue;
-            const int64_t col = im.n0 + e;
-            float* out = nullptr;
-            int64_t ld = 0;
-            if (p.splits > 1) {
-                out = p.partial + int64_t(im.split) * p.m * p.n + col;
-                ld = p.n;
-            } else {
-                out = p.outs[col / p.out_block] + (col % p.out_block);
-                ld = p.ldc;
-            }
-#pragma unroll
-            for (int jj = 0; jj < BT; ++jj) {
-                const int64_t t = im.t0 + jj;
-                if (t < p.m) {
-                    float* o = out + t * ld;
-                    if (p.splits > 1 || p.epilogue == NVLLM_GEMM_STORE) {
-                        *o = acc[jj];
-                    } else if (p.epilogue == NVLLM_GEMM_ACCUMULATE) {
-                        *o += acc[jj];
-                    } else {
-                        *o = silu(acc[jj]);
-                    }
+                const bool chunk_last = s % kChunkSteps == kChunkSteps - 1 || s + 1 == im.nsteps;
+                if (chunk_last) {
+                    pend[n_pend++] = Pending{im.n0, im.t0, g, im.split, s < kChunkSteps,
+                                             s + 1 == im.nsteps};
                 }
             }
         }
+        if (drains && ok) fold_pending(g + 2);
     }
     tc::fence_before_sync();
     __syncthreads();
