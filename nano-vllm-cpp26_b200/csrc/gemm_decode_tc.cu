@@ -16,8 +16,8 @@
 // TMEM columns):
 //   warp 8, lane 0: the TMA copies into an 8-stage ring (W tile 32 x 128 fp32,
 //     no swizzle; X tile 32 rows x 32 fp32, 128-byte swizzle; no multicast);
-//   warps 9 and 10, lane 0: the 12 MMAs of a stage, alternate stages each into
-//     its own accumulators (a single issuing thread leaves the tensor core idle
+//   warps 9-10, lane 0: the 12 MMAs of a stage, alternate stages each into its
+//     own accumulators (a single issuing thread leaves the tensor core idle
 //     around each of its mbarrier waits and commits), never waiting on an MMA;
 //   warps 0-7: converters in two groups of four that take alternate stages.
 //     Lane r of warp w owns output feature 32 (w % 4) + r: it reads column r
@@ -60,21 +60,26 @@ constexpr int kChunk = 4;      // an issuer's stages per TMEM accumulation chunk
 constexpr int kABufs = 4;      // A operand buffers in TMEM (units converted ahead)
 constexpr int kGroupThreads = 128;  // one converter group: a warp per TMEM lane quarter
 constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp0 = 9;   // warps 9 and 10 issue the MMAs of alternate stages
-constexpr int kThreads = 352;  // two converter groups, producer, two MMA issuers
+constexpr int kIssuers = 2;    // MMA-issuing warps: the CTA's unit g to issuer g % 2
+constexpr int kMmaWarp0 = 9;   // warps 9-10
+constexpr int kThreads = 32 * (kMmaWarp0 + kIssuers);  // converters, producer, issuers
 constexpr int kMaxBatch = 3;
 constexpr int kMinUnits = 8;   // stages a CTA handles at least
 constexpr uint32_t kWBytes = kStageK * kTileN * 4;  // 16 KB
 constexpr uint32_t kXBytes = kBT * kStageK * 4;     // 4 KB
 constexpr uint32_t kStageBytes = kWBytes + 2 * kXBytes;  // W, X (hi in place), X lo
 // TMEM: four A buffers (hi 32 + lo 32 columns each) and two accumulators (32
-// columns each) for each of the two MMA issuers
+// columns each) for each MMA issuer
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColA = 0;
 constexpr uint32_t kColD = kABufs * 64;
 constexpr uint32_t kIdesc = tc::tf32_idesc(kTileN, kBT, false, false);
 constexpr uint32_t kSmem = kStages * kStageBytes + 512 + 1024;
 static_assert(kSmem <= 227u * 1024u, "shared memory");
+// every ring slot (and every A buffer) belongs to one issuer: units g and g + kStages
+// (g + kABufs) go to the same issuer
+static_assert(kStages % kIssuers == 0 && kABufs % kIssuers == 0, "issuer assignment");
+static_assert(kABufs * 64 + kIssuers * 2 * kBT <= kTmemCols, "TMEM columns");
 
 struct DecodeParams {
     int64_t m, n, k, ldc;
@@ -91,9 +96,9 @@ struct Control {
     uint64_t full[kStages];    // TMA landed (transaction bytes)
     uint64_t conv[kStages];    // A in TMEM, X split (kGroupThreads arrivals)
     uint64_t empty[kStages];   // the stage's MMAs completed
-    uint64_t d_full[2][2];     // [issuer][buffer] accumulation chunk complete
-    uint64_t d_free[2][2];     // chunk folded into registers (kGroupThreads arrivals)
-    uint64_t drain[2];
+    uint64_t d_full[kIssuers][2];  // [issuer][buffer] accumulation chunk complete
+    uint64_t d_free[kIssuers][2];  // chunk folded into registers (kGroupThreads arrivals)
+    uint64_t drain[kIssuers];
     uint32_t tmem_base;
     int32_t abort;
 };
@@ -190,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&ctl->conv[i], kGroupThreads);
             mbar_init(&ctl->empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kIssuers; ++i) {
             for (int b = 0; b < 2; ++b) {
                 mbar_init(&ctl->d_full[i][b], 1);
                 mbar_init(&ctl->d_free[i][b], kGroupThreads);
@@ -237,11 +242,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait(&ctl->full[h % kStages], (h / kStages) & 1u, kStatusInGemmDecodeTc);
             }
         }
-    } else if (warp == kMmaWarp0 || warp == kMmaWarp0 + 1) {
+    } else if (warp >= kMmaWarp0 && warp < kMmaWarp0 + kIssuers) {
         // ------------------------------------------------------------------ MMAs
-        // issuer i takes the stages j of each segment with j % 2 == i, into its own
-        // accumulators: two threads keep the tensor core busy between the waits
-        // and commits that each of them makes
+        // issuer i takes the CTA's units g with g % kIssuers == i, into its own
+        // accumulators: the threads keep the tensor core busy between the waits
+        // and commits that each of them makes. Assigning by g (not by the position
+        // within a tile's segment) gives every ring slot one issuer, which waits on
+        // that slot's barrier phases in order; an issuer waiting on a slot another
+        // issuer still has to consume could see the phase before its own as done.
         const int me = warp - kMmaWarp0;
         if (lane == 0) {
             uint32_t q = 0;  // this issuer's accumulation chunks
@@ -254,10 +262,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     len = min(p.spt - stage, int(nu - g));
                 }
                 const int jj = j++;
-                if ((jj & 1) != me) continue;
-                const int ji = jj >> 1;  // this issuer's stage within the segment
-                const bool chunk_first = ji % kChunk == 0;
-                const bool chunk_last = ji % kChunk == kChunk - 1 || jj + 2 >= len;
+                if (int(g % kIssuers) != me) continue;
+                // chunks: windows of kIssuers * kChunk units of the segment, kChunk
+                // of them this issuer's
+                const int w = jj % (kIssuers * kChunk);
+                const bool chunk_first = w < kIssuers;
+                const bool chunk_last = w >= kIssuers * (kChunk - 1) || jj + kIssuers >= len;
                 const uint32_t s = g % kStages, ab = g % kABufs, buf = q & 1u;
                 if (!wait_or_abort(&ctl->conv[s], (g / kStages) & 1u, ctl,
                                    where_code(kWhoIssuer + uint32_t(me), kBarConv, g))) {
@@ -303,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float acc[kBT];
 #pragma unroll
         for (int t = 0; t < kBT; ++t) acc[t] = 0.f;
-        uint32_t qf[2] = {0, 0};  // chunks folded, per issuer (group 0)
+        uint32_t qf[kIssuers] = {};  // chunks folded, per issuer (group 0)
         // folds issuer i's next chunk into acc (chunks are folded in the order in
         // which they end, a fixed order)
         auto fold = [&](int i) -> bool {
@@ -380,8 +390,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const int jj = j++;
             const bool seg_end = jj + 1 == len;
-            // the same chunk rule as the issuers: issuer jj % 2, its stage jj / 2
-            const bool chunk_last = (jj >> 1) % kChunk == kChunk - 1 || jj + 2 >= len;
+            // the same chunk rule as the issuers (issuer g % kIssuers)
+            const bool chunk_last =
+                jj % (kIssuers * kChunk) >= kIssuers * (kChunk - 1) || jj + kIssuers >= len;
             if (int(g % 2) == grp) {
                 const uint32_t s = g % kStages, ab = g % kABufs;
                 // A buffer ab was last read by the MMAs of unit g - kABufs, whose
@@ -421,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
             }
-            if (chunk_last) pend[n_pend++] = Pending{tile, g, jj & 1, seg_end};
+            if (chunk_last) pend[n_pend++] = Pending{tile, g, int(g % kIssuers), seg_end};
         }
         if (grp == 0 && ok) fold_pending(nu + 2);
     }
