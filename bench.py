@@ -782,6 +782,145 @@ def serve_main(args):
     return 0
 
 
+HEADMODEL_METRIC = "long-context decode tokens/s in the model (heads split over the GPUs)"
+
+
+def headmodel_main(args):
+    """Long-context decode inside the 4096-wide model with its heads split over
+    the ranks (nvllm_model head_ranks = N): 4 requests of 32768 prompt tokens
+    are prefilled through the generator (not timed), then `steps` decode
+    iterations (4 new tokens each, every rank computing the same tokens) are
+    timed with CUDA events on the engine's stream, max over ranks. Strong
+    scaling: the work per step is fixed, each rank streams heads / N of the KV
+    and a 1 / N slice of W_q, W_k, W_v; W_o, the FFN and the LM head are
+    replicated."""
+    from nvllm.host import GEMM_TF32X3, Engine, Generator, Model, host_lib
+    host_lib()
+    import torch
+    import nvllm
+    from nvllm.headsplit import ModelHeads
+    from nvllm.serving import make_serve, serve_config
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    nvllm.lib()
+    spec = make_serve("longctx_model", seed=args.seed)
+    m = spec.model
+    lay = nvllm.KVLayout(spec.num_blocks, m["layers"], spec.block_size, m["heads"] // world,
+                         m["head_dim"])
+    limits = spec.engine_limits()
+    eng = Engine(lay, device=local, **limits)
+    model = Model(m, eng, gemm_math=GEMM_TF32X3, head_ranks=world)
+    heads = None
+    if world > 1:
+        heads = ModelHeads(dist, limits["max_tokens"], m["hidden"], dev)
+        heads.attach(model)
+    precision = nvllm.PRECISION_TF32 if args.precision == "tf32" else nvllm.PRECISION_FP32
+    gen = Generator(eng, model, spec.max_batch, spec.max_tokens_per_step, spec.watermark,
+                    precision=precision)
+    for i, (p_, n_) in enumerate(zip(spec.prompts, spec.max_new)):
+        gen.add_request(i + 1, p_, n_)
+    estream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+    n_seq = len(spec.prompts)
+    # prefill (a whole prompt per iteration), until an iteration is pure decode
+    while True:
+        s = gen.step()
+        if s["scheduled_tokens"] == n_seq and s["batch_size"] == n_seq:
+            break
+    for _ in range(args.warmup):
+        gen.step()
+    m0 = gen.metrics()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(local).start()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(estream)
+    for _ in range(args.steps):
+        gen.step()
+    e1.record(estream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    elapsed = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    clocks = sampler.stop()
+    m1 = gen.metrics()
+    status = nvllm.get_last_error(eng.stream())
+    if status != nvllm.OK:
+        raise RuntimeError(f"device status {nvllm.status_string(status)}")
+    tokens = m1.total_tokens_generated - m0.total_tokens_generated
+    assert tokens == n_seq * args.steps, tokens
+    # bytes a rank streams per decode iteration: its heads' KV of every layer
+    # (the context grows by one token a step) and the weights it reads
+    D, F, V, Lyr = m["hidden"], m["ffn"], m["vocab"], m["layers"]
+    ctx = len(spec.prompts[0]) + args.warmup + args.steps // 2
+    kv = n_seq * ctx * Lyr * 2 * (D // world) * 4
+    w = Lyr * (3 * D * (D // world) + D * D + 2 * D * F) * 4 + D * V * 4
+    per_step = elapsed / args.steps
+    hbm = measured_peaks().get("hbm_gbs") or 6650.0
+    achieved = (kv + w) / per_step / 1e9
+    line = {
+        "metric": HEADMODEL_METRIC, "value": tokens / elapsed, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded prompts; LCG weights of the reference model)",
+        "config": {**serve_config(spec), "gemm": "tf32x3", "prefill_precision": args.precision,
+                   "parallelism": f"heads split x{world}" if world > 1 else "one GPU",
+                   "context_tokens": ctx,
+                   "l2": "KV and weights (>= 7 GB a step) far above L2; no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_source": "measured (copy)",
+                     "kernel": "whole decode iteration (KV of this rank's heads + weights)",
+                     "kv_bytes_per_step": kv, "weight_bytes_per_step": w, "traffic": None},
+        "e2e": {"value": tokens / elapsed, "unit": UNIT,
+                "h2d_bytes_per_step": (m1.h2d_bytes - m0.h2d_bytes) // args.steps,
+                "d2h_bytes_per_step": (m1.d2h_bytes - m0.d2h_bytes) // args.steps,
+                "path": "libnvllm_host generator C ABI (nvllm_generator_step): metadata and "
+                        "token ids up, sampled ids down every iteration"},
+        "gpu_launches": m1.kernel_launches - m0.kernel_launches,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = {
+            "value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+            "sample": "not timed: the reference's CPU path needs about an hour to prefill "
+                      "4 x 32768 tokens of this model (29 prefill tok/s measured on the "
+                      "4096-wide model); its attention alone at this shape is the longctx "
+                      "workload's cpu_baseline"}
+    gen.close()
+    torch.cuda.synchronize(dev)
+    if heads is not None:
+        barrier()
+        heads.close(dist)
+    model.close()
+    eng.close()
+    if rank == 0:
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -790,7 +929,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["nvllm", "reference"], default="nvllm")
     ap.add_argument("--workload", choices=["decode", "mixed", "longctx", "decode_small",
-                                           "mixed_small", *SERVE_WORKLOADS],
+                                           "mixed_small", "longctx_model", *SERVE_WORKLOADS],
                     default="decode")
     ap.add_argument("--gemm", choices=["fp32", "bf16x9", "tf32x3"], default=None,
                     help="projection arithmetic of the serving workloads: cuBLAS FFMA, cuBLAS "
@@ -815,6 +954,18 @@ def main() -> int:
     if args.warmup < 3:
         log("warm-up raised to 3 steps")
         args.warmup = 3
+    if args.workload == "longctx_model":
+        if args.steps is None:
+            args.steps = 32
+        if args.precision is None:
+            args.precision = "tf32"
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "the reference's CPU path needs about an hour to prefill "
+                                  "4 x 32768 tokens of the 4096-wide model"}))
+            return 0
+        return headmodel_main(args)
     if args.workload in SERVE_WORKLOADS:
         if args.steps is None:
             args.steps = SERVE_DEFAULT_STEPS[args.workload]

@@ -171,10 +171,10 @@ int nvllm_device_status_word(const uint32_t** word);
 
 /* The raw status word that the last nvllm_get_last_error call (in this process)
  * found nonzero and cleared: bit 1 NVLLM_ERR_TIMEOUT, bit 0 NVLLM_ERR_BOUNDS, bit
- * 2 inconsistent metadata; with a timeout, bits 8-13 name the kernel whose
+ * 2 inconsistent metadata; with a timeout, bits 8-14 name the kernel whose
  * bounded wait gave up (8 decode attention, 9 tensor-core prefill, 10
  * nvllm_gemm_tf32x3, 11 nvllm_gemm_skinny, 12 nvllm_gemm_decode_tc, 13 fp32
- * prefill). 0 if none was seen. */
+ * prefill, 14 nvllm_head_gather). 0 if none was seen. */
 uint32_t nvllm_last_status_word(void);
 
 /* With that word, where the first bounded wait that gave up was: info[0] its

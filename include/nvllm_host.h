@@ -136,10 +136,31 @@ typedef struct nvllm_model_config {
      * every step of at most this many new tokens to power-of-two buckets) run
      * as one CUDA graph per bucket, captured on first use. 0: always eager. */
     int32_t graph_max_tokens;
+    /* Head parallelism over this many GPUs, one process each (<= 8; 0 or 1:
+     * single GPU): the engine holds heads / head_ranks heads (layout num_heads),
+     * QKV runs for this rank's heads only, nvllm_head_gather collects every
+     * rank's attention rows before W_o, and W_o, the FFN and the LM head run
+     * replicated, so that every rank samples the same tokens. Needs
+     * nvllm_model_set_head_group before the first forward and graph_max_tokens
+     * 0; with gemm_math 2, hidden / head_ranks a multiple of 128. No
+     * counterpart in the reference (one CPU process). */
+    int32_t head_ranks;
 } nvllm_model_config;
 
 int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvllm_model** out);
 void nvllm_model_destroy(nvllm_model* m);
+
+/* The peers of a head-parallel model (head_ranks = world): this rank, the gather
+ * buffers of every rank by epoch parity (outs[p][r]: [engine max_tokens, hidden]
+ * fp32 on rank r, e.g. nvllm_ipc_alloc'd and opened in every process) and every
+ * rank's flag word (uint32, starting at 0). Every rank must run the same steps
+ * (the same requests and scheduler settings). */
+typedef struct nvllm_model_head_group {
+    int32_t rank, world;
+    float* outs[2][NVLLM_MAX_RANKS];
+    uint32_t* flags[NVLLM_MAX_RANKS];
+} nvllm_model_head_group;
+int nvllm_model_set_head_group(nvllm_model* m, const nvllm_model_head_group* g);
 /* forward_batch over the step begun with nvllm_engine_begin_step: token_ids =
  * the uncomputed tokens of every sequence in batch order (num_tokens of them,
  * taken modulo the vocabulary), prev_tokens[s] = sequence s's last token.

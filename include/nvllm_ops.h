@@ -10,6 +10,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "nvllm.h"
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -110,6 +112,18 @@ int nvllm_gemm_decode_tc(const float* x, int64_t lda, int64_t m, int64_t k, cons
                          int64_t ldw, int64_t n, int32_t batch, int64_t w_batch_stride,
                          float* const* outs, int64_t ldc, int32_t epilogue, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/* Head-parallel layers: rank hs->rank's attention rows local [rows, local_cols]
+ * (its heads, head-major) stored into every rank's full-width buffer
+ * hs->outs[q] ([rows, world * local_cols], columns rank * local_cols + c) over
+ * NVLink, then one increment of every rank's flag; the call returns its stream
+ * once this rank's flag reached epoch * world (every rank's rows landed here;
+ * bounded wait, 2 s, then NVLLM_ERR_TIMEOUT in nvllm_get_last_error). epoch
+ * counts this group's calls from 1, flags start at 0; alternate two sets of
+ * output buffers by epoch parity so that a rank never overwrites rows a slower
+ * rank still reads. No counterpart in the reference (one CPU process). */
+int nvllm_head_gather(const float* local, int64_t rows, int64_t local_cols,
+                      const nvllm_head_split* hs, void* stream);
 
 #ifdef __cplusplus
 }

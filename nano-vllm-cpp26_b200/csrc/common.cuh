@@ -19,6 +19,7 @@ enum : uint32_t {
     kStatusInGemmSkinny = 1u << 11,
     kStatusInGemmDecodeTc = 1u << 12,
     kStatusInPrefill = 1u << 13,
+    kStatusInHeadGather = 1u << 14,
 };
 
 extern __device__ uint32_t g_status;

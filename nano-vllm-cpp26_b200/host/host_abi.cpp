@@ -311,7 +311,8 @@ int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvll
                           .heads = cfg->heads, .head_dim = cfg->head_dim, .ffn = cfg->ffn,
                           .emb_scale = cfg->emb_scale, .ffn_scale = cfg->ffn_scale,
                           .gemm_math = cfg->gemm_math,
-                          .graph_max_tokens = cfg->graph_max_tokens};
+                          .graph_max_tokens = cfg->graph_max_tokens,
+                          .head_ranks = cfg->head_ranks > 0 ? cfg->head_ranks : 1};
     auto r = nvllm::DeviceModel::create(mc, *engine->impl);
     if (!r) return engine_status(r.error());
     auto* m = new (std::nothrow) nvllm_model{std::move(*r)};
@@ -321,6 +322,22 @@ int nvllm_model_create(const nvllm_model_config* cfg, nvllm_engine* engine, nvll
 }
 
 void nvllm_model_destroy(nvllm_model* m) { delete m; }
+
+int nvllm_model_set_head_group(nvllm_model* m, const nvllm_model_head_group* g) {
+    if (m == nullptr || g == nullptr || g->world < 1 || g->world > NVLLM_MAX_RANKS) {
+        return NVLLM_ERR_INVALID;
+    }
+    nvllm::HeadGroup hg;
+    hg.rank = g->rank;
+    hg.world = g->world;
+    for (int r = 0; r < g->world; ++r) {
+        hg.outs[0][r] = g->outs[0][r];
+        hg.outs[1][r] = g->outs[1][r];
+        hg.flags[r] = g->flags[r];
+    }
+    const auto r = m->impl->set_head_group(hg);
+    return r ? NVLLM_OK : engine_status(r.error());
+}
 
 int nvllm_model_forward(nvllm_model* m, const int64_t* token_ids, int64_t num_tokens,
                         const int64_t* prev_tokens, int64_t num_seqs, int64_t* sampled,

@@ -57,7 +57,11 @@ std::expected<std::unique_ptr<DeviceModel>, EngineError> DeviceModel::create(
     if (cfg.vocab <= 0 || cfg.vocab > INT32_MAX || cfg.hidden <= 0 || cfg.layers <= 0 ||
         cfg.heads <= 0 || cfg.head_dim <= 0 || cfg.ffn <= 0 ||
         cfg.hidden != cfg.heads * cfg.head_dim || cfg.hidden > INT32_MAX ||
-        cfg.ffn > INT32_MAX || L.num_layers != cfg.layers || L.num_heads != cfg.heads ||
+        cfg.ffn > INT32_MAX || cfg.head_ranks < 1 || cfg.head_ranks > 8 ||
+        cfg.heads % cfg.head_ranks != 0 || L.num_layers != cfg.layers ||
+        L.num_heads * cfg.head_ranks != cfg.heads ||
+        (cfg.head_ranks > 1 && cfg.graph_max_tokens != 0) ||
+        (cfg.head_ranks > 1 && cfg.gemm_math == 2 && (cfg.hidden / cfg.head_ranks) % 128 != 0) ||
         L.head_dim != cfg.head_dim || cfg.emb_scale < 0.0f || cfg.ffn_scale < 0.0f ||
         cfg.gemm_math < 0 || cfg.gemm_math > 2 || cfg.graph_max_tokens < 0 ||
         (cfg.gemm_math == 2 &&
@@ -148,7 +152,8 @@ std::expected<void, EngineError> DeviceModel::init() {
         const int64_t tmax = eng_.config().max_tokens;
         for (int64_t m = 33; m <= tmax; ++m) {
             for (const auto& [k, n] : {std::pair{D, 3 * D}, std::pair{D, D}, std::pair{D, F},
-                                       std::pair{F, D}, std::pair{D, V}}) {
+                                       std::pair{F, D}, std::pair{D, V},
+                                       std::pair{D, D / cfg_.head_ranks}}) {
                 gemm_ws_bytes_ = std::max(gemm_ws_bytes_, nvllm_gemm_workspace_size(m, n, k));
             }
         }
@@ -156,7 +161,8 @@ std::expected<void, EngineError> DeviceModel::init() {
         for (int64_t m = 1; m <= std::min<int64_t>(tmax, 32); ++m) {
             for (const auto& [k, n, b] : {std::tuple{D, D, 3}, std::tuple{D, D, 1},
                                           std::tuple{D, F, 1}, std::tuple{F, D, 1},
-                                          std::tuple{D, V, 1}}) {
+                                          std::tuple{D, V, 1},
+                                          std::tuple{D, D / cfg_.head_ranks, 3}}) {
                 gemm_ws_bytes_ = std::max(
                     {gemm_ws_bytes_, nvllm_gemm_skinny_workspace_size(m, n, k, int32_t(b)),
                      nvllm_gemm_decode_tc_workspace_size(m, n, k, int32_t(b))});
@@ -241,16 +247,30 @@ std::expected<void, EngineError> DeviceModel::gemm_tc(const float* a, int64_t m,
 }
 
 std::expected<void, EngineError> DeviceModel::gemm_small(const float* a, int64_t m, int64_t k,
-                                                         const float* w, int64_t n,
+                                                         const float* w, int64_t ldw, int64_t n,
                                                          int32_t batch, int64_t w_stride,
                                                          float* const* outs, int32_t epilogue) {
     if (use_decode_tc(m)) {
-        NVLLM_OP_TRY(nvllm_gemm_decode_tc(a, k, m, k, w, n, n, batch, w_stride, outs, n, epilogue,
-                                          d_gemm_ws_, gemm_ws_bytes_, eng_.stream()));
+        NVLLM_OP_TRY(nvllm_gemm_decode_tc(a, k, m, k, w, ldw, n, batch, w_stride, outs, n,
+                                          epilogue, d_gemm_ws_, gemm_ws_bytes_, eng_.stream()));
     } else {
-        NVLLM_OP_TRY(nvllm_gemm_skinny(a, k, m, k, w, n, n, batch, w_stride, outs, n, epilogue,
+        NVLLM_OP_TRY(nvllm_gemm_skinny(a, k, m, k, w, ldw, n, batch, w_stride, outs, n, epilogue,
                                        d_gemm_ws_, gemm_ws_bytes_, eng_.stream()));
     }
+    return {};
+}
+
+std::expected<void, EngineError> DeviceModel::set_head_group(const HeadGroup& g) {
+    if (g.world != cfg_.head_ranks || g.world < 2 || g.rank < 0 || g.rank >= g.world) {
+        return invalid();
+    }
+    for (int r = 0; r < g.world; ++r) {
+        if (g.outs[0][r] == nullptr || g.outs[1][r] == nullptr || g.flags[r] == nullptr) {
+            return invalid();
+        }
+    }
+    heads_ = g;
+    have_heads_ = true;
     return {};
 }
 
@@ -269,14 +289,18 @@ std::size_t DeviceModel::small_workspace(int64_t m, int64_t n, int64_t k, int32_
 uint64_t DeviceModel::step_launches(const MetadataLayout& step) const {
     const int64_t D = cfg_.hidden, F = cfg_.ffn, V = cfg_.vocab;
     const int64_t T = step.num_tokens, S = step.num_seqs;
-    uint64_t per_layer = 2 + 4 + (step.max_query_len > 1 ? 1 : 0);
+    const int64_t hr = cfg_.head_ranks, Dl = D / hr;
+    // + the head gather (copy, signal, wait) of a head-parallel model
+    uint64_t per_layer = 2 + 4 + (step.max_query_len > 1 ? 1 : 0) + (hr > 1 ? 3 : 0);
     if (use_tc(T)) {
-        for (const auto& [k, n] : {std::pair{D, 3 * D}, std::pair{D, D}, std::pair{D, F},
-                                   std::pair{F, D}}) {
+        // Q, K, V as one three-way GEMM, or one GEMM each for a head slice
+        const int64_t qkv_calls = hr > 1 ? 3 : 1, qkv_n = hr > 1 ? Dl : 3 * D;
+        per_layer += uint64_t(qkv_calls) * (1 + (nvllm_gemm_workspace_size(T, qkv_n, D) > 0 ? 1 : 0));
+        for (const auto& [k, n] : {std::pair{D, D}, std::pair{D, F}, std::pair{F, D}}) {
             per_layer += 1 + (nvllm_gemm_workspace_size(T, n, k) > 0 ? 1 : 0);
         }
     } else if (use_small(T)) {
-        for (const auto& [k, n, b] : {std::tuple{D, D, 3}, std::tuple{D, D, 1},
+        for (const auto& [k, n, b] : {std::tuple{D, Dl, 3}, std::tuple{D, D, 1},
                                       std::tuple{D, F, 1}, std::tuple{F, D, 1}}) {
             per_layer += 1 + (small_workspace(T, n, k, int32_t(b)) > 0 ? 1 : 0);
         }
@@ -352,6 +376,8 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
                                                    int32_t top_k) {
     const int64_t V = cfg_.vocab, D = cfg_.hidden, F = cfg_.ffn;
     const int64_t T = step.num_tokens, S = step.num_seqs;
+    const int32_t hr = cfg_.head_ranks;
+    if (hr > 1 && !have_heads_) return invalid();
     cudaStream_t st = eng_.stream();
     const float* emb = d_w_;
     NVLLM_OP_TRY(nvllm_embedding_gather(d_hidden_, emb, d_tokens_, T, V, D, st));
@@ -363,43 +389,76 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
         const float* w_up = lw + 4 * D * D;
         const float* w_down = w_up + D * F;
         const std::size_t l_off = std::size_t(V * D) + std::size_t(l) * layer_floats_;
+        // this rank's heads: columns [c0, c0 + Dl) of w_q, w_k, w_v (all of them on
+        // one GPU)
+        const int64_t Dl = D / hr, c0 = int64_t(heads_.rank) * Dl;
         float* q = d_qkv_;
-        float* k = d_qkv_ + T * D;
-        float* v = d_qkv_ + 2 * T * D;
+        float* k = d_qkv_ + T * Dl;
+        float* v = d_qkv_ + 2 * T * Dl;
         NVLLM_OP_TRY(nvllm_rms_norm(d_norm_, d_hidden_, nullptr, T, D, kRmsEps, st));
         // Q, K, V = norm . {w_q, w_k, w_v} (src/model.cpp:184-186): one GEMM over the
-        // stacked transposed weights with a three-way output, or one batched SGEMM
+        // stacked transposed weights with a three-way output (one per matrix for a
+        // head slice), or one batched GEMM
         if (use_tc(T)) {
-            float* const outs[3] = {q, k, v};
-            if (auto r = gemm_tc(d_norm_, T, D, l_off, 3 * D, outs, 3, D, D, NVLLM_GEMM_STORE); !r) {
-                return r;
+            if (hr == 1) {
+                float* const outs[3] = {q, k, v};
+                if (auto r = gemm_tc(d_norm_, T, D, l_off, 3 * D, outs, 3, D, D, NVLLM_GEMM_STORE);
+                    !r) {
+                    return r;
+                }
+            } else {
+                float* const qkv[3] = {q, k, v};
+                for (int i = 0; i < 3; ++i) {
+                    float* const outs[1] = {qkv[i]};
+                    // rows c0.. of the transposed matrix i
+                    if (auto r = gemm_tc(d_norm_, T, D, l_off + std::size_t(i * D * D + c0 * D), Dl,
+                                         outs, 1, Dl, Dl, NVLLM_GEMM_STORE);
+                        !r) {
+                        return r;
+                    }
+                }
             }
         } else if (use_small(T)) {
             float* const outs[3] = {q, k, v};
-            if (auto r = gemm_small(d_norm_, T, D, w_q, D, 3, D * D, outs, NVLLM_GEMM_STORE); !r) {
+            if (auto r = gemm_small(d_norm_, T, D, w_q + c0, D, Dl, 3, D * D, outs, NVLLM_GEMM_STORE);
+                !r) {
                 return r;
             }
         } else {
-            NVLLM_BLAS_TRY(cublasSgemmStridedBatched(blas_, CUBLAS_OP_N, CUBLAS_OP_N, int(D),
-                                                     int(T), int(D), &one, w_q, int(D), D * D,
-                                                     d_norm_, int(D), 0, &zero, d_qkv_, int(D),
-                                                     T * D, 3));
+            NVLLM_BLAS_TRY(cublasSgemmStridedBatched(blas_, CUBLAS_OP_N, CUBLAS_OP_N, int(Dl),
+                                                     int(T), int(D), &one, w_q + c0, int(D), D * D,
+                                                     d_norm_, int(D), 0, &zero, d_qkv_, int(Dl),
+                                                     T * Dl, 3));
         }
         if (auto r = eng_.attention_device(int32_t(l), q, k, v, d_attn_, precision); !r) return r;
+        const float* attn = d_attn_;
+        if (hr > 1) {
+            // every rank's heads into the gather buffer of this call's epoch parity
+            nvllm_head_split hs{};
+            hs.rank = heads_.rank;
+            hs.world = hr;
+            hs.epoch = ++gather_epoch_;
+            for (int r = 0; r < hr; ++r) {
+                hs.outs[r] = heads_.outs[hs.epoch & 1u][r];
+                hs.flags[r] = heads_.flags[r];
+            }
+            NVLLM_OP_TRY(nvllm_head_gather(d_attn_, T, Dl, &hs, st));
+            attn = heads_.outs[hs.epoch & 1u][heads_.rank];
+        }
         // hidden += attn . w_o (src/model.cpp:263-266)
         if (use_tc(T)) {
             float* const outs[1] = {d_hidden_};
-            if (auto r = gemm_tc(d_attn_, T, D, l_off + 3 * D * D, D, outs, 1, D, D,
+            if (auto r = gemm_tc(attn, T, D, l_off + 3 * D * D, D, outs, 1, D, D,
                                  NVLLM_GEMM_ACCUMULATE);
                 !r) {
                 return r;
             }
         } else if (use_small(T)) {
             float* const outs[1] = {d_hidden_};
-            if (auto r = gemm_small(d_attn_, T, D, w_o, D, 1, 0, outs, NVLLM_GEMM_ACCUMULATE); !r) {
+            if (auto r = gemm_small(attn, T, D, w_o, D, D, 1, 0, outs, NVLLM_GEMM_ACCUMULATE); !r) {
                 return r;
             }
-        } else if (auto r = gemm(d_attn_, w_o, d_hidden_, T, D, D, 1.0f); !r) {
+        } else if (auto r = gemm(attn, w_o, d_hidden_, T, D, D, 1.0f); !r) {
             return r;
         }
         NVLLM_OP_TRY(nvllm_rms_norm(d_norm_, d_hidden_, nullptr, T, D, kRmsEps, st));
@@ -413,7 +472,7 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
             }
         } else if (use_small(T)) {
             float* const outs[1] = {d_up_};
-            if (auto r = gemm_small(d_norm_, T, D, w_up, F, 1, 0, outs, NVLLM_GEMM_SILU); !r) {
+            if (auto r = gemm_small(d_norm_, T, D, w_up, F, F, 1, 0, outs, NVLLM_GEMM_SILU); !r) {
                 return r;
             }
         } else {
@@ -430,7 +489,7 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
             }
         } else if (use_small(T)) {
             float* const outs[1] = {d_hidden_};
-            if (auto r = gemm_small(d_up_, T, F, w_down, D, 1, 0, outs, NVLLM_GEMM_ACCUMULATE); !r) {
+            if (auto r = gemm_small(d_up_, T, F, w_down, D, D, 1, 0, outs, NVLLM_GEMM_ACCUMULATE); !r) {
                 return r;
             }
         } else if (auto r = gemm(d_up_, w_down, d_hidden_, T, F, D, 1.0f); !r) {
@@ -447,7 +506,7 @@ std::expected<void, EngineError> DeviceModel::body(const MetadataLayout& step, i
         }
     } else if (use_small(S)) {
         float* const outs[1] = {d_logits_};
-        if (auto r = gemm_small(d_last_, S, D, d_w_ + lm_off, V, 1, 0, outs, NVLLM_GEMM_STORE); !r) {
+        if (auto r = gemm_small(d_last_, S, D, d_w_ + lm_off, V, V, 1, 0, outs, NVLLM_GEMM_STORE); !r) {
             return r;
         }
     } else if (auto r = gemm(d_last_, d_w_ + lm_off, d_logits_, S, D, V, 0.0f); !r) {

@@ -47,6 +47,19 @@ struct ModelConfig {
     // Steps of at most this many new tokens run as one CUDA graph per padded
     // (tokens, sequences) bucket, captured on first use (0: always eager).
     int32_t graph_max_tokens = 0;
+    // Head parallelism over this many GPUs (one process each, <= 8): the engine
+    // holds heads / head_ranks heads; set_head_group() names this rank and the
+    // gather buffers before the first forward. 1: single GPU.
+    int32_t head_ranks = 1;
+};
+
+// The peers of a head-parallel model: gather buffers [max_tokens, hidden] on
+// every rank by epoch parity, and every rank's flag word (device pointers valid
+// in this process: the peers' through CUDA IPC).
+struct HeadGroup {
+    int32_t rank = 0, world = 1;
+    float* outs[2][8] = {};
+    uint32_t* flags[8] = {};
 };
 
 class DeviceModel {
@@ -86,6 +99,13 @@ public:
                                              int32_t precision, int32_t top_k = 0);
     const int32_t* device_sampled() const noexcept { return d_sampled_; }
 
+    // Head parallelism (config head_ranks > 1): QKV for this rank's heads only
+    // (column slices of w_q, w_k, w_v), attention on the engine's head slice,
+    // nvllm_head_gather of every rank's attention rows into the gather buffer of
+    // the call's epoch parity, then W_o, the FFN and the LM head on the full
+    // rows, replicated on every rank (all ranks then sample the same tokens).
+    std::expected<void, EngineError> set_head_group(const HeadGroup& g);
+
     // Totals over every forward so far: launches of this library's kernels
     // (cuBLAS GEMMs not counted) and bytes copied host->device (token ids,
     // previous tokens, the engine's metadata) and device->host (results).
@@ -106,11 +126,11 @@ private:
                                              int32_t n_outs, int64_t out_block, int64_t ldc,
                                              int32_t epilogue);
     // nvllm_gemm_skinny (rows <= 16) or nvllm_gemm_decode_tc (17-32) on the
-    // row-major weights (batch matrices at stride w_stride)
+    // row-major weights (row stride ldw; batch matrices at stride w_stride)
     std::expected<void, EngineError> gemm_small(const float* a, int64_t m, int64_t k,
-                                                const float* w, int64_t n, int32_t batch,
-                                                int64_t w_stride, float* const* outs,
-                                                int32_t epilogue);
+                                                const float* w, int64_t ldw, int64_t n,
+                                                int32_t batch, int64_t w_stride,
+                                                float* const* outs, int32_t epilogue);
     bool use_small(int64_t rows) const noexcept { return use_skinny(rows) || use_decode_tc(rows); }
     std::size_t small_workspace(int64_t m, int64_t n, int64_t k, int32_t batch) const;
     bool use_tc(int64_t rows) const noexcept { return cfg_.gemm_math == 2 && rows > 32; }
@@ -127,6 +147,9 @@ private:
 
     ModelConfig cfg_;
     AttentionEngine& eng_;
+    HeadGroup heads_;
+    bool have_heads_ = false;
+    uint32_t gather_epoch_ = 0;
     cublasHandle_t blas_ = nullptr;
     float* d_w_ = nullptr;
     std::size_t w_floats_ = 0;

@@ -120,3 +120,59 @@ class HeadSplitGroup:
             L.nvllm_ipc_free(ptr)
         L.nvllm_ipc_free(self._flag[0])
         self._own = []
+
+
+class ModelHeads:
+    """The gather buffers of a head-parallel model (nvllm_model_set_head_group):
+    two [rows, hidden] fp32 buffers (by epoch parity) and a flag word per rank,
+    allocated with nvllm_ipc_alloc and opened in every rank's process."""
+
+    def __init__(self, dist, rows: int, hidden: int, device):
+        import torch
+        self.rank = dist.get_rank()
+        self.world = dist.get_world_size()
+        if self.world > MAX_RANKS:
+            raise ValueError(f"head parallelism supports at most {MAX_RANKS} ranks")
+        torch.cuda.set_device(device)
+        nbytes = max(rows * hidden * 4, 256)
+        self._own = [_ipc_alloc(nbytes) for _ in range(2)]
+        self._flag = _ipc_alloc(256)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, ([h for _, h in self._own], self._flag[1]))
+        self._opened = []
+        self.outs = [[0] * self.world for _ in range(2)]
+        self.flags = [0] * self.world
+        for r, (out_handles, flag_handle) in enumerate(everyone):
+            for par in range(2):
+                if r == self.rank:
+                    self.outs[par][r] = self._own[par][0]
+                else:
+                    self.outs[par][r] = _ipc_open(out_handles[par])
+                    self._opened.append(self.outs[par][r])
+            if r == self.rank:
+                self.flags[r] = self._flag[0]
+            else:
+                self.flags[r] = _ipc_open(flag_handle)
+                self._opened.append(self.flags[r])
+        dist.barrier()
+
+    def attach(self, model) -> None:
+        model.set_head_group(self.rank, self.world, self.outs, self.flags)
+
+    def close(self, dist=None):
+        import torch
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()  # no peer still writes into our buffers
+        L = host_lib()
+        L.nvllm_ipc_close.argtypes = [ctypes.c_void_p]
+        L.nvllm_ipc_free.argtypes = [ctypes.c_void_p]
+        for ptr in self._opened:
+            L.nvllm_ipc_close(ptr)
+        self._opened = []
+        if dist is not None:
+            dist.barrier()  # every peer unmapped ours
+        for ptr, _ in self._own:
+            L.nvllm_ipc_free(ptr)
+        L.nvllm_ipc_free(self._flag[0])
+        self._own = []

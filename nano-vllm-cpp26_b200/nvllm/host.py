@@ -69,7 +69,13 @@ class ModelConfig(ctypes.Structure):
     _fields_ = [("vocab", ctypes.c_int64), ("hidden", ctypes.c_int64), ("layers", ctypes.c_int64),
                 ("heads", ctypes.c_int64), ("head_dim", ctypes.c_int64), ("ffn", ctypes.c_int64),
                 ("emb_scale", ctypes.c_float), ("ffn_scale", ctypes.c_float),
-                ("gemm_math", ctypes.c_int32), ("graph_max_tokens", ctypes.c_int32)]
+                ("gemm_math", ctypes.c_int32), ("graph_max_tokens", ctypes.c_int32),
+                ("head_ranks", ctypes.c_int32)]
+
+
+class ModelHeadGroup(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32),
+                ("outs", (ctypes.c_void_p * 8) * 2), ("flags", ctypes.c_void_p * 8)]
 
 
 GEMM_FP32 = 0
@@ -334,16 +340,18 @@ class Model:
     LCG weights generated on the device, forward_batch as device kernels.
     ``cfg`` holds vocab, hidden, layers, heads, head_dim, ffn; ``scales`` the
     optional [emb_scale, ffn_scale] of the weights; ``gemm_math`` GEMM_FP32
-    (FFMA) or GEMM_BF16X9 (fp32 emulated on the tensor cores)."""
+    (FFMA) or GEMM_BF16X9 (fp32 emulated on the tensor cores); ``head_ranks``
+    > 1 makes it one rank of a head-parallel model (the engine holding heads /
+    head_ranks heads; see nvllm.headsplit.ModelHeads)."""
 
     def __init__(self, cfg: dict, engine: Engine, scales=None, gemm_math: int = GEMM_FP32,
-                 graph_max_tokens: int = 0):
+                 graph_max_tokens: int = 0, head_ranks: int = 1):
         self.L = host_lib()
         self.engine = engine  # the model uses the engine's arenas and stream
         self.cfg = dict(cfg)
         es, fs = (0.0, 0.0) if scales is None else (float(scales[0]), float(scales[1]))
         mc = ModelConfig(cfg["vocab"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["head_dim"],
-                         cfg["ffn"], es, fs, gemm_math, graph_max_tokens)
+                         cfg["ffn"], es, fs, gemm_math, graph_max_tokens, head_ranks)
         h = _vp()
         rc = self.L.nvllm_model_create(ctypes.byref(mc), engine.h, ctypes.byref(h))
         if rc != OK:
@@ -376,6 +384,20 @@ class Model:
         if top_k > 0:
             return sampled[:s], margins[:s], ti[:s, :top_k], tv[:s, :top_k]
         return sampled[:s]
+
+    def set_head_group(self, rank: int, world: int, outs, flags) -> None:
+        """outs[parity][r], flags[r]: device pointers valid in this process."""
+        g = ModelHeadGroup()
+        g.rank, g.world = rank, world
+        for par in range(2):
+            for r in range(world):
+                g.outs[par][r] = outs[par][r]
+        for r in range(world):
+            g.flags[r] = flags[r]
+        self.L.nvllm_model_set_head_group.argtypes = [_vp, ctypes.POINTER(ModelHeadGroup)]
+        rc = self.L.nvllm_model_set_head_group(self.h, ctypes.byref(g))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_model_set_head_group")
 
     def weights(self) -> tuple[int, int]:
         """(device pointer, float count) of the weight buffer."""

@@ -8,6 +8,10 @@ the sizing of an engine for them.
   8 + i % 12 tokens, 128 new tokens when i % 5 == 0, else 16).
 * ``serve_toy_seeded``: the same with seeded prompts of uniform length 8-32
   and uniform token ids, 20 % of the requests asking for 128 tokens.
+* ``longctx_model``: long-context decode inside the 4096-wide model: 4
+  requests of 32768 seeded prompt tokens each (the long-context attention
+  workload's shape), 16384 tokens per step, then decode; with head
+  parallelism every rank holds heads / N of every sequence.
 * ``serve``: the 4096-wide model (32 heads of 128, ffn 11008, 4 layers, vocab
   32000, LCG weights) under a serving load: prompt lengths lognormal with
   median 256 (sigma 1.0, at most 4096 tokens), completions 16 tokens for 80 %
@@ -89,6 +93,14 @@ def make_serve(name: str, seed: int = 0, requests: int | None = None) -> ServeSp
     if name == "serve_toy_seeded":
         prompts, max_new = seeded_toy_requests(requests or 96, TOY_MODEL["vocab"], seed)
         return ServeSpec(name, TOY_MODEL, 1024, 16, 16, 512, 2, prompts, max_new)
+    if name == "longctx_model":
+        n = requests or 4
+        rng = np.random.default_rng(seed)
+        prompts = [rng.integers(1, WIDE_MODEL["vocab"], 32768).tolist() for _ in range(n)]
+        max_new = [4096] * n  # decode runs longer than any timed window
+        spec = ServeSpec(name, WIDE_MODEL, 0, 16, n, 16384, 0, prompts, max_new)
+        spec.num_blocks = int(sum((len(p) + m + 15) // 16 for p, m in zip(prompts, max_new)) + 16)
+        return spec
     if name == "serve":
         prompts, max_new = lognormal_requests(requests or 128, WIDE_MODEL["vocab"], seed)
         spec = ServeSpec(name, WIDE_MODEL, 0, 16, 256, 16384, 4, prompts, max_new)
@@ -106,6 +118,8 @@ def serve_config(spec: ServeSpec) -> dict:
         "serve_toy": "reference continuous-batching benchmark (toy model, 96 requests)",
         "serve_toy_seeded": "toy model, 96 seeded requests (prompts U[8,32])",
         "serve": "e2e serving, 4096-wide 4-layer model, 128 requests per GPU",
+        "longctx_model": "long-context decode in the 4096-wide model: 4 sequences of 32768 "
+                         "prompt tokens, heads split over the GPUs",
     }[spec.name], "model": f"d{m['hidden']} L{m['layers']} H{m['heads']}x{m['head_dim']} "
                           f"ffn{m['ffn']} vocab{m['vocab']} (LCG weights)",
         "requests": len(spec.prompts), "prompt_tokens": spec.prompt_tokens,

@@ -34,3 +34,19 @@ def test_head_split(world):
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count(f"head split over {world} ranks ok") == world
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_head_parallel_model(world):
+    """The whole model with its heads split over the ranks (tests/mp_model_heads.py):
+    every rank reproduces the reference's 4096-wide token trace."""
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={world}", "--master-addr=127.0.0.1",
+           f"--master-port={_free_port()}", str(ROOT / "tests" / "mp_model_heads.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=420)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count(f"head-parallel model over {world} ranks") == 2 * world
