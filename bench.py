@@ -831,10 +831,12 @@ def headmodel_main(args):
     estream = torch.cuda.ExternalStream(eng.stream(), device=dev)
     n_seq = len(spec.prompts)
     # prefill (a whole prompt per iteration), until an iteration is pure decode
-    while True:
+    for _ in range(2 * n_seq + 4):
         s = gen.step()
         if s["scheduled_tokens"] == n_seq and s["batch_size"] == n_seq:
             break
+    else:
+        raise RuntimeError("the prompts were not all prefilled within the expected iterations")
     for _ in range(args.warmup):
         gen.step()
     m0 = gen.metrics()

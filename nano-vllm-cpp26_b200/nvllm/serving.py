@@ -10,8 +10,8 @@ the sizing of an engine for them.
   and uniform token ids, 20 % of the requests asking for 128 tokens.
 * ``longctx_model``: long-context decode inside the 4096-wide model: 4
   requests of 32768 seeded prompt tokens each (the long-context attention
-  workload's shape), 16384 tokens per step, then decode; with head
-  parallelism every rank holds heads / N of every sequence.
+  workload's shape), one prompt per step beside the running decodes, then
+  decode; with head parallelism every rank holds heads / N of every sequence.
 * ``serve``: the 4096-wide model (32 heads of 128, ffn 11008, 4 layers, vocab
   32000, LCG weights) under a serving load: prompt lengths lognormal with
   median 256 (sigma 1.0, at most 4096 tokens), completions 16 tokens for 80 %
@@ -97,8 +97,10 @@ def make_serve(name: str, seed: int = 0, requests: int | None = None) -> ServeSp
         n = requests or 4
         rng = np.random.default_rng(seed)
         prompts = [rng.integers(1, WIDE_MODEL["vocab"], 32768).tolist() for _ in range(n)]
-        max_new = [4096] * n  # decode runs longer than any timed window
-        spec = ServeSpec(name, WIDE_MODEL, 0, 16, n, 16384, 0, prompts, max_new)
+        max_new = [512] * n  # decode runs longer than any timed window
+        # a step holds one whole prompt beside the running decodes (the scheduler
+        # admits a prompt over the token budget only into an empty batch)
+        spec = ServeSpec(name, WIDE_MODEL, 0, 16, n, 32768 + n, 0, prompts, max_new)
         spec.num_blocks = int(sum((len(p) + m + 15) // 16 for p, m in zip(prompts, max_new)) + 16)
         return spec
     if name == "serve":
