@@ -159,3 +159,40 @@ def test_model_ops_validate_on_the_host(nvlib, nvmod):
                                    ctypes.c_int32(1), i64(128), i64(128), ctypes.c_int32(0),
                                    None, ctypes.c_size_t(0), st) == nvmod.OK  # m = 0
     assert nvlib.nvllm_gemm_workspace_size(i64(4), i64(100), i64(64)) == 0
+
+
+def test_head_gather_validates_on_the_host(nvlib, nvmod):
+    """nvllm_head_gather refuses a missing group, a rank outside it, epoch 0, empty
+    rows of zero width and missing peer pointers before touching the device."""
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    nvlib.nvllm_head_gather.argtypes = [vp, i64, i64, ctypes.POINTER(nvmod.HeadSplit), vp]
+
+    def group(rank, world, epoch, fill=True):
+        hs = nvmod.HeadSplit()
+        hs.rank, hs.world, hs.epoch = rank, world, epoch
+        for r in range(min(world, 8) if fill else 0):
+            hs.outs[r] = 256 * (r + 1)
+            hs.flags[r] = 4096 * (r + 1)
+        return hs
+
+    assert nvlib.nvllm_head_gather(vp(256), i64(4), i64(8), None, None) == nvmod.ERR_INVALID
+    for hs in (group(2, 2, 1), group(0, 9, 1), group(0, 2, 0), group(0, 2, 1, fill=False)):
+        rc = nvlib.nvllm_head_gather(vp(256), i64(4), i64(8), ctypes.byref(hs), None)
+        assert rc == nvmod.ERR_INVALID
+    hs = group(0, 2, 1)
+    assert nvlib.nvllm_head_gather(vp(256), i64(4), i64(0), ctypes.byref(hs),
+                                   None) == nvmod.ERR_INVALID  # zero width
+    assert nvlib.nvllm_head_gather(None, i64(4), i64(8), ctypes.byref(hs),
+                                   None) == nvmod.ERR_INVALID  # rows without data
+
+
+def test_model_head_group_validates_on_the_host(nvmod):
+    from nvllm.host import ModelHeadGroup, host_lib
+    L = host_lib()
+    L.nvllm_model_set_head_group.argtypes = [ctypes.c_void_p, ctypes.POINTER(ModelHeadGroup)]
+    g = ModelHeadGroup()
+    g.rank, g.world = 0, 2
+    assert L.nvllm_model_set_head_group(None, ctypes.byref(g)) == nvmod.ERR_INVALID
+    assert L.nvllm_model_set_head_group(ctypes.c_void_p(256), None) == nvmod.ERR_INVALID
+    g.world = 9
+    assert L.nvllm_model_set_head_group(ctypes.c_void_p(256), ctypes.byref(g)) == nvmod.ERR_INVALID
