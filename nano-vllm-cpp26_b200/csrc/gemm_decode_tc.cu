@@ -10,13 +10,15 @@
 // X_tile^T (M = 128 output features in TMEM lanes, N = 32 tokens, K = 8 per
 // instruction), every product in 3xTF32: hi = x rounded to tf32 (nearest),
 // lo = x - hi, and W_hi X_hi + W_lo X_hi + W_hi X_lo (the tensor core reads a
-// tf32 operand as the top 19 bits of its fp32 container).
+// tf32 operand as the top 19 bits of its fp32 container). X_lo is stored right
+// after X_hi, so W_hi [X_hi | X_lo] is a single N = 64 MMA into a 64-column
+// accumulator whose halves are added when it is folded.
 //
 // Per stage (32 rows of K), with 11 warps per CTA (one CTA per SM, all 512
 // TMEM columns):
 //   warp 8, lane 0: the TMA copies into an 8-stage ring (W tile 32 x 128 fp32,
 //     no swizzle; X tile 32 rows x 32 fp32, 128-byte swizzle; no multicast);
-//   warps 9-10, lane 0: the 12 MMAs of a stage, alternate stages each into its
+//   warps 9-10, lane 0: the 8 MMAs of a stage, alternate stages each into its
 //     own accumulators (a single issuing thread leaves the tensor core idle
 //     around each of its mbarrier waits and commits), never waiting on an MMA;
 //   warps 0-7: converters in two groups of four that take alternate stages.
@@ -68,18 +70,22 @@ constexpr int kMinUnits = 8;   // stages a CTA handles at least
 constexpr uint32_t kWBytes = kStageK * kTileN * 4;  // 16 KB
 constexpr uint32_t kXBytes = kBT * kStageK * 4;     // 4 KB
 constexpr uint32_t kStageBytes = kWBytes + 2 * kXBytes;  // W, X (hi in place), X lo
-// TMEM: four A buffers (hi 32 + lo 32 columns each) and two accumulators (32
-// columns each) for each MMA issuer
+// TMEM: four A buffers (hi 32 + lo 32 columns each) and two accumulators (64
+// columns each: W_hi X_hi + W_lo X_hi in 0-31, W_hi X_lo in 32-63) for each MMA issuer
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColA = 0;
 constexpr uint32_t kColD = kABufs * 64;
-constexpr uint32_t kIdesc = tc::tf32_idesc(kTileN, kBT, false, false);
+constexpr uint32_t kDCols = 2 * kBT;
+// X lo lies directly after X hi in the stage (same swizzle, 1024-byte row groups),
+// so W_hi [X_hi | X_lo] is one N = 64 MMA
+constexpr uint32_t kIdescHi = tc::tf32_idesc(kTileN, 2 * kBT, false, false);
+constexpr uint32_t kIdescLo = tc::tf32_idesc(kTileN, kBT, false, false);
 constexpr uint32_t kSmem = kStages * kStageBytes + 512 + 1024;
 static_assert(kSmem <= 227u * 1024u, "shared memory");
 // every ring slot (and every A buffer) belongs to one issuer: units g and g + kStages
 // (g + kABufs) go to the same issuer
 static_assert(kStages % kIssuers == 0 && kABufs % kIssuers == 0, "issuer assignment");
-static_assert(kABufs * 64 + kIssuers * 2 * kBT <= kTmemCols, "TMEM columns");
+static_assert(kABufs * 64 + kIssuers * 2 * kDCols <= kTmemCols, "TMEM columns");
 
 struct DecodeParams {
     int64_t m, n, k, ldc;
@@ -280,17 +286,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc::fence_after_sync();
                 const uint32_t xhi = smem_addr(smem + s * kStageBytes + kWBytes);
-                const uint32_t xlo = xhi + kXBytes;
                 const uint32_t a_hi = tmem + kColA + ab * 64u;
                 const uint32_t a_lo = a_hi + 32u;
-                const uint32_t d = tmem + kColD + uint32_t(me * 2 + int(buf)) * uint32_t(kBT);
+                const uint32_t d = tmem + kColD + uint32_t(me * 2 + int(buf)) * kDCols;
 #pragma unroll
                 for (int kk = 0; kk < kStageK / 8; ++kk) {
+                    // B = rows 0-31 X_hi, rows 32-63 X_lo (N = 64) / X_hi alone (N = 32)
                     const uint64_t dh = tc::sw128_desc(xhi + uint32_t(kk) * 32u, 16, 1024);
-                    const uint64_t dl = tc::sw128_desc(xlo + uint32_t(kk) * 32u, 16, 1024);
-                    tc::mma_tf32_ts(d, a_lo + uint32_t(kk) * 8u, dh, kIdesc, !chunk_first || kk > 0);
-                    tc::mma_tf32_ts(d, a_hi + uint32_t(kk) * 8u, dl, kIdesc, true);
-                    tc::mma_tf32_ts(d, a_hi + uint32_t(kk) * 8u, dh, kIdesc, true);
+                    tc::mma_tf32_ts(d, a_hi + uint32_t(kk) * 8u, dh, kIdescHi,
+                                    !chunk_first || kk > 0);
+                    tc::mma_tf32_ts(d, a_lo + uint32_t(kk) * 8u, dh, kIdescLo, true);
                 }
                 tc::commit(&ctl->empty[s]);
                 if (chunk_last) {
@@ -323,11 +328,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return false;
             }
             tc::fence_after_sync();
-            float v[32];
-            tc::tmem_ld32(tmem + kColD + uint32_t(i * 2 + int(buf)) * uint32_t(kBT) + lane_off, v);
+            const uint32_t dcol = tmem + kColD + uint32_t(i * 2 + int(buf)) * kDCols + lane_off;
+            float v[kBT], w[kBT];
+            tc::tmem_ld32(dcol, v);
+            tc::tmem_ld32(dcol + uint32_t(kBT), w);
             tc::tmem_ld_wait();
 #pragma unroll
-            for (int t = 0; t < kBT; ++t) acc[t] += v[t];
+            for (int t = 0; t < kBT; ++t) acc[t] += v[t] + w[t];
             tc::fence_before_sync();
             mbar_arrive(&ctl->d_free[i][buf]);
             qf[i] = q + 1;
