@@ -97,7 +97,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -109,6 +109,10 @@ class ClockSampler:
 
         self.thread = threading.Thread(target=reader, daemon=True)
         self.thread.start()
+        # nvidia-smi takes a while to start: the timed region begins once it samples
+        t0 = time.monotonic()
+        while not self.lines and self.proc.poll() is None and time.monotonic() - t0 < 5.0:
+            time.sleep(0.01)
         return self
 
     def stop(self) -> dict:
