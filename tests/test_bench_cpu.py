@@ -10,6 +10,7 @@ import pytest
 
 import bench
 
+
 def sample(sm, mx=1965, power_cap="Not Active", hw="Not Active"):
     return f"0, {sm}, {mx}, 900.1, 0x4, {hw}, Not Active, Not Active, {power_cap}"
 
