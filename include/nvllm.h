@@ -106,9 +106,11 @@ int nvllm_paged_attention(float* out, const float* query, const float* k_arena,
  * The workspace is owned by the library: a 64 MiB device array of which every
  * GPU that loads libnvllm.so holds one copy until the process exits. A batch
  * whose nvllm_paged_attention_workspace_size() exceeds 64 MiB is refused with
- * NVLLM_ERR_WORKSPACE. The entry point itself allocates nothing. The first
- * call on a device looks up the array's device address (cudaGetSymbolAddress,
- * with that device current); make that first call before any stream capture.
+ * NVLLM_ERR_WORKSPACE. The entry point itself allocates nothing. Every call
+ * looks up the array's device address (cudaGetSymbolAddress, with the
+ * caller's device current); the first one on a device may load the library's
+ * module there, so make that first call before any stream capture. Do not use
+ * a device across a reset with calls in flight.
  * All calls share the one array, so calls that overlap on the GPU (different
  * streams, or host threads, without ordering between them) race and corrupt
  * each other's results: order them on one stream. Arguments and results are

@@ -11,7 +11,6 @@
 // kStaticWorkspaceBytes. Every GPU that loads the library holds one copy of it
 // until the process exits.
 #include <cstddef>
-#include <mutex>
 
 #include <cuda_runtime.h>
 
@@ -25,26 +24,16 @@ constexpr size_t kStaticWorkspaceBytes = size_t(64) << 20;  // 64 MiB
 static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
 
 // Host code must not use g_static_workspace's name as a pointer: on the host it
-// is only a stand-in for the symbol. Its device address is looked up once per
-// device, with that device current, and cached here.
-constexpr int kMaxDevices = 64;
-void* g_static_workspace_addr[kMaxDevices] = {};
-std::mutex g_static_workspace_mutex;
-
+// is only a stand-in for the symbol. Its device address is looked up on every
+// call, with the caller's device current. The lookup allocates nothing and is
+// cheap, and it stays right if the device's context was torn down and the
+// module reloaded at another address (after a cudaDeviceReset, for instance).
 int static_workspace_address(void** addr) {
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_workspace) != cudaSuccess || p == nullptr) {
         return NVLLM_ERR_CUDA;
     }
-    std::lock_guard<std::mutex> lock(g_static_workspace_mutex);
-    if (g_static_workspace_addr[dev] == nullptr) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_static_workspace) != cudaSuccess || p == nullptr) {
-            return NVLLM_ERR_CUDA;
-        }
-        g_static_workspace_addr[dev] = p;
-    }
-    *addr = g_static_workspace_addr[dev];
+    *addr = p;
     return NVLLM_OK;
 }
 

@@ -22,7 +22,12 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libref_harness.so"
-REF_SOURCES = Path(os.environ.get("NVLLM_REFERENCE_DIR", "/root/reference"))
+
+def reference_sources() -> Path | None:
+    """Where the reference's sources lie: ``NVLLM_REFERENCE_DIR`` (no default;
+    the reference harness is built only when it names a checkout)."""
+    d = os.environ.get("NVLLM_REFERENCE_DIR")
+    return Path(d) if d else None
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _i64p = ctypes.POINTER(ctypes.c_int64)
@@ -44,14 +49,20 @@ def _ptr(a: np.ndarray, t):
     return a.ctypes.data_as(t)
 
 
-def build(with_reference: bool | None = None) -> None:
-    """Compile the C oracle and, when the reference sources are present, the
-    reference harness (``make -C oracle [ref]``)."""
+def build(with_reference: bool | None = None, reference_dir: Path | str | None = None) -> None:
+    """Compile the C oracle and, when the reference sources are present
+    (``reference_dir``, else ``NVLLM_REFERENCE_DIR``), the reference harness
+    (``make -C oracle [ref] REF=...``)."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    src = Path(reference_dir) if reference_dir is not None else reference_sources()
+    present = src is not None and (src / "src" / "model.cpp").exists()
     if with_reference is None:
-        with_reference = (REF_SOURCES / "src" / "model.cpp").exists()
+        with_reference = present
     if with_reference:
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REF_SOURCES}"], check=True)
+        if not present:
+            raise FileNotFoundError("the reference sources are needed: set NVLLM_REFERENCE_DIR "
+                                    "to a checkout of nano-vllm-cpp26")
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={src}"], check=True)
 
 
 class Oracle:

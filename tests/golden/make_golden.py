@@ -3,7 +3,8 @@ C++ (PagedKVCache + TransformerModel::forward_batch, built by
 ``make -C oracle ref`` from the reference sources) on the deterministic cases
 of ``tests/casegen.py``.
 
-Run from the repository root:  python tests/golden/make_golden.py
+Run from the repository root, with ``NVLLM_REFERENCE_DIR`` naming a checkout of
+the reference:  NVLLM_REFERENCE_DIR=<checkout> python tests/golden/make_golden.py
 
 Each ``<case>.npz`` holds the case description (geometry, per-sequence
 num_computed / total_len, block tables), checksums of the generated inputs,

@@ -16,7 +16,7 @@ def sample(sm, mx=1965, power_cap="Not Active", hw="Not Active"):
 
 
 def test_clock_sampler_summary():
-    s = bench.ClockSampler(0)
+    s = bench.ClockSampler("GPU-0")
     s.lines = [sample(1800), sample(1900, power_cap="Active"), sample(1965),
                "0, [N/A], 1965, 1, 0, a, b, c, d", "garbage", ""]
     out = s.stop()
@@ -27,7 +27,7 @@ def test_clock_sampler_summary():
 
 
 def test_clock_sampler_reports_a_slowdown():
-    s = bench.ClockSampler(0)
+    s = bench.ClockSampler("GPU-0")
     s.lines = [sample(1200, hw="Active"), sample(1250)]
     out = s.stop()
     assert out["reasons"] == ["hw_slowdown"] and out["samples"] == 2
@@ -38,8 +38,40 @@ def test_clock_sampler_without_nvidia_smi(monkeypatch):
         raise FileNotFoundError("nvidia-smi")
 
     monkeypatch.setattr(bench.subprocess, "Popen", missing)
-    out = bench.ClockSampler(0).start().stop()
-    assert out == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+    out = bench.ClockSampler("GPU-0").start().stop()
+    assert out == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                   "device": "GPU-0"}
+
+
+class FakeUUID:
+    def __init__(self, raw: bytes):
+        self.bytes = raw
+
+
+class FakeProps:
+    def __init__(self, raw: bytes, bus: int):
+        self.uuid = FakeUUID(raw)
+        self.pci_domain_id, self.pci_bus_id, self.pci_device_id = 0, bus, 0
+
+
+def test_clock_sampler_names_the_visible_gpu_not_the_local_ordinal(monkeypatch):
+    """With CUDA_VISIBLE_DEVICES=3 the process's cuda:0 is the machine's GPU 3;
+    nvidia-smi ignores the variable, so the sampler must name the device by its
+    UUID (here the fake UUID of the machine's GPU 3), never by --id=0."""
+    import torch
+    machine = {i: FakeProps(bytes([i]) * 16, 0x10 + i) for i in range(8)}
+    visible = [3]
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "3")
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda d: machine[visible[d]])
+    dev_id = bench.smi_device_id(0)
+    assert dev_id == "GPU-03030303-0303-0303-0303-030303030303"
+    cmd = bench.ClockSampler(dev_id).command()
+    assert f"--id={dev_id}" in cmd and "--id=0" not in cmd
+    # without a UUID the PCI bus id names it
+    props = FakeProps(b"", 0x13)
+    props.uuid = None
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda d: props)
+    assert bench.smi_device_id(0) == "00000000:13:00.0"
 
 
 class SlowSmi:
@@ -75,7 +107,7 @@ def test_clock_sampler_start_waits_for_the_first_sample(monkeypatch):
     monkeypatch.setattr(bench.subprocess, "Popen",
                         lambda *a, **k: SlowSmi(0.3, [sample(1965)] * 50))
     t0 = time.monotonic()
-    s = bench.ClockSampler(0).start()
+    s = bench.ClockSampler("GPU-0").start()
     waited = time.monotonic() - t0
     assert s.lines, "start() returned before nvidia-smi produced a sample"
     assert 0.25 <= waited < 5.0
@@ -85,7 +117,7 @@ def test_clock_sampler_start_waits_for_the_first_sample(monkeypatch):
 def test_clock_sampler_start_is_bounded(monkeypatch):
     monkeypatch.setattr(bench.subprocess, "Popen", lambda *a, **k: SlowSmi(30.0, []))
     t0 = time.monotonic()
-    s = bench.ClockSampler(0).start()
+    s = bench.ClockSampler("GPU-0").start()
     assert time.monotonic() - t0 < 6.0
     s.proc.terminate()
 

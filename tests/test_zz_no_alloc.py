@@ -7,7 +7,10 @@ mid-step): the workspace is a 64 MiB array owned by the library on each GPU.
 
 The test calls it through the C ABI twice in a row on the same mixed prefill +
 decode batch and compares both outputs with those of the workspace entry point
-(nvllm_paged_attention) within the fp32 tolerance of the other parity tests.
+(nvllm_paged_attention) at the same precision: fp32 prefill tiles within the
+fp32 tolerance of the other parity tests, tensor-core (3xTF32) prefill tiles,
+which lay the shared array out for their 128-row query tiles, within the TF32
+tolerance.
 It also checks that a batch needing more than 64 MiB of workspace is refused.
 This file is collected last so that a run stopping at the first failure has
 already run every other test; it builds its own batch and passes alone too.
@@ -18,7 +21,7 @@ import math
 import numpy as np
 import pytest
 
-from helpers import TOL_FP32
+from helpers import TOL_FP32, TOL_TF32
 
 pytestmark = pytest.mark.gpu
 
@@ -61,27 +64,30 @@ def _mixed_batch(nv):
                 max_q=int(ql.max()), max_ctx=int(ctx.max()), scale=1.0 / math.sqrt(hd))
 
 
-def test_no_alloc_entry_point_matches_workspace_entry_point(nv):
+@pytest.mark.parametrize("precision_name,tol", [("PRECISION_FP32", TOL_FP32),
+                                                ("PRECISION_TF32", TOL_TF32)])
+def test_no_alloc_entry_point_matches_workspace_entry_point(nv, precision_name, tol):
     import torch
+    precision = getattr(nv, precision_name)
     static_attn = _bind(nv)
     b = _mixed_batch(nv)
     lay = b["lay"]
     assert nv.workspace_size(len(b["ctx"]), b["max_q"], b["max_ctx"], lay) <= STATIC_WORKSPACE_BYTES
     ref = torch.full_like(b["q"], float("nan"))
     nv.paged_attention(ref, b["q"], b["ka"], b["va"], b["bt"], b["cu"], b["ctx"], b["max_q"],
-                       b["max_ctx"], 0, lay, scale=b["scale"])
+                       b["max_ctx"], 0, lay, scale=b["scale"], precision=precision)
     stream = torch.cuda.current_stream().cuda_stream
     for call in range(2):
         out = torch.full_like(b["q"], float("nan"))
         rc = static_attn(out.data_ptr(), b["q"].data_ptr(), b["ka"].data_ptr(), b["va"].data_ptr(),
                          b["bt"].data_ptr(), b["bt"].shape[1], b["cu"].data_ptr(),
                          b["ctx"].data_ptr(), len(b["ctx"]), b["max_q"], b["max_ctx"], 0,
-                         b["scale"], nv.PRECISION_FP32, ctypes.byref(lay), stream)
+                         b["scale"], precision, ctypes.byref(lay), stream)
         assert rc == nv.OK, nv.status_string(rc)
         torch.cuda.synchronize()
         assert nv.get_last_error() == nv.OK
         err = (out - ref).abs().max().item()
-        assert err <= TOL_FP32, f"call {call}: max-abs {err} vs the workspace entry point"
+        assert err <= tol, f"call {call}: max-abs {err} vs the workspace entry point"
 
 
 def test_no_alloc_entry_point_refuses_oversized_batches(nv):
