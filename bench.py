@@ -48,7 +48,6 @@ sys.path.insert(0, str(ROOT))
 METRIC = "paged-attn tokens/s + HBM GB/s (% peak) at 1/2/4/8 B200 vs host-CPU ref"
 UNIT = "tokens/s"
 FALLBACK_HBM_GBS = 6650.0
-KERNELS_PER_STEP = 4  # reshape_and_cache, plan, decode (+prefill if any), merge
 
 
 def log(*a):
@@ -117,6 +116,7 @@ class ClockSampler:
     def __init__(self, device_id: str):
         self.device_id = device_id
         self.lines: list[str] = []
+        self.stamps: list[float] = []  # time.monotonic() at which each line arrived
         self.proc = None
         self.thread = None
 
@@ -135,6 +135,7 @@ class ClockSampler:
 
         def reader():
             for line in self.proc.stdout:
+                self.stamps.append(time.monotonic())
                 self.lines.append(line.strip())
 
         self.thread = threading.Thread(target=reader, daemon=True)
@@ -154,9 +155,20 @@ class ClockSampler:
                 self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=2)
+        return self.summary(self.lines)
+
+    def window(self, t0: float, t1: float) -> dict:
+        """Summary of the samples that arrived between two time.monotonic()
+        readings (a timed region; nvidia-smi prints a sample as it takes it)."""
+        lines = [ln for ln, t in zip(list(self.lines), list(self.stamps)) if t0 <= t <= t1]
+        out = self.summary(lines)
+        out["seconds"] = t1 - t0
+        return out
+
+    def summary(self, lines) -> dict:
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -295,9 +307,158 @@ def workload_config(spec) -> dict:
 # the nvllm path
 
 
+class Ranks:
+    """The process group around a timed region: barriers, the maximum over
+    ranks, gathering per-rank figures. With one process all are no-ops."""
+
+    def __init__(self, dist, dev):
+        self.dist, self.dev = dist, dev
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.dist is None:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, values) -> list[list[float]]:
+        """One row of floats per rank, in rank order."""
+        import torch
+        t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=self.dev)
+        if self.dist is None:
+            return [t.tolist()]
+        out = [torch.empty_like(t) for _ in range(self.dist.get_world_size())]
+        self.dist.all_gather(out, t)
+        return [o.tolist() for o in out]
+
+
+def timed_leg(fn, steps: int, warmup: int, stream, ranks: Ranks, sampler, inner=None):
+    """W untimed calls of ``fn``, then exactly ``steps`` calls bracketed by a
+    barrier and a device synchronize on both sides, timed with CUDA events on
+    ``stream``. ``inner(i)`` may return a pair of events to record around
+    part of step i. Returns (max-over-ranks seconds, this rank's seconds, the
+    clock record of the region)."""
+    import torch
+    dev = ranks.dev
+    for _ in range(warmup):
+        fn(None)
+    torch.cuda.synchronize(dev)
+    ranks.barrier()
+    torch.cuda.synchronize(dev)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    t0 = time.monotonic()
+    a.record(stream)
+    for i in range(steps):
+        fn(i)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    t1 = time.monotonic()
+    ranks.barrier()
+    mine = a.elapsed_time(b) / 1e3
+    return ranks.max(mine), mine, sampler.window(t0, t1)
+
+
+class DeviceBatch:
+    """A :class:`nvllm.workload.BatchSpec` on the device over given arenas:
+    Q/K/V rows of the step's new tokens (N(0,1) from ``gen``), metadata, output
+    and workspace; ``step()`` is one pass of the hot path (KV write of the new
+    rows + paged attention)."""
+
+    def __init__(self, nvllm, spec, lay, ka, va, gen, dev, stream, precision):
+        import torch
+        self.nv, self.spec, self.lay, self.ka, self.va = nvllm, spec, lay, ka, va
+        self.stream, self.precision = stream, precision
+        n, D = spec.n_tokens, spec.hidden
+        self.q = torch.randn((n, D), generator=gen, device=dev)
+        self.k = torch.randn((n, D), generator=gen, device=dev)
+        self.v = torch.randn((n, D), generator=gen, device=dev)
+        self.out = torch.empty_like(self.q)
+        self.bt = torch.from_numpy(spec.block_tables).to(dev)
+        self.cu = torch.from_numpy(spec.cu_seqlens_q).to(dev)
+        self.ctx = torch.from_numpy(spec.ctx_lens).to(dev)
+        self.slots = torch.from_numpy(spec.slot_mapping()).to(dev)
+        self.max_q = int(spec.q_lens.max())
+        self.max_ctx = int(spec.ctx_lens.max())
+        self.ws = nvllm.alloc_workspace(spec.num_seqs, self.max_q, self.max_ctx, lay, device=dev)
+
+    def write(self):
+        self.nv.reshape_and_cache(self.k, self.v, self.ka, self.va, self.slots, 0, self.lay,
+                                  stream=self.stream)
+
+    def attend(self, precision=None):
+        p = self.precision if precision is None else precision
+        self.nv.paged_attention(self.out, self.q, self.ka, self.va, self.bt, self.cu, self.ctx,
+                                self.max_q, self.max_ctx, 0, self.lay, workspace=self.ws,
+                                stream=self.stream, precision=p)
+
+    def step(self, precision=None):
+        self.write()
+        self.attend(precision)
+
+    def launches(self) -> int:
+        """This library's kernels per step: KV write, plan, decode, merge, and
+        the prefill kernel when a sequence has several query rows."""
+        return 4 + (1 if self.max_q > 1 else 0)
+
+
+def oracle_parity(db, seqs, host_budget: int = 2 << 30) -> dict:
+    """The step's output rows of ``seqs`` against the oracle (the C restatement
+    of the reference's attention loop), from host copies of the blocks those
+    sequences read, in groups of at most ``host_budget`` bytes. A check only:
+    it runs after the timed regions."""
+    import torch
+
+    from oracle.oracle import KVLayout, Oracle
+    orc = Oracle()
+    spec, lay = db.spec, db.lay
+    nbs = (spec.ctx_lens + spec.block_size - 1) // spec.block_size
+    row_bytes = 2 * spec.block_size * spec.hidden * 4
+    cu = spec.cu_seqlens_q
+    groups, cur, blocks = [], [], 0
+    for s in seqs:
+        if cur and (blocks + int(nbs[s])) * row_bytes > host_budget:
+            groups.append(cur)
+            cur, blocks = [], 0
+        cur.append(int(s))
+        blocks += int(nbs[s])
+    if cur:
+        groups.append(cur)
+    worst, rows = 0.0, 0
+    for g in groups:
+        used = np.unique(np.concatenate([spec.block_tables[s, :nbs[s]] for s in g]))
+        remap = np.full(int(used.max()) + 1, -1, np.int64)
+        remap[used] = np.arange(len(used))
+        idx = torch.from_numpy(used.astype(np.int64)).to(db.ka.device)
+        ka = db.ka.index_select(0, idx).cpu().numpy()
+        va = db.va.index_select(0, idx).cpu().numpy()
+        bt = np.zeros((len(g), spec.block_tables.shape[1]), np.int32)
+        q_rows, gcu = [], [0]
+        for j, s in enumerate(g):
+            bt[j, :nbs[s]] = remap[spec.block_tables[s, :nbs[s]]]
+            q_rows.extend(range(int(cu[s]), int(cu[s + 1])))
+            gcu.append(len(q_rows))
+        ridx = torch.as_tensor(q_rows, device=db.q.device)
+        q = db.q.index_select(0, ridx).cpu().numpy()
+        got = db.out.index_select(0, ridx).cpu().numpy()
+        olay = KVLayout(len(used), 1, spec.block_size, spec.num_heads, spec.head_dim)
+        ref = orc.paged_attention(q, ka, va, bt, np.array(gcu, np.int32),
+                                  spec.ctx_lens[g].astype(np.int32), 0,
+                                  1.0 / math.sqrt(spec.head_dim), olay)
+        worst = max(worst, float(np.abs(got - ref).max()))
+        rows += len(q_rows)
+    return {"max_abs": worst, "rows": rows, "seqs": len(seqs)}
+
+
 def nvllm_main(args, spec):
     import torch
     import nvllm
+    from nvllm.workload import make_batch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -310,12 +471,12 @@ def nvllm_main(args, spec):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
+    ranks = Ranks(dist, dev)
     nvllm.lib()  # fails loudly when the CUDA library is missing
 
-    # per-rank batch: sequence partitioning gives every GPU its own sequences
-    if rank != 0:
-        from nvllm.workload import make_batch
-        spec = make_batch(args.workload, seed=args.seed + rank)
+    # per-rank batch (sequence partitioning): the same context lengths on every
+    # GPU, in a rank-seeded order with rank-seeded block tables and values
+    spec = make_batch(args.workload, seed=args.seed, rank=rank)
     lay = nvllm.KVLayout(spec.num_blocks, 1, spec.block_size, spec.num_heads, spec.head_dim)
     D = spec.hidden
     # The arenas belong to the host engine (libnvllm_host: allocator, pinned
@@ -331,76 +492,52 @@ def nvllm_main(args, spec):
     gen.manual_seed(1000 + rank)
     ka.normal_(generator=gen)
     va.normal_(generator=gen)
-    n = spec.n_tokens
-    q = torch.randn((n, D), generator=gen, device=dev)
-    k = torch.randn((n, D), generator=gen, device=dev)
-    v = torch.randn((n, D), generator=gen, device=dev)
-    out = torch.empty_like(q)
-    bt = torch.from_numpy(spec.block_tables).to(dev)
-    cu = torch.from_numpy(spec.cu_seqlens_q).to(dev)
-    ctx = torch.from_numpy(spec.ctx_lens).to(dev)
-    slots = torch.from_numpy(spec.slot_mapping()).to(dev)
-    max_q = int(spec.q_lens.max())
-    max_ctx = int(spec.ctx_lens.max())
-    ws = nvllm.alloc_workspace(spec.num_seqs, max_q, max_ctx, lay, device=dev)
     stream = torch.cuda.current_stream(dev)
-
     precision = nvllm.PRECISION_TF32 if args.precision == "tf32" else nvllm.PRECISION_FP32
-
-    def step():
-        nvllm.reshape_and_cache(k, v, ka, va, slots, 0, lay, stream=stream)
-        nvllm.paged_attention(out, q, ka, va, bt, cu, ctx, max_q, max_ctx, 0, lay,
-                              workspace=ws, stream=stream, precision=precision)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    db = DeviceBatch(nvllm, spec, lay, ka, va, gen, dev, stream, precision)
+    n = spec.n_tokens
+    warm = max(args.warmup, 3)
+    launches = 0
 
     sampler = ClockSampler(smi_device_id(local)).start()
+    t_first = time.monotonic()
 
     # ---- device-resident throughput --------------------------------------
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize(dev)
-    if nvllm.get_last_error(stream) != nvllm.OK:
-        raise RuntimeError("device status after warm-up is not OK")
-    barrier()
-    torch.cuda.synchronize(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    # per-step attention timing (events bracket the attention call only)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
-    e0.record(stream)
-    for i in range(args.steps):
-        nvllm.reshape_and_cache(k, v, ka, va, slots, 0, lay, stream=stream)
-        ev[i][0].record(stream)
-        nvllm.paged_attention(out, q, ka, va, bt, cu, ctx, max_q, max_ctx, 0, lay,
-                              workspace=ws, stream=stream, precision=precision)
-        ev[i][1].record(stream)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    elapsed = e0.elapsed_time(e1) / 1e3
-    attn_s = sum(a.elapsed_time(b) for a, b in ev) / 1e3 / args.steps
-    elapsed_max = max_over_ranks(elapsed)
-    attn_max = max_over_ranks(attn_s)
+
+    def step(i):
+        db.write()
+        if i is not None:
+            ev[i][0].record(stream)
+        db.attend()
+        if i is not None:
+            ev[i][1].record(stream)
+
+    elapsed_max, elapsed_mine, clocks_dev = timed_leg(step, args.steps, warm, stream, ranks,
+                                                      sampler)
+    launches += db.launches() * args.steps
+    if nvllm.get_last_error(stream) != nvllm.OK:
+        raise RuntimeError("device status after the timed steps is not OK")
+    attn_mine = sum(a.elapsed_time(b) for a, b in ev) / 1e3 / args.steps
+    alg_bytes = spec.decode_algorithmic_bytes()
+
+    # ---- the same step back to back for >= 1.5 s: a clock record of sustained load
+    sus_steps = int(min(20000, max(args.steps, math.ceil(1.5 / max(elapsed_mine / args.steps,
+                                                                    1e-6)))))
+    sus_steps = int(ranks.max(sus_steps))
+    sus_max, _, clocks_sus = timed_leg(lambda i: db.step(), sus_steps, 0, stream, ranks,
+                                       sampler)
+    launches_sus = db.launches() * sus_steps
 
     # ---- end to end through the engine's C ABI with host buffers ---------
     # per step: pack + one pinned upload of the metadata, H2D of the Q/K/V rows
     # from the engine's pinned buffers, KV write + attention, D2H of the output
     torch.cuda.synchronize(dev)
     h_q, h_k, h_v, h_out = (b[:n] for b in eng.pinned)
-    h_q[:] = q.cpu().numpy()
-    h_k[:] = k.cpu().numpy()
-    h_v[:] = v.cpu().numpy()
+    h_q[:] = db.q.cpu().numpy()
+    h_k[:] = db.k.cpu().numpy()
+    h_v[:] = db.v.cpu().numpy()
     nc = np.ascontiguousarray(spec.ctx_lens - spec.q_lens, np.int32)
     tl = np.ascontiguousarray(spec.ctx_lens, np.int32)
     nbs = (spec.ctx_lens + spec.block_size - 1) // spec.block_size
@@ -411,31 +548,45 @@ def nvllm_main(args, spec):
     d2h = n * D * 4
     estream = torch.cuda.ExternalStream(eng.stream(), device=dev)
 
-    def e2e_step():
+    def e2e_step(i):
         eng.begin_step_raw(nc, tl, ids, lens)
         eng.attention(0, h_q, h_k, h_v, h_out, precision)
 
-    for _ in range(max(args.warmup, 3)):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    barrier()
-    torch.cuda.synchronize(dev)
-    f0 = torch.cuda.Event(enable_timing=True)
-    f1 = torch.cuda.Event(enable_timing=True)
-    f0.record(estream)
-    for _ in range(args.steps):
-        e2e_step()
-    f1.record(estream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_elapsed = max_over_ranks(f0.elapsed_time(f1) / 1e3)
-    clocks = sampler.stop()
+    e2e_elapsed, _, clocks_e2e = timed_leg(e2e_step, args.steps, warm, estream, ranks, sampler)
+    launches += db.launches() * args.steps
     status = nvllm.get_last_error(stream)
     if status != nvllm.OK:
         raise RuntimeError(f"device status {nvllm.status_string(status)}")
-    del ka, va  # views of the engine's arenas
-    eng.close()
+    e2e_diff = float(np.abs(h_out - db.out.cpu().numpy()).max())
 
+    # ---- parity of the timed batch, after its timed regions and before the
+    # other batches below write into the same arenas
+    parity = None
+    if not args.no_parity:
+        seqs = list(range(spec.num_seqs)) if world == 1 else list(range(0, spec.num_seqs, 8))
+        pr = oracle_parity(db, seqs)
+        worst = ranks.max(pr["max_abs"])
+        parity = {"max_abs": worst, "tol": 2e-5, "ok": worst <= 2e-5,
+                  "rows_per_rank": pr["rows"], "seqs_per_rank": pr["seqs"],
+                  "e2e_output_max_abs_vs_device_output": ranks.max(e2e_diff),
+                  "oracle": "C restatement of the reference's attention loop, on the output "
+                            "of the last timed step"}
+
+    # ---- the other benchmark batches (outside `value`) --------------------
+    extra = {}
+    if args.workload == "decode" and not args.no_extra:
+        extra["mixed"] = mixed_leg(args, nvllm, lay, ka, va, dev, stream, ranks, sampler, rank)
+        extra["head_split"] = headsplit_leg(args, nvllm, dev, stream, ranks, sampler, rank,
+                                            world)
+    t_last = time.monotonic()
+    clocks_all = sampler.window(t_first, t_last)
+    sampler.stop()
+
+    # ---- per-rank figures; the roofline from the slowest rank's own bytes --
+    per_rank = ranks.gather([alg_bytes, elapsed_mine, attn_mine])
+    slow = max(range(len(per_rank)), key=lambda r: per_rank[r][2])
+    attn_max = per_rank[slow][2]
+    achieved = per_rank[slow][0] / attn_max / 1e9
     tokens = n * args.steps * world
     value = tokens / elapsed_max
     e2e_value = tokens / e2e_elapsed
@@ -444,54 +595,185 @@ def nvllm_main(args, spec):
     peak_src = "measured" if peak else "fallback"
     if not peak:
         peak = FALLBACK_HBM_GBS
-    alg_bytes = spec.decode_algorithmic_bytes()
-    achieved = alg_bytes / attn_max / 1e9
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic", "config": {**workload_config(spec), "prefill_precision": args.precision,
-                                        "parallelism": f"sequence-partitioned x{world}"},
+        "data": "synthetic", "config": workload_config(spec),
+        "parallelism": f"sequence-partitioned x{world} (equal KV bytes per GPU)",
+        "prefill_precision": args.precision,
         "hbm_gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_src,
                      "kernel": "nvllm_paged_attention (plan + split-K decode + merge)",
-                     "algorithmic_bytes_per_launch": alg_bytes,
-                     "ms_per_launch": attn_max * 1e3,
+                     "algorithmic_bytes_per_launch": per_rank[slow][0],
+                     "ms_per_launch": attn_max * 1e3, "rank": slow,
                      "traffic": profile_traffic(spec.name)},
+        "per_rank": [{"rank": r, "algorithmic_bytes": b_, "ms_per_step": t_ / args.steps * 1e3,
+                      "attention_ms": a_ * 1e3, "hbm_frac": b_ / a_ / 1e9 / peak}
+                     for r, (b_, t_, a_) in enumerate(per_rank)],
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "path": "libnvllm_host engine C ABI: nvllm_engine_begin_step + "
                         "nvllm_engine_attention (host rows)"},
-        "gpu_launches": KERNELS_PER_STEP * args.steps * 2 + (args.steps if max_q > 1 else 0) * 2,
-        "clocks": clocks,
+        "gpu_launches": launches,
+        "clocks": clocks_all,
+        "clocks_by_region": {"device": clocks_dev, "sustained": clocks_sus, "e2e": clocks_e2e},
+        "sustained": {"steps": sus_steps, "ms_per_step": sus_max / sus_steps * 1e3,
+                      "value": n * sus_steps * world / sus_max, "gpu_launches": launches_sus,
+                      "note": "the same step back to back for >= 1.5 s after the timed steps; "
+                              "its clock record is clocks_by_region.sustained"},
+        "parity": parity,
     }
+    if extra:
+        line["extra"] = extra
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle.oracle import reference_available
         try:
             if reference_available():
                 r = reference_time(spec, steps=50, warmup=1, budget_s=12.0)
-                kind = "reference"
-            else:
-                r = None
-                kind = None
-            if r is not None:
                 line["cpu_baseline"] = {
                     "value": r["tokens_per_s"], "unit": UNIT, "cores": r["threads"],
-                    "kind": kind,
+                    "kind": "reference",
                     "sample": f"{r['steps']} calls of the full {r['num_seqs']}-sequence batch "
                               f"(~12 s of CPU work); KV {r['kv_gbs']:.1f} GB/s"}
             else:
                 line["cpu_baseline"] = None
         except Exception as exc:  # reported, never fatal
             line["cpu_baseline"] = {"error": str(exc)}
+    del db, ka, va  # views of the engine's arenas
+    eng.close()
     if rank == 0:
         print(json.dumps(line))
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def mixed_leg(args, nvllm, lay, ka, va, dev, stream, ranks: Ranks, sampler, rank: int) -> dict:
+    """The mixed prefill + decode super-batch (8 causal prefills U[512, 2048] +
+    120 decodes with contexts U[256, 8192]) on the same arenas: the whole step
+    with tensor-core (3xTF32) and with fp32 prefill tiles, and its two parts
+    alone (prefills; decodes), each timed like the main leg. Per part: the
+    prefill's QK^T + PV FLOPs per second, the decode's algorithmic bytes per
+    second. A sample of the step's rows is checked against the oracle."""
+    import torch
+    from nvllm.workload import make_batch
+    spec = make_batch("mixed", seed=args.seed, rank=rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3000 + rank)
+    full = DeviceBatch(nvllm, spec, lay, ka, va, gen, dev, stream, nvllm.PRECISION_TF32)
+    pre_idx = np.flatnonzero(spec.q_lens > 1)
+    dec_idx = np.flatnonzero(spec.q_lens == 1)
+    pre = DeviceBatch(nvllm, spec.subset(pre_idx), lay, ka, va, gen, dev, stream,
+                      nvllm.PRECISION_TF32)
+    dec = DeviceBatch(nvllm, spec.subset(dec_idx), lay, ka, va, gen, dev, stream,
+                      nvllm.PRECISION_FP32)
+    warm = max(args.warmup, 3)
+    res = {"workload": "mixed prefill+decode super-batch (8 prefills U[512,2048] + 120 decodes "
+                       "ctx U[256,8192]), 32 heads x hd 128, block 16, 65536-block arena",
+           "rows_per_step": spec.n_tokens}
+    legs = (("step_tf32", lambda i: full.step(nvllm.PRECISION_TF32)),
+            ("step_fp32", lambda i: full.step(nvllm.PRECISION_FP32)),
+            ("prefill_tf32", lambda i: pre.step(nvllm.PRECISION_TF32)),
+            ("prefill_fp32", lambda i: pre.step(nvllm.PRECISION_FP32)),
+            ("decode", lambda i: dec.step()))
+    flops = spec.prefill_flops()
+    dec_bytes = spec.subset(dec_idx).decode_algorithmic_bytes()
+    for name, fn in legs:
+        t, _, clk = timed_leg(fn, args.steps, warm, stream, ranks, sampler)
+        ms = t / args.steps * 1e3
+        r = {"ms_per_step": ms, "clocks": clk}
+        if name.startswith("step"):
+            r["tokens_per_s"] = spec.n_tokens / (ms / 1e3)
+        if name.startswith("prefill"):
+            r["tflops"] = flops / (ms / 1e3) / 1e12
+        if name == "decode":
+            r["hbm_gbs"] = dec_bytes / (ms / 1e3) / 1e9
+        res[name] = r
+    res["prefill_flops_per_step"] = flops
+    res["decode_algorithmic_bytes_per_step"] = dec_bytes
+    status = nvllm.get_last_error(stream)
+    if status != nvllm.OK:
+        raise RuntimeError(f"mixed leg: device status {nvllm.status_string(status)}")
+    res["gpu_launches"] = args.steps * (2 * full.launches() + 2 * pre.launches() + dec.launches())
+    if not args.no_parity:
+        full.step(nvllm.PRECISION_TF32)
+        torch.cuda.synchronize(dev)
+        sample = list(pre_idx[:2]) + list(dec_idx[::15])
+        p = oracle_parity(full, sample)
+        p["max_abs"] = ranks.max(p["max_abs"])
+        res["parity"] = {**p, "tol": 1e-3, "ok": p["max_abs"] <= 1e-3,
+                         "precision": "tf32 prefill tiles"}
+    del full, pre, dec
+    torch.cuda.empty_cache()
+    return res
+
+
+def headsplit_leg(args, nvllm, dev, stream, ranks: Ranks, sampler, rank: int,
+                  world: int) -> dict:
+    """The long-context decode batch (4 sequences x 32768 positions) with its
+    32 heads split over the ranks (strong scaling): rank r holds heads
+    [r*H/N, (r+1)*H/N) in its own arena and runs
+    nvllm_paged_attention_head_split, whose merge epilogue stores every row
+    into all ranks' output buffers over NVLink; the NCCL variant (local
+    attention + all_gather_into_tensor) is timed beside it. With one GPU the
+    step is the plain attention call over all heads."""
+    import torch
+    from nvllm.workload import make_batch
+    spec = make_batch("longctx", seed=args.seed)
+    H, hd = spec.num_heads, spec.head_dim
+    Hl = H // world
+    lay = nvllm.KVLayout(spec.num_blocks, 1, spec.block_size, Hl, hd)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2000 + rank)
+    ka = torch.empty(lay.arena_shape(), device=dev).normal_(generator=gen)
+    va = torch.empty_like(ka).normal_(generator=gen)
+    db = DeviceBatch(nvllm, spec, lay, ka, va, gen, dev, stream, nvllm.PRECISION_FP32)
+    warm = max(args.warmup, 3)
+    res = {"workload": "long-context decode (4 seqs x 32768 ctx), heads split over the GPUs",
+           "heads_per_gpu": Hl, "scaling": "strong"}
+    per_gpu_bytes = spec.kv_bytes() / world
+    if world == 1:
+        t, _, clk = timed_leg(lambda i: db.step(), args.steps, warm, stream, ranks, sampler)
+        res["fused"] = {"ms_per_step": t / args.steps * 1e3, "clocks": clk}
+        res["gpu_launches"] = db.launches() * args.steps
+    else:
+        from nvllm.headsplit import HeadSplitGroup
+        dist = ranks.dist
+        grp = HeadSplitGroup(dist, n_rows=spec.n_tokens, local_cols=Hl * hd, device=dev)
+        gathered = torch.empty((world, spec.n_tokens, Hl * hd), device=dev)
+
+        def fused(i):
+            db.write()
+            grp.attention(db.q, ka, va, db.bt, db.cu, db.ctx, db.max_ctx, 0, lay,
+                          workspace=db.ws, stream=stream)
+
+        def nccl(i):
+            db.step()
+            dist.all_gather_into_tensor(gathered, db.out)
+
+        t, _, clk = timed_leg(fused, args.steps, warm, stream, ranks, sampler)
+        res["fused"] = {"ms_per_step": t / args.steps * 1e3, "clocks": clk,
+                        "how": "merge epilogue stores rows into every rank's buffer over "
+                               "NVLink (peer stores), bounded flag wait"}
+        st = nvllm.get_last_error(stream)
+        t2, _, clk2 = timed_leg(nccl, args.steps, warm, stream, ranks, sampler)
+        res["nccl_allgather"] = {"ms_per_step": t2 / args.steps * 1e3, "clocks": clk2}
+        res["gpu_launches"] = args.steps * (db.launches() + 2 + db.launches())
+        torch.cuda.synchronize(dev)
+        grp.close(dist)
+        if st != nvllm.OK:
+            raise RuntimeError(f"head split: device status {nvllm.status_string(st)}")
+    ms = res["fused"]["ms_per_step"]
+    res["tokens_per_s"] = spec.n_tokens / (ms / 1e3)
+    res["hbm_gbs_per_gpu"] = per_gpu_bytes / (ms / 1e3) / 1e9
+    res["kv_bytes_per_gpu"] = per_gpu_bytes
+    del db, ka, va
+    torch.cuda.empty_cache()
+    return res
 
 
 def headsplit_main(args, spec):
@@ -1199,6 +1481,10 @@ def main() -> int:
                          "3xTF32 (fp32 quality); default tf32 for a serving workload whose "
                          "projections run on the tcgen05 GEMMs, else fp32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="decode workload: skip the mixed and head-split legs of `extra`")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle check of the timed batch after the timed regions")
     ap.add_argument("--head-split", action="store_true",
                     help="split the batch's heads over the ranks (long-context decode)")
     ap.add_argument("--shapes", nargs="*", default=None,

@@ -173,16 +173,19 @@ int nvllm_device_status_word(const uint32_t** word);
 
 /* The raw status word that the last nvllm_get_last_error call (in this process)
  * found nonzero and cleared: bit 1 NVLLM_ERR_TIMEOUT, bit 0 NVLLM_ERR_BOUNDS, bit
- * 2 inconsistent metadata; with a timeout, bits 8-14 name the kernel whose
+ * 2 inconsistent metadata; with a timeout, bits 8-15 name the kernel whose
  * bounded wait gave up (8 decode attention, 9 tensor-core prefill, 10
  * nvllm_gemm_tf32x3, 11 nvllm_gemm_skinny, 12 nvllm_gemm_decode_tc, 13 fp32
- * prefill, 14 nvllm_head_gather). 0 if none was seen. */
+ * prefill, 14 nvllm_head_gather's wait for every rank's rows, 15
+ * nvllm_paged_attention_head_split's). 0 if none was seen. */
 uint32_t nvllm_last_status_word(void);
 
 /* With that word, where the first bounded wait that gave up was: info[0] its
  * kernel bits (as above, | 1), info[1] a kernel-specific code (the role,
  * barrier and pipeline stage of the wait), info[2] the CTA, info[3] the low
- * word of the mbarrier at the time. All 0 when no wait gave up. */
+ * word of the mbarrier at the time. For the two cross-GPU flag waits (bits 14
+ * and 15) info[1] is the flag value awaited and info[3] the value last read.
+ * All 0 when no wait gave up. */
 int nvllm_last_timeout_info(uint32_t* info);
 
 /* Static string for a status code. */

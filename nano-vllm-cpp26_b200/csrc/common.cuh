@@ -20,6 +20,7 @@ enum : uint32_t {
     kStatusInGemmDecodeTc = 1u << 12,
     kStatusInPrefill = 1u << 13,
     kStatusInHeadGather = 1u << 14,
+    kStatusInHeadSplit = 1u << 15,  // the head split's wait for every rank's rows
 };
 
 extern __device__ uint32_t g_status;
@@ -35,6 +36,18 @@ __device__ __forceinline__ void record_timeout(uint32_t site, uint32_t where, co
         g_timeout_info[1] = where;
         g_timeout_info[2] = blockIdx.x;
         g_timeout_info[3] = static_cast<uint32_t>(*reinterpret_cast<const volatile uint64_t*>(bar));
+        __threadfence();
+    }
+}
+
+// The same record for a cross-GPU flag wait that gave up: the value awaited
+// and the value last read instead of the mbarrier fields.
+__device__ __forceinline__ void record_flag_timeout(uint32_t site, uint32_t target,
+                                                    uint32_t seen) {
+    if (atomicCAS(&g_timeout_info[0], 0u, site | 1u) == 0u) {
+        g_timeout_info[1] = target;
+        g_timeout_info[2] = blockIdx.x;
+        g_timeout_info[3] = seen;
         __threadfence();
     }
 }

@@ -73,6 +73,7 @@ __global__ void gather_wait_kernel(const uint32_t* flag, uint32_t target) {
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
         if (int32_t(v - target) >= 0) return;
         if (global_ns() - t0 > kWaitLimitNs) {
+            record_flag_timeout(kStatusInHeadGather, target, v);
             raise_status(kStatusTimeout | kStatusInHeadGather);
             return;
         }

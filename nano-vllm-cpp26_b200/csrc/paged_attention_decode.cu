@@ -495,7 +495,8 @@ __global__ void flag_wait_kernel(const uint32_t* flag, uint32_t target) {
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
         if (int32_t(v - target) >= 0) return;
         if (global_ns() - t0 > kWaitLimitNs) {
-            raise_status(kStatusTimeout | kStatusInDecode);
+            record_flag_timeout(kStatusInHeadSplit, target, v);
+            raise_status(kStatusTimeout | kStatusInHeadSplit);
             return;
         }
         __nanosleep(200);

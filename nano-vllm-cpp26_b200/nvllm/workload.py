@@ -15,6 +15,11 @@
 
 Context lengths and block tables come from numpy's PCG64 with the given seed;
 tensor values from torch's CUDA generator. No public dataset is involved.
+
+Sequence partitioning (one batch per GPU): rank r > 0 gets the same multiset of
+context lengths as rank 0, in an order and with block tables drawn from a
+generator seeded with (seed, r), so every GPU moves the same bytes and the
+curve over GPU counts measures the system rather than unequal batches.
 """
 from __future__ import annotations
 
@@ -82,6 +87,17 @@ class BatchSpec:
         return (self.kv_bytes() + self.n_tokens * self.hidden * 4 * 2 + int(nb.sum()) * 4 +
                 self.num_seqs * 8 + 4)
 
+    def subset(self, seqs) -> "BatchSpec":
+        """The batch restricted to the sequences ``seqs`` (same arena, same
+        tables)."""
+        seqs = np.asarray(seqs, np.int64)
+        nb = (self.ctx_lens[seqs] + self.block_size - 1) // self.block_size
+        width = max(int(nb.max()) if len(nb) else 1, 1)
+        return BatchSpec(name=self.name, num_heads=self.num_heads, head_dim=self.head_dim,
+                         block_size=self.block_size, num_blocks=self.num_blocks,
+                         ctx_lens=self.ctx_lens[seqs].copy(), q_lens=self.q_lens[seqs].copy(),
+                         block_tables=np.ascontiguousarray(self.block_tables[seqs, :width]))
+
     def prefill_flops(self) -> int:
         """QK^T + PV FLOPs of the multi-row sequences (causal)."""
         f = 0
@@ -105,7 +121,7 @@ def _tables(rng, ctx, block_size, num_blocks):
     return bt
 
 
-def make_batch(name: str = "decode", seed: int = 0) -> BatchSpec:
+def make_batch(name: str = "decode", seed: int = 0, rank: int = 0) -> BatchSpec:
     geo = WORKLOADS[name]
     rng = np.random.Generator(np.random.PCG64(seed))
     if name == "decode":
@@ -129,6 +145,14 @@ def make_batch(name: str = "decode", seed: int = 0) -> BatchSpec:
         ql = np.ones(4, np.int32)
     else:
         raise KeyError(name)
+    if rank:
+        # same lengths, another order within the prefill and the decode group,
+        # other physical blocks
+        rng = np.random.Generator(np.random.PCG64([seed, rank]))
+        pre = np.flatnonzero(ql > 1)
+        dec = np.flatnonzero(ql == 1)
+        order = np.concatenate([rng.permutation(pre), rng.permutation(dec)])
+        ctx, ql = ctx[order], ql[order]
     bt = _tables(rng, ctx, geo["block_size"], geo["num_blocks"])
     return BatchSpec(name=name, num_heads=geo["num_heads"], head_dim=geo["head_dim"],
                      block_size=geo["block_size"], num_blocks=geo["num_blocks"], ctx_lens=ctx,

@@ -44,10 +44,11 @@ def _torch():
 
 
 def build_batch(nv, *, seed, num_blocks, block_size, num_heads, head_dim, ctx_lens, q_lens,
-                num_layers=1, layer=0, arena_fill=True):
+                num_layers=1, layer=0, arena_fill=True, block_tables=None):
     """Device batch: arena filled with N(0,1), block tables from a seeded
-    permutation, the new tokens' K/V written by nvllm_reshape_and_cache, Q
-    N(0,1). Returns a dict of device tensors and host metadata."""
+    permutation (or the given ``block_tables``), the new tokens' K/V written by
+    nvllm_reshape_and_cache, Q N(0,1). Returns a dict of device tensors and host
+    metadata."""
     torch = _torch()
     dev = torch.device("cuda:0")
     gen = torch.Generator(device=dev)
@@ -67,15 +68,19 @@ def build_batch(nv, *, seed, num_blocks, block_size, num_heads, head_dim, ctx_le
     S = len(ctx_lens)
     nbs = (ctx_lens + block_size - 1) // block_size
     max_blocks = int(nbs.max())
-    hg = torch.Generator()
-    hg.manual_seed(seed)
-    perm = torch.randperm(num_blocks, generator=hg).numpy().astype(np.int32)
-    assert nbs.sum() <= num_blocks
-    bt = np.zeros((S, max_blocks), np.int32)
-    off = 0
-    for s in range(S):
-        bt[s, :nbs[s]] = perm[off:off + nbs[s]]
-        off += nbs[s]
+    if block_tables is None:
+        hg = torch.Generator()
+        hg.manual_seed(seed)
+        perm = torch.randperm(num_blocks, generator=hg).numpy().astype(np.int32)
+        assert nbs.sum() <= num_blocks
+        bt = np.zeros((S, max_blocks), np.int32)
+        off = 0
+        for s in range(S):
+            bt[s, :nbs[s]] = perm[off:off + nbs[s]]
+            off += nbs[s]
+    else:
+        bt = np.ascontiguousarray(block_tables, np.int32)
+        assert bt.shape[0] == S and bt.shape[1] >= max_blocks
     cu = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
     n = int(cu[-1])
     slots = np.zeros(n, np.int32)
@@ -106,9 +111,42 @@ def run_attention(nv, b, precision=0, workspace=None):
     return out
 
 
-def oracle_check(nv, oracle, b, out, seqs, tol=TOL_FP32):
-    """Copies the blocks of the chosen sequences into a compact host arena and
-    compares their output rows with the oracle."""
+def oracle_check(nv, oracle, b, out, seqs, tol=TOL_FP32, more=(), host_budget=2 << 30):
+    """Compares the output rows of the chosen sequences with the oracle.
+
+    The sequences go in groups whose blocks fit ``host_budget`` bytes of host
+    memory (K + V); each group's blocks are copied into a compact host arena and
+    the oracle attends them once. ``out`` is checked within ``tol`` and every
+    further ``(output, tol)`` pair of ``more`` (the same batch computed another
+    way) against the same oracle rows. Returns the largest error of ``out``."""
+    torch = _torch()
+    lay = b["lay"]
+    nbs = (b["ctx"] + lay.block_size - 1) // lay.block_size
+    row_bytes = 2 * lay.num_layers * lay.block_size * lay.num_heads * lay.head_dim * 4
+    groups, cur, cur_blocks = [], [], 0
+    for s in seqs:
+        if cur and (cur_blocks + int(nbs[s])) * row_bytes > host_budget:
+            groups.append(cur)
+            cur, cur_blocks = [], 0
+        cur.append(s)
+        cur_blocks += int(nbs[s])
+    if cur:
+        groups.append(cur)
+    worst = 0.0
+    for g in groups:
+        ref, q_rows = _oracle_rows(oracle, b, g)
+        for o, t in ((out, tol), *more):
+            got = o[torch.as_tensor(q_rows, device=o.device)].cpu().numpy()
+            err = float(np.abs(got - ref).max()) if len(q_rows) else 0.0
+            assert err <= t, f"sequences {g[0]}..{g[-1]}: max-abs {err} > {t}"
+            if o is out:
+                worst = max(worst, err)
+    return worst
+
+
+def _oracle_rows(oracle, b, seqs):
+    """The oracle's output rows for ``seqs`` (and their row indices in the
+    batch), from a compact host copy of the blocks those sequences use."""
     from oracle.oracle import KVLayout
     torch = _torch()
     lay = b["lay"]
@@ -129,15 +167,12 @@ def oracle_check(nv, oracle, b, out, seqs, tol=TOL_FP32):
         bt_c[j, :nbs[s]] = [remap[int(x)] for x in bt[s, :nbs[s]]]
         q_rows.extend(range(b["cu"][s], b["cu"][s + 1]))
         cu.append(len(q_rows))
-    q = b["q"].cpu().numpy()[q_rows]
+    q = b["q"][torch.as_tensor(q_rows, device=b["q"].device)].cpu().numpy()
     olay = KVLayout(len(used), lay.num_layers, lay.block_size, lay.num_heads, lay.head_dim)
     ref = oracle.paged_attention(q, ka, va, bt_c, np.array(cu, np.int32),
                                  b["ctx"][list(seqs)].astype(np.int32), b["layer"],
                                  1.0 / math.sqrt(lay.head_dim), olay)
-    got = out.cpu().numpy()[q_rows]
-    err = np.abs(got - ref).max()
-    assert err <= tol, f"max-abs {err} > {tol}"
-    return err
+    return ref, q_rows
 
 
 def test_decode_shape_vs_oracle(nv, oracle):
@@ -201,22 +236,24 @@ def test_long_context_decode(nv, oracle):
                     ctx_lens=ctx, q_lens=np.ones(4, np.int32))
     out = run_attention(nv, b)
     assert nv.get_last_error() == nv.OK
-    oracle_check(nv, oracle, b, out, [0, 3])
+    oracle_check(nv, oracle, b, out, [0, 1, 2, 3])
 
 
 def test_decode_benchmark_full_size(nv, oracle):
-    """64 sequences, contexts U[512, 4096], 65536-block arena (34 GB K+V):
-    sampled oracle check, finiteness, and bit-exact invariance of the output
-    under relocation of every physical block."""
+    """The decode benchmark's batch: 64 sequences, contexts U[512, 4096],
+    block tables from the seeded permutation of the 65536-block arena (34 GB
+    K+V) that the benchmark uses; every sequence against the oracle,
+    finiteness, and bit-exact invariance of the output under relocation of
+    every physical block."""
+    from nvllm.workload import make_batch
     torch = _torch()
-    rng = np.random.default_rng(0)
-    ctx = rng.integers(512, 4097, 64).astype(np.int32)
+    spec = make_batch("decode", seed=0)
     b = build_batch(nv, seed=16, num_blocks=65536, block_size=16, num_heads=32, head_dim=128,
-                    ctx_lens=ctx, q_lens=np.ones(64, np.int32))
+                    ctx_lens=spec.ctx_lens, q_lens=spec.q_lens, block_tables=spec.block_tables)
     out = run_attention(nv, b)
     assert nv.get_last_error() == nv.OK
     assert torch.isfinite(out).all()
-    oracle_check(nv, oracle, b, out, [0, 7, 21, 42, 63])
+    oracle_check(nv, oracle, b, out, list(range(64)))
     # relocate: physical block j -> perm[j]; tables rewritten accordingly
     g = torch.Generator()
     g.manual_seed(99)
@@ -231,6 +268,63 @@ def test_decode_benchmark_full_size(nv, oracle):
     b["bt_d"] = perm[b["bt_d"].long()].to(torch.int32)
     out2 = run_attention(nv, b)
     assert torch.equal(out, out2), "output must not depend on physical placement"
+
+
+def test_mixed_benchmark_full_size(nv, oracle):
+    """The mixed super-batch exactly as benchmarked: 8 fresh causal prefills of
+    U[512, 2048] rows + 120 decodes with contexts U[256, 8192], 32 heads x hd 128,
+    block size 16, block tables from the seeded permutation of the 65536-block
+    arena. All 128 sequences (8376 query rows) against the oracle, with fp32
+    prefill tiles (TOL_FP32) and with tensor-core 3xTF32 tiles (TOL_TF32)."""
+    from nvllm.workload import make_batch
+    torch = _torch()
+    spec = make_batch("mixed", seed=0)
+    assert spec.num_seqs == 128 and int((spec.q_lens > 1).sum()) == 8
+    b = build_batch(nv, seed=30, num_blocks=65536, block_size=16, num_heads=32, head_dim=128,
+                    ctx_lens=spec.ctx_lens, q_lens=spec.q_lens, block_tables=spec.block_tables)
+    ws = nv.alloc_workspace(spec.num_seqs, b["max_q"], b["max_ctx"], b["lay"],
+                            device=b["q"].device)
+    out = run_attention(nv, b, workspace=ws)
+    assert nv.get_last_error() == nv.OK
+    out_tc = run_attention(nv, b, precision=nv.PRECISION_TF32, workspace=ws)
+    assert nv.get_last_error() == nv.OK
+    assert torch.isfinite(out).all() and torch.isfinite(out_tc).all()
+    err = oracle_check(nv, oracle, b, out, list(range(spec.num_seqs)),
+                       more=[(out_tc, TOL_TF32)])
+    assert err <= TOL_FP32
+
+
+def test_longctx_benchmark_full_size(nv, oracle):
+    """The long-context batch as benchmarked (4 x 32768 positions, block tables
+    from the benchmark's seeded permutation): all 4 sequences against the
+    oracle, and every head-group slice of it (heads split over 2, 4 and 8
+    ranks, each slice attended on its own arena slice, as a rank of the head
+    split does) bit-identical to the matching columns of the whole."""
+    from nvllm.workload import make_batch
+    torch = _torch()
+    spec = make_batch("longctx", seed=0)
+    b = build_batch(nv, seed=31, num_blocks=spec.num_blocks, block_size=16, num_heads=32,
+                    head_dim=128, ctx_lens=spec.ctx_lens, q_lens=spec.q_lens,
+                    block_tables=spec.block_tables)
+    out = run_attention(nv, b)
+    assert nv.get_last_error() == nv.OK
+    oracle_check(nv, oracle, b, out, [0, 1, 2, 3])
+    hd = 128
+    for n in (2, 4, 8):
+        hl = 32 // n
+        for r in (0, n - 1):
+            cols = slice(r * hl * hd, (r + 1) * hl * hd)
+            lay = nv.KVLayout(spec.num_blocks, 1, 16, hl, hd)
+            ka = b["ka"][..., cols].contiguous()
+            va = b["va"][..., cols].contiguous()
+            q = b["q"][:, cols].contiguous()
+            part = torch.full_like(q, float("nan"))
+            nv.paged_attention(part, q, ka, va, b["bt_d"], b["cu_d"], b["ctx_d"], 1,
+                               b["max_ctx"], 0, lay)
+            torch.cuda.synchronize()
+            assert nv.get_last_error() == nv.OK
+            assert torch.equal(part, out[:, cols]), f"heads split {n} ways, rank {r}"
+            del ka, va
 
 
 def test_constant_values_give_constant_output(nv):

@@ -1,7 +1,8 @@
 """The multi-rank host logic on the CPU (gloo, world size 2): sequence
-partitioning gives each rank its own batch, the timing reduction takes the
-maximum over ranks, and the handle exchange of the head split gives every
-rank every peer's handles in rank order."""
+partitioning gives each rank its own batch of the same total size (the same
+context lengths in another order, other blocks), the timing reduction takes the
+maximum over ranks, and the handle exchange of the head split gives every rank
+every peer's handles in rank order."""
 import socket
 
 import numpy as np
@@ -28,8 +29,9 @@ def _worker(rank, world, port, q):
     try:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                                 world_size=world, timeout=datetime.timedelta(seconds=60))
-        spec = make_batch("decode", seed=rank)  # bench.py: rank r uses seed + r
-        mine = (rank, spec.ctx_lens.tolist(), bytes([rank]) * 64)
+        spec = make_batch("decode", seed=0, rank=rank)  # as bench.py builds rank r's batch
+        mine = (rank, spec.ctx_lens.tolist(), bytes([rank]) * 64, spec.block_tables[:, 0].tolist(),
+                spec.decode_algorithmic_bytes())
         every = [None] * world
         dist.all_gather_object(every, mine)
         t = torch.tensor([0.5 + rank], dtype=torch.float64)
@@ -59,6 +61,10 @@ def test_two_rank_host_logic():
         assert [e[0] for e in every] == list(range(world))  # rank order
         assert every[rank][2] == bytes([rank]) * 64
         assert tmax == pytest.approx(0.5 + world - 1)
-    ctxs = [np.array(e[1]) for e in results[0][1]]
+    every = results[0][1]
+    ctxs = [np.array(e[1]) for e in every]
     assert not np.array_equal(ctxs[0], ctxs[1])  # each rank serves its own sequences
+    assert np.array_equal(np.sort(ctxs[0]), np.sort(ctxs[1]))  # of the same lengths
+    assert every[0][3] != every[1][3]  # in other physical blocks
+    assert every[0][4] == every[1][4]  # so every GPU moves the same bytes
     assert all(((c >= 512) & (c <= 4096)).all() and len(c) == 64 for c in ctxs)
