@@ -103,6 +103,22 @@ int nvllm_engine_attention(nvllm_engine* e, int32_t layer, const float* q, const
 /* The engine's pinned row buffers (pass them to nvllm_engine_attention to skip
  * the staging copy), its device arenas and its CUDA stream. */
 int nvllm_engine_host_buffers(nvllm_engine* e, float** q, float** k, float** v, float** out);
+/* Pipelined host-row attention over two slots (no counterpart in the
+ * reference, whose attention is a synchronous CPU loop): fill a slot's pinned
+ * rows (nvllm_engine_slot_buffers, slot 0 or 1; slot 0's are those of
+ * nvllm_engine_host_buffers), then nvllm_engine_attention_submit queues, for
+ * the step begun last, their H2D on the engine's copy stream, the KV write +
+ * attention on its compute stream once they have landed, and the D2H of the
+ * output into the slot's pinned output buffer once the kernels are done, and
+ * returns without waiting; nvllm_engine_attention_collect waits for that
+ * output. Alternating slots lets one step's copies overlap the other step's
+ * kernels. A slot must be collected before its rows are refilled or it is
+ * submitted again; nvllm_engine_attention refuses while a slot is in flight. */
+int nvllm_engine_slot_buffers(nvllm_engine* e, int32_t slot, float** q, float** k, float** v,
+                              float** out);
+int nvllm_engine_attention_submit(nvllm_engine* e, int32_t layer, int32_t slot,
+                                  int32_t precision);
+int nvllm_engine_attention_collect(nvllm_engine* e, int32_t slot);
 int nvllm_engine_arenas(nvllm_engine* e, float** k_arena, float** v_arena);
 void* nvllm_engine_stream(nvllm_engine* e);
 int32_t nvllm_engine_step_tokens(const nvllm_engine* e);

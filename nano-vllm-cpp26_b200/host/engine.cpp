@@ -57,12 +57,7 @@ std::expected<void, EngineError> AttentionEngine::init() {
     }
     NVLLM_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&d_meta_), meta_capacity_));
 
-    const std::size_t rows_bytes = std::size_t(cfg_.max_tokens) * row_floats_ * sizeof(float);
-    NVLLM_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&d_rows_), 4 * rows_bytes));
-    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_q_), rows_bytes));
-    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_k_), rows_bytes));
-    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_v_), rows_bytes));
-    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_out_), rows_bytes));
+    if (auto r = init_slot(0); !r) return r;
 
     const int32_t max_ctx = cfg_.max_blocks_per_seq * L.block_size;
     ws_bytes_ = nvllm_paged_attention_workspace_size(cfg_.max_seqs, cfg_.max_tokens, max_ctx, &L);
@@ -72,20 +67,36 @@ std::expected<void, EngineError> AttentionEngine::init() {
     return {};
 }
 
+std::expected<void, EngineError> AttentionEngine::init_slot(int slot) {
+    if (d_rows_[slot] != nullptr) return {};
+    const std::size_t rows_bytes = std::size_t(cfg_.max_tokens) * row_floats_ * sizeof(float);
+    NVLLM_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&d_rows_[slot]), 4 * rows_bytes));
+    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_q_[slot]), rows_bytes));
+    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_k_[slot]), rows_bytes));
+    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_v_[slot]), rows_bytes));
+    NVLLM_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&h_out_[slot]), rows_bytes));
+    return {};
+}
+
 AttentionEngine::~AttentionEngine() {
     if (stream_ != nullptr) {
         cudaSetDevice(cfg_.device);
         cudaStreamSynchronize(stream_);
     }
+    if (copy_stream_ != nullptr) cudaStreamSynchronize(copy_stream_);
     for (int i = 0; i < 2; ++i) {
         if (meta_done_[i]) cudaEventDestroy(meta_done_[i]);
         if (h_meta_[i]) cudaFreeHost(h_meta_[i]);
+        for (cudaEvent_t ev : {in_ready_[i], out_ready_[i], out_done_[i]}) {
+            if (ev) cudaEventDestroy(ev);
+        }
+        for (float* p : {h_q_[i], h_k_[i], h_v_[i], h_out_[i]}) {
+            if (p) cudaFreeHost(p);
+        }
+        if (d_rows_[i]) cudaFree(d_rows_[i]);
     }
-    for (float* p : {h_q_, h_k_, h_v_, h_out_}) {
-        if (p) cudaFreeHost(p);
-    }
+    if (copy_stream_) cudaStreamDestroy(copy_stream_);
     if (d_meta_) cudaFree(d_meta_);
-    if (d_rows_) cudaFree(d_rows_);
     if (d_ws_) cudaFree(d_ws_);
     if (d_k_) cudaFree(d_k_);
     if (d_v_) cudaFree(d_v_);
@@ -151,26 +162,97 @@ std::expected<void, EngineError> AttentionEngine::attention(int32_t layer, const
                                                             const float* k, const float* v,
                                                             float* out, int32_t precision) {
     if (!have_step_) return std::unexpected(EngineError{EngineError::Kind::NoStep, 0});
+    if (in_flight_[0] || in_flight_[1]) {
+        return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    }
     NVLLM_CUDA_TRY(cudaSetDevice(cfg_.device));
     const std::size_t n = std::size_t(step_.num_tokens);
     if (n == 0) return {};
     const std::size_t bytes = n * row_floats_ * sizeof(float);
     const std::size_t stride = std::size_t(cfg_.max_tokens) * row_floats_;
-    float* dq = d_rows_;
-    float* dk = d_rows_ + stride;
-    float* dv = d_rows_ + 2 * stride;
-    float* dout = d_rows_ + 3 * stride;
+    float* dq = d_rows_[0];
+    float* dk = d_rows_[0] + stride;
+    float* dv = d_rows_[0] + 2 * stride;
+    float* dout = d_rows_[0] + 3 * stride;
     const float* srcs[3] = {q, k, v};
-    float* pinned[3] = {h_q_, h_k_, h_v_};
+    float* pinned[3] = {h_q_[0], h_k_[0], h_v_[0]};
     float* dsts[3] = {dq, dk, dv};
     for (int i = 0; i < 3; ++i) {
         if (srcs[i] != pinned[i]) std::memcpy(pinned[i], srcs[i], bytes);
         NVLLM_CUDA_TRY(cudaMemcpyAsync(dsts[i], pinned[i], bytes, cudaMemcpyHostToDevice, stream_));
     }
     if (auto r = attention_device(layer, dq, dk, dv, dout, precision); !r) return r;
-    NVLLM_CUDA_TRY(cudaMemcpyAsync(h_out_, dout, bytes, cudaMemcpyDeviceToHost, stream_));
+    NVLLM_CUDA_TRY(cudaMemcpyAsync(h_out_[0], dout, bytes, cudaMemcpyDeviceToHost, stream_));
     NVLLM_CUDA_TRY(cudaStreamSynchronize(stream_));
-    if (out != h_out_) std::memcpy(out, h_out_, bytes);
+    if (out != h_out_[0]) std::memcpy(out, h_out_[0], bytes);
+    return {};
+}
+
+std::expected<void, EngineError> AttentionEngine::slot_buffers(int32_t slot, float** q, float** k,
+                                                               float** v, float** out) {
+    if (slot < 0 || slot > 1) return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    NVLLM_CUDA_TRY(cudaSetDevice(cfg_.device));
+    if (auto r = init_slot(slot); !r) return r;
+    if (q) *q = h_q_[slot];
+    if (k) *k = h_k_[slot];
+    if (v) *v = h_v_[slot];
+    if (out) *out = h_out_[slot];
+    return {};
+}
+
+std::expected<void, EngineError> AttentionEngine::submit(int32_t layer, int32_t slot,
+                                                         int32_t precision) {
+    if (!have_step_) return std::unexpected(EngineError{EngineError::Kind::NoStep, 0});
+    if (slot < 0 || slot > 1 || in_flight_[slot]) {
+        return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    }
+    NVLLM_CUDA_TRY(cudaSetDevice(cfg_.device));
+    if (auto r = init_slot(slot); !r) return r;
+    if (copy_stream_ == nullptr) {
+        NVLLM_CUDA_TRY(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+        for (int i = 0; i < 2; ++i) {
+            for (cudaEvent_t* ev : {&in_ready_[i], &out_ready_[i], &out_done_[i]}) {
+                NVLLM_CUDA_TRY(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
+            }
+        }
+    }
+    const std::size_t n = std::size_t(step_.num_tokens);
+    const std::size_t bytes = n * row_floats_ * sizeof(float);
+    const std::size_t stride = std::size_t(cfg_.max_tokens) * row_floats_;
+    float* dq = d_rows_[slot];
+    float* dk = dq + stride;
+    float* dv = dq + 2 * stride;
+    float* dout = dq + 3 * stride;
+    // The slot's device rows were last read by its previous kernels and its
+    // output copied out after them, both ordered before these copies (the
+    // previous D2H is on this copy stream, after that step's out_ready).
+    if (n > 0) {
+        NVLLM_CUDA_TRY(cudaMemcpyAsync(dq, h_q_[slot], bytes, cudaMemcpyHostToDevice, copy_stream_));
+        NVLLM_CUDA_TRY(cudaMemcpyAsync(dk, h_k_[slot], bytes, cudaMemcpyHostToDevice, copy_stream_));
+        NVLLM_CUDA_TRY(cudaMemcpyAsync(dv, h_v_[slot], bytes, cudaMemcpyHostToDevice, copy_stream_));
+    }
+    NVLLM_CUDA_TRY(cudaEventRecord(in_ready_[slot], copy_stream_));
+    NVLLM_CUDA_TRY(cudaStreamWaitEvent(stream_, in_ready_[slot], 0));
+    if (n > 0) {
+        if (auto r = attention_device(layer, dq, dk, dv, dout, precision); !r) return r;
+    }
+    NVLLM_CUDA_TRY(cudaEventRecord(out_ready_[slot], stream_));
+    NVLLM_CUDA_TRY(cudaStreamWaitEvent(copy_stream_, out_ready_[slot], 0));
+    if (n > 0) {
+        NVLLM_CUDA_TRY(cudaMemcpyAsync(h_out_[slot], dout, bytes, cudaMemcpyDeviceToHost,
+                                       copy_stream_));
+    }
+    NVLLM_CUDA_TRY(cudaEventRecord(out_done_[slot], copy_stream_));
+    in_flight_[slot] = true;
+    return {};
+}
+
+std::expected<void, EngineError> AttentionEngine::collect(int32_t slot) {
+    if (slot < 0 || slot > 1 || !in_flight_[slot]) {
+        return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    }
+    in_flight_[slot] = false;
+    NVLLM_CUDA_TRY(cudaEventSynchronize(out_done_[slot]));
     return {};
 }
 

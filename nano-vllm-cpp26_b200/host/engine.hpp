@@ -59,10 +59,10 @@ public:
     float* v_arena() noexcept { return d_v_; }
     cudaStream_t stream() noexcept { return stream_; }
     // pinned staging for one layer's rows ([max_tokens, H*hd] each)
-    float* host_query() noexcept { return h_q_; }
-    float* host_key() noexcept { return h_k_; }
-    float* host_value() noexcept { return h_v_; }
-    float* host_output() noexcept { return h_out_; }
+    float* host_query() noexcept { return h_q_[0]; }
+    float* host_key() noexcept { return h_k_[0]; }
+    float* host_value() noexcept { return h_v_[0]; }
+    float* host_output() noexcept { return h_out_[0]; }
     const MetadataLayout& step() const noexcept { return step_; }
     bool has_step() const noexcept { return have_step_; }
     // the step's packed metadata on the device (offsets in step())
@@ -89,9 +89,25 @@ public:
                                                       const float* d_k, const float* d_v,
                                                       float* d_out, int32_t precision);
 
+    // Pipelined host rows, two slots. submit(layer, slot) queues, for the step
+    // begun last, the H2D of the slot's pinned Q/K/V rows on a copy stream, the
+    // KV write + attention on stream() once they have landed, and the D2H of the
+    // output into the slot's pinned output buffer on the copy stream once the
+    // kernels are done; it returns without waiting. collect(slot) waits for that
+    // output. While one slot's kernels run, the other slot's copies proceed, so
+    // the copies of consecutive steps overlap the kernels. A slot must be
+    // collected before it is submitted again (its pinned rows stay in use until
+    // then); the synchronous attention() refuses while a slot is in flight.
+    std::expected<void, EngineError> submit(int32_t layer, int32_t slot, int32_t precision);
+    std::expected<void, EngineError> collect(int32_t slot);
+    // pinned rows of a slot ([max_tokens, H*hd] each); slot 0's are host_query() etc.
+    std::expected<void, EngineError> slot_buffers(int32_t slot, float** q, float** k, float** v,
+                                                  float** out);
+
 private:
     explicit AttentionEngine(const EngineConfig& cfg);
     std::expected<void, EngineError> init();
+    std::expected<void, EngineError> init_slot(int slot);
 
     EngineConfig cfg_;
     BlockAllocator allocator_;
@@ -108,12 +124,19 @@ private:
     unsigned char* d_meta_ = nullptr;
     float* d_k_ = nullptr;
     float* d_v_ = nullptr;
-    float* d_rows_ = nullptr;  // Q, K, V, out rows on the device
+    // per slot: Q, K, V, out rows on the device and their pinned host copies
+    // (slot 1 is allocated on its first use)
+    float* d_rows_[2] = {nullptr, nullptr};
     void* d_ws_ = nullptr;
-    float* h_q_ = nullptr;
-    float* h_k_ = nullptr;
-    float* h_v_ = nullptr;
-    float* h_out_ = nullptr;
+    float* h_q_[2] = {nullptr, nullptr};
+    float* h_k_[2] = {nullptr, nullptr};
+    float* h_v_[2] = {nullptr, nullptr};
+    float* h_out_[2] = {nullptr, nullptr};
+    cudaStream_t copy_stream_ = nullptr;  // the pipelined path's H2D and D2H
+    cudaEvent_t in_ready_[2] = {nullptr, nullptr};   // slot's rows landed
+    cudaEvent_t out_ready_[2] = {nullptr, nullptr};  // slot's kernels done
+    cudaEvent_t out_done_[2] = {nullptr, nullptr};   // slot's output back on the host
+    bool in_flight_[2] = {false, false};
 };
 
 }  // namespace nvllm

@@ -292,6 +292,26 @@ int nvllm_engine_host_buffers(nvllm_engine* e, float** q, float** k, float** v, 
     return NVLLM_OK;
 }
 
+int nvllm_engine_slot_buffers(nvllm_engine* e, int32_t slot, float** q, float** k, float** v,
+                              float** out) {
+    if (e == nullptr) return NVLLM_ERR_INVALID;
+    auto r = e->impl->slot_buffers(slot, q, k, v, out);
+    return r ? NVLLM_OK : engine_status(r.error());
+}
+
+int nvllm_engine_attention_submit(nvllm_engine* e, int32_t layer, int32_t slot,
+                                  int32_t precision) {
+    if (e == nullptr) return NVLLM_ERR_INVALID;
+    auto r = e->impl->submit(layer, slot, precision);
+    return r ? NVLLM_OK : engine_status(r.error());
+}
+
+int nvllm_engine_attention_collect(nvllm_engine* e, int32_t slot) {
+    if (e == nullptr) return NVLLM_ERR_INVALID;
+    auto r = e->impl->collect(slot);
+    return r ? NVLLM_OK : engine_status(r.error());
+}
+
 int nvllm_engine_arenas(nvllm_engine* e, float** k_arena, float** v_arena) {
     if (e == nullptr) return NVLLM_ERR_INVALID;
     if (k_arena) *k_arena = e->impl->k_arena();

@@ -123,6 +123,10 @@ def host_lib() -> ctypes.CDLL:
     L.nvllm_engine_attention.argtypes = [_vp, ctypes.c_int32, _f32p, _f32p, _f32p, _f32p,
                                          ctypes.c_int32]
     L.nvllm_engine_host_buffers.argtypes = [_vp] + [ctypes.POINTER(_f32p)] * 4
+    L.nvllm_engine_slot_buffers.argtypes = [_vp, ctypes.c_int32] + [ctypes.POINTER(_f32p)] * 4
+    L.nvllm_engine_attention_submit.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32,
+                                                ctypes.c_int32]
+    L.nvllm_engine_attention_collect.argtypes = [_vp, ctypes.c_int32]
     L.nvllm_engine_arenas.argtypes = [_vp, ctypes.POINTER(_f32p), ctypes.POINTER(_f32p)]
     L.nvllm_engine_stream.restype = _vp
     L.nvllm_engine_stream.argtypes = [_vp]
@@ -322,6 +326,29 @@ class Engine:
                                            _ptr(v, _f32p), _ptr(out, _f32p), precision)
         if rc != OK:
             raise NvllmError(rc, "nvllm_engine_attention")
+
+    def slot_pinned(self, slot: int):
+        """numpy views of a pipeline slot's pinned Q, K, V and output rows
+        ([max_tokens, hidden] each; slot 0's are ``pinned``)."""
+        bufs = [_f32p() for _ in range(4)]
+        rc = self.L.nvllm_engine_slot_buffers(self.h, slot, *[ctypes.byref(b) for b in bufs])
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_engine_slot_buffers")
+        d = self.layout.hidden
+        return [np.ctypeslib.as_array(b, shape=(self.max_tokens, d)) for b in bufs]
+
+    def submit(self, layer: int, slot: int, precision: int = 0) -> None:
+        """Queues the slot's rows through KV write + attention for the step
+        begun last (nvllm_engine_attention_submit); returns at once."""
+        rc = self.L.nvllm_engine_attention_submit(self.h, layer, slot, precision)
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_engine_attention_submit")
+
+    def collect(self, slot: int) -> None:
+        """Waits until the slot's output rows are in its pinned output buffer."""
+        rc = self.L.nvllm_engine_attention_collect(self.h, slot)
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_engine_attention_collect")
 
     def arenas(self):
         k, v = _f32p(), _f32p()

@@ -90,3 +90,60 @@ def test_engine_allocator_and_errors():
             eng.begin_step([0], [8], [[0]])
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("name", ["mixed_h4_hd32_b4", "mixed_h32_hd128_b16"])
+def test_engine_pipelined_slots_match_golden(name):
+    """The two-slot pipeline (nvllm_engine_attention_submit / _collect): the
+    step's layers go alternately to slots 0 and 1, each slot collected only
+    before its reuse, so one layer's copies overlap the other's kernels; every
+    layer's output equals the reference's. A busy slot and the synchronous
+    path are refused while a slot is in flight."""
+    import nvllm
+    from nvllm.host import Engine
+    case = golden_case(name)
+    g = load_golden(name)
+    lay = nvllm.KVLayout(case.num_blocks, case.num_layers, case.block_size, case.num_heads,
+                         case.head_dim)
+    n_hist = int(case.num_computed.sum())
+    eng = Engine(lay, max_seqs=len(case.total_len), max_tokens=max(n_hist, case.n_tokens, 1),
+                 max_blocks_per_seq=case.block_tables.shape[1], device=0)
+    tables = _tables(case)
+    try:
+        if n_hist:
+            eng.begin_step(np.zeros_like(case.num_computed), case.num_computed, tables)
+            junk = np.zeros((n_hist, case.hidden), np.float32)
+            for layer in range(case.num_layers):
+                eng.attention(layer, junk, case.hist_k[layer], case.hist_v[layer], junk.copy())
+        eng.begin_step(case.num_computed, case.total_len, tables)
+        n = case.n_tokens
+        slots = [eng.slot_pinned(0), eng.slot_pinned(1)]
+        outs = [None] * case.num_layers
+        pending = []  # (slot, layer)
+        for rep in range(2):  # the layers twice: slots reused across the step
+            for layer in range(case.num_layers):
+                slot = (rep * case.num_layers + layer) % 2
+                for s_, lay_ in list(pending):
+                    if s_ == slot:
+                        eng.collect(s_)
+                        outs[lay_] = slots[s_][3][:n].copy()
+                        pending.remove((s_, lay_))
+                q, k, v, o = slots[slot]
+                q[:n], k[:n], v[:n] = case.q[layer], case.k[layer], case.v[layer]
+                o[:n] = np.nan
+                eng.submit(layer, slot, 0)
+                pending.append((slot, layer))
+                with pytest.raises(nvllm.NvllmError):
+                    eng.submit(layer, slot, 0)  # in flight
+                with pytest.raises(nvllm.NvllmError):
+                    eng.attention(layer, q[:n], k[:n], v[:n], o[:n].copy())
+        for s_, lay_ in pending:
+            eng.collect(s_)
+            outs[lay_] = slots[s_][3][:n].copy()
+        with pytest.raises(nvllm.NvllmError):
+            eng.collect(0)  # nothing in flight
+        assert nvllm.get_last_error(eng.stream()) == nvllm.OK
+        err = np.abs(np.stack(outs) - g["attn_out"]).max()
+        assert err <= TOL_FP32, f"{name}: pipelined engine vs reference max-abs {err}"
+    finally:
+        eng.close()
