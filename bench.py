@@ -909,9 +909,9 @@ def headsplit_main(args, spec):
 # ---------------------------------------------------------------------------
 # serving: the reference's engine loop (scheduler + forward_batch) end to end
 
-SERVE_WORKLOADS = ("serve", "serve_toy", "serve_toy_seeded")
+SERVE_WORKLOADS = ("serve", "serve_toy", "serve_toy_seeded", "serve_router")
 SERVE_METRIC = "e2e serving output tokens/s (continuous batching, greedy)"
-SERVE_DEFAULT_STEPS = {"serve": 3, "serve_toy": 10, "serve_toy_seeded": 10}
+SERVE_DEFAULT_STEPS = {"serve": 3, "serve_toy": 10, "serve_toy_seeded": 10, "serve_router": 2}
 
 
 def model_flops(model: dict, tokens_computed: int, rows_sampled: int) -> float:
@@ -1115,6 +1115,137 @@ def serve_main(args):
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def serve_router_main(args):
+    """Config-5 serving over the GPUs of one box through nvllm_router: one
+    stream of 128 x N requests (lognormal prompts, 16 / 512 completions) placed
+    by the router on the GPU with the least outstanding work; every GPU has its
+    own engine (arena, allocator), model, scheduler and engine thread, and
+    nothing is shared on the data path. One process drives the N devices (the
+    engine threads are C++); under torchrun rank 0 does and the other ranks
+    return. One step = one complete run of the stream; its time is taken on
+    every device with CUDA events on that device's engine stream (from before
+    the first request is placed to after the router went idle), max over the
+    devices."""
+    from nvllm.host import GEMM_TF32X3, Engine, Generator, Model, Router, host_lib
+    host_lib()
+    import torch
+    import nvllm
+    from nvllm.serving import make_serve, serve_config
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    n_gpu = args.gpus
+    if torch.cuda.device_count() < n_gpu:
+        raise RuntimeError(f"{n_gpu} GPUs asked for, {torch.cuda.device_count()} visible")
+    nvllm.lib()
+    spec = make_serve("serve", seed=args.seed, requests=128 * n_gpu)
+    need = sum((len(p_) + m_ + spec.block_size - 1) // spec.block_size
+               for p_, m_ in zip(spec.prompts, spec.max_new))
+    blocks = int(need * 1.25 / n_gpu) + 256  # a GPU's share with room for imbalance
+    lay = nvllm.KVLayout(blocks, spec.model["layers"], spec.block_size, spec.model["heads"],
+                         spec.model["head_dim"])
+    limits = spec.engine_limits()
+    precision = nvllm.PRECISION_TF32 if args.precision == "tf32" else nvllm.PRECISION_FP32
+    lanes = []
+    for d in range(n_gpu):
+        torch.cuda.set_device(d)
+        eng = Engine(lay, device=d, **limits)
+        model = Model(spec.model, eng, gemm_math=GEMM_TF32X3,
+                      graph_max_tokens=args.graph_max_tokens)
+        gen = Generator(eng, model, spec.max_batch, spec.max_tokens_per_step, spec.watermark,
+                        precision=precision)
+        lanes.append((eng, model, gen))
+    torch.cuda.set_device(0)
+    router = Router([g for _, _, g in lanes])
+    streams = [torch.cuda.ExternalStream(e.stream(), device=torch.device("cuda", d))
+               for d, (e, _, _) in enumerate(lanes)]
+    samplers = [ClockSampler(smi_device_id(d)).start() for d in range(n_gpu)]
+
+    def one_run(run: int):
+        base = (run + 1) * 1_000_000
+        for i, (p_, m_) in enumerate(zip(spec.prompts, spec.max_new)):
+            router.add_request(base + i, p_, m_)
+        router.wait_idle()
+
+    for r in range(args.warmup):
+        one_run(r)
+    for d in range(n_gpu):
+        torch.cuda.synchronize(d)
+    before = [router.metrics(d) for d in range(n_gpu)]
+    placed0 = [router.placed(d) for d in range(n_gpu)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(n_gpu)]
+    t0 = time.monotonic()
+    for d in range(n_gpu):
+        with torch.cuda.device(d):
+            ev[d][0].record(streams[d])
+    for r in range(args.steps):
+        one_run(args.warmup + r)
+    for d in range(n_gpu):
+        with torch.cuda.device(d):
+            ev[d][1].record(streams[d])
+    for d in range(n_gpu):
+        torch.cuda.synchronize(d)
+    t1 = time.monotonic()
+    per_dev = [ev[d][0].elapsed_time(ev[d][1]) / 1e3 for d in range(n_gpu)]
+    elapsed = max(per_dev)
+    clocks = [samplers[d].window(t0, t1) for d in range(n_gpu)]
+    for smp in samplers:
+        smp.stop()
+    after = [router.metrics(d) for d in range(n_gpu)]
+    for _, _, gen in lanes:
+        st = nvllm.get_last_error(gen.engine.stream())
+        if st != nvllm.OK:
+            raise RuntimeError(f"device status {nvllm.status_string(st)}")
+    gen_tok = [a.total_tokens_generated - b.total_tokens_generated for a, b in zip(after, before)]
+    out_tokens = sum(gen_tok)
+    assert out_tokens == spec.output_tokens * args.steps, (out_tokens, spec.output_tokens)
+    computed = sum(a.total_tokens_computed - b.total_tokens_computed
+                   for a, b in zip(after, before))
+    placed = [router.placed(d) - placed0[d] for d in range(n_gpu)]
+    value = out_tokens / elapsed
+    flops = model_flops(spec.model, computed, out_tokens)
+    peak = measured_peaks().get("bf16_tflops") or 1590.0
+    h2d = sum(a.h2d_bytes - b.h2d_bytes for a, b in zip(after, before)) // args.steps
+    d2h = sum(a.d2h_bytes - b.d2h_bytes for a, b in zip(after, before)) // args.steps
+    reasons = sorted({x for c in clocks for x in c["reasons"]})
+    sm = [c["sm_mhz"] for c in clocks if c["sm_mhz"]]
+    line = {
+        "metric": SERVE_METRIC, "value": value, "unit": UNIT, "n_gpus": n_gpu,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded prompts; LCG weights of the reference model)",
+        "config": {**serve_config(spec), "workload": "e2e serving, 4096-wide 4-layer model, "
+                   "one stream of 128 requests per GPU through the router"},
+        "parallelism": f"sequence-partitioned x{n_gpu} (router: least outstanding work)",
+        "gemm": "tf32x3", "prefill_precision": args.precision,
+        "graph_max_tokens": args.graph_max_tokens,
+        "per_gpu": [{"gpu": d, "requests": placed[d], "tokens_generated": gen_tok[d],
+                     "seconds": per_dev[d] / args.steps} for d in range(n_gpu)],
+        "roofline": {"bound": "tensor", "achieved": flops / elapsed / 1e12 / n_gpu,
+                     "peak": peak, "unit": "TFLOP/s", "frac": flops / elapsed / 1e12 / n_gpu / peak,
+                     "per": "GPU", "kernel": "whole engine iteration (fp32 projections dominate)",
+                     "traffic": None},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "libnvllm_host router C ABI (nvllm_router_add_request + "
+                        "nvllm_router_wait_idle); every engine iteration uploads its metadata "
+                        "and token ids and reads the sampled ids back"},
+        "gpu_launches": sum(a.kernel_launches - b.kernel_launches for a, b in zip(after, before)),
+        "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
+                   "sm_max_mhz": max((c["sm_max_mhz"] or 0) for c in clocks) or None,
+                   "reasons": reasons, "samples": sum(c["samples"] for c in clocks),
+                   "per_gpu": clocks},
+    }
+    router.close()
+    for eng, model, gen in lanes:
+        gen.close()
+        model.close()
+        eng.close()
+    print(json.dumps(line))
     return 0
 
 
@@ -1536,11 +1667,16 @@ def main() -> int:
         if args.steps is None:
             args.steps = SERVE_DEFAULT_STEPS[args.workload]
         if args.gemm is None:
-            args.gemm = "tf32x3" if args.workload == "serve" else "fp32"
+            args.gemm = "tf32x3" if args.workload in ("serve", "serve_router") else "fp32"
         if args.graph_max_tokens is None:
             args.graph_max_tokens = 0 if args.workload == "serve" and args.gemm != "tf32x3" else 512
         if args.precision is None:
             args.precision = "tf32" if args.gemm == "tf32x3" else "fp32"
+        if args.workload == "serve_router":
+            if args.impl == "reference":
+                args.workload = "serve"
+                return reference_serve_main(args)
+            return serve_router_main(args)
         return reference_serve_main(args) if args.impl == "reference" else serve_main(args)
     if args.steps is None:
         args.steps = 1000

@@ -267,6 +267,33 @@ int nvllm_generator_metrics(const nvllm_generator* g, nvllm_metrics* out);
  * (without the terminator), writing it when it fits in cap. */
 int64_t nvllm_metrics_to_json(const nvllm_metrics* m, char* buf, int64_t cap);
 
+/* ---- router: one request stream over the GPUs of a box -------------------
+ * Sequence partitioning: each generator (one per GPU, each with its own
+ * engine, arena, allocator, scheduler and model) gets its own engine thread
+ * and ingress queue, the counterpart of the reference engine's ingress queue
+ * and engine thread (src/engine.cpp:79-104, :163-246), one per device here.
+ * nvllm_router_add_request places a request on the GPU with the least
+ * outstanding work (rows still to run through the forward pass: uncomputed
+ * prompt tokens plus tokens still to generate, of what the GPU holds or has
+ * queued) and returns that GPU's index in gens. The generators must outlive the
+ * router and must not be used directly while it exists. */
+typedef struct nvllm_router nvllm_router;
+int nvllm_router_create(nvllm_generator* const* gens, int32_t n, nvllm_router** out);
+/* Stops and joins the engine threads (work still pending is dropped). */
+void nvllm_router_destroy(nvllm_router* r);
+int nvllm_router_add_request(nvllm_router* r, uint64_t seq_id, const int64_t* prompt,
+                             int64_t prompt_len, int64_t max_new_tokens, int32_t* gpu);
+/* Blocks until every GPU is idle with an empty queue; the error of a GPU whose
+ * loop failed (its thread stops; the others carry on). */
+int nvllm_router_wait_idle(nvllm_router* r);
+/* As nvllm_generator_output, for a finished request on whichever GPU served
+ * it; -1 while that GPU is busy, or for an unknown or unfinished request. */
+int64_t nvllm_router_output(nvllm_router* r, uint64_t seq_id, int64_t* tokens, int64_t cap);
+/* A GPU's telemetry as of its engine thread's last idle moment. */
+int nvllm_router_metrics(nvllm_router* r, int32_t gpu, nvllm_metrics* out);
+/* Requests placed on a GPU so far (-1 for a bad index). */
+int64_t nvllm_router_placed(const nvllm_router* r, int32_t gpu);
+
 /* ---- cross-process device buffers (head split) ---------------------------
  * nvllm_ipc_alloc: cudaMalloc of `bytes` on the current device, zero-filled,
  * and its 64-byte CUDA IPC handle. nvllm_ipc_open maps a peer process's buffer

@@ -80,6 +80,18 @@ void Generator::add_request(SeqId id, std::vector<int64_t> prompt, std::size_t m
     ++received_;
 }
 
+std::size_t Generator::outstanding_tokens() const noexcept {
+    auto rows = [](const Sequence& q) {
+        const std::size_t left = q.max_new_tokens > q.generated_len()
+                                     ? q.max_new_tokens - q.generated_len() : 0;
+        return (q.total_len() - q.num_computed) + left;
+    };
+    std::size_t n = 0;
+    for (const Sequence& q : sched_.running()) n += rows(q);
+    for (const Sequence& q : sched_.waiting()) n += rows(q);
+    return n;
+}
+
 bool Generator::set_trace(const std::string& path) {
     if (trace_ != nullptr) {
         std::fclose(trace_);

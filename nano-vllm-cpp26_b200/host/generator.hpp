@@ -64,6 +64,11 @@ public:
     // Steps until no work is pending (or max_steps > 0 steps ran).
     std::expected<int64_t, EngineError> run(int64_t max_steps);
     bool has_pending_work() const noexcept { return sched_.has_pending_work(); }
+    // Rows still to run through the forward pass for the sequences it holds:
+    // their uncomputed tokens plus the tokens still to generate (the router's
+    // load measure).
+    std::size_t outstanding_tokens() const noexcept;
+    int32_t device() const noexcept { return eng_.config().device; }
 
     // Token list (prompt + generated) of a finished sequence, or nullptr.
     const std::vector<int64_t>* output(SeqId id) const;

@@ -11,6 +11,7 @@
 #include "metadata.hpp"
 #include "generator.hpp"
 #include "model.hpp"
+#include "router.hpp"
 #include "scheduler.hpp"
 
 struct nvllm_block_allocator {
@@ -32,6 +33,10 @@ struct nvllm_scheduler {
 
 struct nvllm_generator {
     std::unique_ptr<nvllm::Generator> impl;
+};
+
+struct nvllm_router {
+    std::unique_ptr<nvllm::Router> impl;
 };
 
 namespace {
@@ -499,16 +504,79 @@ int nvllm_generator_trace(nvllm_generator* g, const char* path) {
                                                                          : NVLLM_ERR_INVALID;
 }
 
-int nvllm_generator_metrics(const nvllm_generator* g, nvllm_metrics* out) {
-    if (g == nullptr || out == nullptr) return NVLLM_ERR_INVALID;
-    const nvllm::Metrics m = g->impl->metrics();
-    *out = nvllm_metrics{m.uptime_secs, m.total_requests_received, m.total_requests_completed,
+namespace {
+nvllm_metrics c_metrics(const nvllm::Metrics& m) {
+    return nvllm_metrics{m.uptime_secs, m.total_requests_received, m.total_requests_completed,
                          m.total_tokens_generated, m.throughput_tokens_per_sec,
                          m.active_batch_size, m.waiting_queue_depth, m.kv_cache_used_blocks,
                          m.kv_cache_total_blocks, m.kv_cache_utilization_pct, m.avg_ttft_ms,
                          m.avg_iteration_latency_ms, m.total_preemptions, m.total_iterations,
                          m.total_tokens_computed, m.h2d_bytes, m.d2h_bytes, m.kernel_launches};
+}
+}  // namespace
+
+int nvllm_generator_metrics(const nvllm_generator* g, nvllm_metrics* out) {
+    if (g == nullptr || out == nullptr) return NVLLM_ERR_INVALID;
+    *out = c_metrics(g->impl->metrics());
     return NVLLM_OK;
+}
+
+int nvllm_router_create(nvllm_generator* const* gens, int32_t n, nvllm_router** out) {
+    if (gens == nullptr || n <= 0 || out == nullptr) return NVLLM_ERR_INVALID;
+    std::vector<nvllm::Generator*> g;
+    for (int32_t i = 0; i < n; ++i) {
+        if (gens[i] == nullptr) return NVLLM_ERR_INVALID;
+        for (nvllm::Generator* other : g) {
+            if (other == gens[i]->impl.get()) return NVLLM_ERR_INVALID;  // one lane each
+        }
+        g.push_back(gens[i]->impl.get());
+    }
+    auto* h = new (std::nothrow) nvllm_router{std::make_unique<nvllm::Router>(g)};
+    if (h == nullptr) return NVLLM_ERR_INVALID;
+    *out = h;
+    return NVLLM_OK;
+}
+
+void nvllm_router_destroy(nvllm_router* r) { delete r; }
+
+int nvllm_router_add_request(nvllm_router* r, uint64_t seq_id, const int64_t* prompt,
+                             int64_t prompt_len, int64_t max_new_tokens, int32_t* gpu) {
+    std::vector<int64_t> p;
+    if (r == nullptr || !make_prompt(prompt, prompt_len, p)) return NVLLM_ERR_INVALID;
+    auto res = r->impl->add_request(seq_id, std::move(p),
+                                    std::size_t(std::max<int64_t>(max_new_tokens, 1)));
+    if (!res) return engine_status(res.error());
+    if (gpu != nullptr) *gpu = *res;
+    return NVLLM_OK;
+}
+
+int nvllm_router_wait_idle(nvllm_router* r) {
+    if (r == nullptr) return NVLLM_ERR_INVALID;
+    auto res = r->impl->wait_idle();
+    return res ? NVLLM_OK : engine_status(res.error());
+}
+
+int64_t nvllm_router_output(nvllm_router* r, uint64_t seq_id, int64_t* tokens, int64_t cap) {
+    if (r == nullptr) return -1;
+    const auto t = r->impl->output(seq_id);
+    if (!t) return -1;
+    if (tokens != nullptr && int64_t(t->size()) <= cap) {
+        std::memcpy(tokens, t->data(), t->size() * sizeof(int64_t));
+    }
+    return int64_t(t->size());
+}
+
+int nvllm_router_metrics(nvllm_router* r, int32_t gpu, nvllm_metrics* out) {
+    if (r == nullptr || out == nullptr || gpu < 0 || gpu >= r->impl->num_gpus()) {
+        return NVLLM_ERR_INVALID;
+    }
+    *out = c_metrics(r->impl->metrics(gpu));
+    return NVLLM_OK;
+}
+
+int64_t nvllm_router_placed(const nvllm_router* r, int32_t gpu) {
+    if (r == nullptr || gpu < 0 || gpu >= r->impl->num_gpus()) return -1;
+    return int64_t(r->impl->placed(gpu));
 }
 
 int64_t nvllm_metrics_to_json(const nvllm_metrics* m, char* buf, int64_t cap) {

@@ -127,6 +127,16 @@ def host_lib() -> ctypes.CDLL:
     L.nvllm_engine_attention_submit.argtypes = [_vp, ctypes.c_int32, ctypes.c_int32,
                                                 ctypes.c_int32]
     L.nvllm_engine_attention_collect.argtypes = [_vp, ctypes.c_int32]
+    L.nvllm_router_create.argtypes = [ctypes.POINTER(_vp), ctypes.c_int32, ctypes.POINTER(_vp)]
+    L.nvllm_router_destroy.argtypes = [_vp]
+    L.nvllm_router_add_request.argtypes = [_vp, ctypes.c_uint64, _i64p, ctypes.c_int64,
+                                           ctypes.c_int64, ctypes.POINTER(ctypes.c_int32)]
+    L.nvllm_router_wait_idle.argtypes = [_vp]
+    L.nvllm_router_output.restype = ctypes.c_int64
+    L.nvllm_router_output.argtypes = [_vp, ctypes.c_uint64, _i64p, ctypes.c_int64]
+    L.nvllm_router_metrics.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(Metrics)]
+    L.nvllm_router_placed.restype = ctypes.c_int64
+    L.nvllm_router_placed.argtypes = [_vp, ctypes.c_int32]
     L.nvllm_engine_arenas.argtypes = [_vp, ctypes.POINTER(_f32p), ctypes.POINTER(_f32p)]
     L.nvllm_engine_stream.restype = _vp
     L.nvllm_engine_stream.argtypes = [_vp]
@@ -568,3 +578,61 @@ class Generator:
         if rc != OK:
             raise NvllmError(rc, "nvllm_generator_metrics")
         return m
+
+
+class Router:
+    """One request stream over several generators (one per GPU), each with its
+    own engine thread (nvllm_router_*): requests go to the GPU with the least
+    outstanding work. The generators must stay open while the router exists
+    and are not to be used directly meanwhile."""
+
+    def __init__(self, generators):
+        self.L = host_lib()
+        self.generators = list(generators)
+        arr = (_vp * len(self.generators))(*[g.h for g in self.generators])
+        h = _vp()
+        rc = self.L.nvllm_router_create(arr, len(self.generators), ctypes.byref(h))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_router_create")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.nvllm_router_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def add_request(self, seq_id: int, prompt, max_new_tokens: int) -> int:
+        """Places the request; returns the index of the GPU that got it."""
+        p = np.ascontiguousarray(prompt, np.int64)
+        gpu = ctypes.c_int32()
+        rc = self.L.nvllm_router_add_request(self.h, seq_id, _ptr(p, _i64p), len(p),
+                                             max_new_tokens, ctypes.byref(gpu))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_router_add_request")
+        return gpu.value
+
+    def wait_idle(self) -> None:
+        rc = self.L.nvllm_router_wait_idle(self.h)
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_router_wait_idle")
+
+    def output(self, seq_id: int):
+        n = self.L.nvllm_router_output(self.h, seq_id, None, 0)
+        if n < 0:
+            return None
+        out = np.zeros(n, np.int64)
+        self.L.nvllm_router_output(self.h, seq_id, _ptr(out, _i64p), n)
+        return out
+
+    def metrics(self, gpu: int) -> Metrics:
+        m = Metrics()
+        rc = self.L.nvllm_router_metrics(self.h, gpu, ctypes.byref(m))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_router_metrics")
+        return m
+
+    def placed(self, gpu: int) -> int:
+        return self.L.nvllm_router_placed(self.h, gpu)

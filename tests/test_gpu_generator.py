@@ -102,3 +102,64 @@ def test_generator_step_by_step_and_preemption_count():
         gen.close()
         model.close()
         eng.close()
+
+
+@pytest.mark.parametrize("lanes", [2, 3])
+def test_router_serves_every_request_with_the_reference_stream(lanes):
+    """The reference benchmark's 96 requests through nvllm_router over several
+    generators, each with its own engine (arena, allocator, scheduler), model
+    and engine thread: on distinct GPUs where the box has them, else several on
+    cuda:0. Every request finishes on the GPU the router chose with the token
+    stream the reference produced for it; the requests spread over the lanes by
+    outstanding work."""
+    import torch
+
+    import nvllm
+    from nvllm.host import Engine, Generator, Model, Router
+    cfg, z, steps = load_trace("tokens_toy_bench")
+    max_batch, max_tokens, watermark = (int(x) for x in z["sched"])
+    prompts, max_new = trace_requests(z)
+    want = {i + 1: list(p) for i, p in enumerate(prompts)}
+    for st in steps:
+        for s, t in zip(st["seqs"], st["sampled"]):
+            want[s["seq_id"]].append(int(t))
+    longest = max(len(p) + m for p, m in zip(prompts, max_new))
+    B = int(z["block_size"])
+    lay = nvllm.KVLayout(int(z["num_blocks"]), cfg["layers"], B, cfg["heads"], cfg["head_dim"])
+    gpus = torch.cuda.device_count()
+    objs = []
+    try:
+        for i in range(lanes):
+            eng = Engine(lay, max_seqs=max_batch, max_tokens=max(max_tokens, longest),
+                         max_blocks_per_seq=(longest + B - 1) // B, device=i % gpus)
+            model = Model(cfg, eng, scales=z["scales"][:2])
+            gen = Generator(eng, model, max_batch, max_tokens, watermark)
+            objs.append((eng, model, gen))
+        router = Router([g for _, _, g in objs])
+        try:
+            placed = [router.add_request(i + 1, p, m)
+                      for i, (p, m) in enumerate(zip(prompts, max_new))]
+            router.wait_idle()
+            assert sorted(set(placed)) == list(range(lanes))
+            for lane in range(lanes):
+                assert router.placed(lane) == placed.count(lane)
+            for sid, stream in want.items():
+                got = router.output(sid)
+                assert got is not None and got.tolist() == stream, f"sequence {sid}"
+            total = 0
+            for lane in range(lanes):
+                m = router.metrics(lane)
+                assert m.total_requests_received == m.total_requests_completed
+                assert m.total_requests_completed == placed.count(lane)
+                assert m.active_batch_size == 0 and m.kv_cache_used_blocks == 0
+                total += m.total_tokens_generated
+            assert total == sum(max_new)
+            with pytest.raises(nvllm.NvllmError):
+                router.add_request(1, prompts[0], 4)  # id already used
+        finally:
+            router.close()
+    finally:
+        for eng, model, gen in objs:
+            gen.close()
+            model.close()
+            eng.close()
