@@ -374,7 +374,7 @@ class DeviceBatch:
         import torch
         self.nv, self.spec, self.lay, self.ka, self.va = nvllm, spec, lay, ka, va
         self.stream, self.precision = stream, precision
-        n, D = spec.n_tokens, spec.hidden
+        n, D = spec.n_tokens, lay.num_heads * lay.head_dim  # this GPU's heads
         self.q = torch.randn((n, D), generator=gen, device=dev)
         self.k = torch.randn((n, D), generator=gen, device=dev)
         self.v = torch.randn((n, D), generator=gen, device=dev)
@@ -636,7 +636,8 @@ def nvllm_main(args, spec):
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "path": "libnvllm_host engine C ABI: nvllm_engine_begin_step + "
-                        "nvllm_engine_attention (host rows)"},
+                        "nvllm_engine_attention_submit / _collect (host rows, two pipeline "
+                        "slots)"},
         "gpu_launches": launches,
         "clocks": clocks_all,
         "clocks_by_region": {"device": clocks_dev, "sustained": clocks_sus, "e2e": clocks_e2e},

@@ -86,8 +86,10 @@ cudaError_t launch_signal(uint32_t* const* flags, int n, cudaStream_t stream);
 // Waits (bounded) until *flag >= target; one thread.
 cudaError_t launch_flag_wait(const uint32_t* flag, uint32_t target, cudaStream_t stream);
 cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream);
-cudaError_t launch_prefill_fp32(const AttnParams& p, cudaStream_t stream);
-cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream);
+// max_sms > 0 bounds the persistent grid to that many SMs' worth of CTAs (the
+// rest of the GPU is left to a decode kernel running beside it); 0 = all SMs.
+cudaError_t launch_prefill_fp32(const AttnParams& p, cudaStream_t stream, int max_sms = 0);
+cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream, int max_sms = 0);
 bool prefill_tc_supported(const ArenaGeom& g);
 int32_t prefill_tc_tile_rows();
 

@@ -1,9 +1,12 @@
 // The extern "C" boundary of libnvllm.so (declared in include/nvllm.h):
 // argument validation, workspace carve-up and kernel dispatch.
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "../../include/nvllm.h"
 #include "common.cuh"
@@ -14,6 +17,8 @@ namespace nvllm {
 namespace {
 
 constexpr size_t kAlign = 256;
+// SMs for a prefill beside the decode by default (0: one after the other)
+constexpr int kDefaultPrefillSms = 0;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -165,7 +170,59 @@ int prepare_attention(AttnParams& p, const float* query, const float* k_arena,
     return NVLLM_OK;
 }
 
-// plan -> prefill (if any multi-row sequence) -> decode + merge
+// The prefill beside the decode: a high-priority stream per in-flight call
+// with the events that fork it from and join it back into the caller's stream.
+// Lanes are pooled per device; a lane goes back to the pool as soon as its
+// launches are queued (a later call that takes it queues behind them).
+struct SideLane {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_lanes_mu;
+std::vector<SideLane> g_lanes;  // idle lanes
+
+cudaError_t take_lane(int dev, SideLane& out) {
+    {
+        std::lock_guard<std::mutex> lk(g_lanes_mu);
+        for (std::size_t i = 0; i < g_lanes.size(); ++i) {
+            if (g_lanes[i].device == dev) {
+                out = g_lanes[i];
+                g_lanes.erase(g_lanes.begin() + std::ptrdiff_t(i));
+                return cudaSuccess;
+            }
+        }
+    }
+    int least = 0, greatest = 0;
+    cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    if (e != cudaSuccess) return e;
+    out.device = dev;
+    e = cudaStreamCreateWithPriority(&out.stream, cudaStreamNonBlocking, greatest);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&out.fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&out.join, cudaEventDisableTiming);
+    return e;
+}
+
+void give_lane(const SideLane& lane) {
+    std::lock_guard<std::mutex> lk(g_lanes_mu);
+    g_lanes.push_back(lane);
+}
+
+// SMs given to the prefill when it runs beside the decode (NVLLM_PREFILL_SMS:
+// a count of SMs; 0 = the prefill first on the whole GPU, then the decode).
+int prefill_beside_sms() {
+    static const int v = [] {
+        const char* s = std::getenv("NVLLM_PREFILL_SMS");
+        return s != nullptr ? std::max(0, std::atoi(s)) : kDefaultPrefillSms;
+    }();
+    return v;
+}
+
+// plan -> prefill (if any multi-row sequence) and decode + merge. With a
+// prefill share configured, the prefill runs on a bounded persistent grid on a
+// high-priority side stream while the decode's persistent grid takes the other
+// SMs and, as the prefill's CTAs retire, theirs: the HBM-bound decode and the
+// tensor-bound prefill overlap instead of running one after the other.
 cudaError_t launch_attention(AttnParams& p, int32_t precision, cudaStream_t st) {
     // TF32 prefill runs on the tensor cores where the kernel's geometry allows
     // (hd 128, block size 16); elsewhere the fp32 FFMA kernel serves it, whose
@@ -174,10 +231,31 @@ cudaError_t launch_attention(AttnParams& p, int32_t precision, cudaStream_t st) 
         precision == NVLLM_PRECISION_TF32 && p.max_query_len > 1 && prefill_tc_supported(p.g);
     if (tc_prefill) p.prefill_tile = prefill_tc_tile_rows();
     cudaError_t e = launch_plan(p, st);
-    if (e == cudaSuccess && p.max_query_len > 1) {
-        e = tc_prefill ? launch_prefill_tc(p, st) : launch_prefill_fp32(p, st);
+    if (e != cudaSuccess) return e;
+    const int beside = p.max_query_len > 1 ? prefill_beside_sms() : 0;
+    if (beside <= 0) {
+        if (p.max_query_len > 1) {
+            e = tc_prefill ? launch_prefill_tc(p, st) : launch_prefill_fp32(p, st);
+            if (e != cudaSuccess) return e;
+        }
+        return launch_decode(p, st);
     }
+    int dev = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    SideLane lane;
+    e = take_lane(dev, lane);
+    if (e != cudaSuccess) return e;
+    e = cudaEventRecord(lane.fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(lane.stream, lane.fork, 0);
+    if (e == cudaSuccess) {
+        e = tc_prefill ? launch_prefill_tc(p, lane.stream, beside)
+                       : launch_prefill_fp32(p, lane.stream, beside);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(lane.join, lane.stream);
     if (e == cudaSuccess) e = launch_decode(p, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, lane.join, 0);
+    give_lane(lane);
     return e;
 }
 

@@ -12,6 +12,8 @@
 //
 // Persistent grid: CTAs pull (item, head) pairs from the plan kernel's
 // prefill list (tiles with the most keys first within a sequence).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -293,7 +295,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_fp32_kernel(const 
 }
 
 template <int HD>
-cudaError_t launch_prefill_t(const AttnParams& p, cudaStream_t stream) {
+cudaError_t launch_prefill_t(const AttnParams& p, cudaStream_t stream, int max_sms) {
     constexpr size_t smem = PrefillShape<HD>::SMEM;
     static int grid_per_device[64] = {0};
     int dev = 0;
@@ -312,7 +314,14 @@ cudaError_t launch_prefill_t(const AttnParams& p, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         grid_per_device[dev] = sms * (per_sm > 0 ? per_sm : 1);
     }
-    prefill_fp32_kernel<HD><<<grid_per_device[dev], kPrefillThreads, smem, stream>>>(p);
+    int grid = grid_per_device[dev];
+    if (max_sms > 0) {
+        int sms = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        if (max_sms < sms) grid = std::max(1, grid / sms * max_sms);
+    }
+    prefill_fp32_kernel<HD><<<grid, kPrefillThreads, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -320,12 +329,12 @@ cudaError_t launch_prefill_t(const AttnParams& p, cudaStream_t stream) {
 
 int32_t prefill_tile_rows(int32_t /*head_dim*/) { return QT; }
 
-cudaError_t launch_prefill_fp32(const AttnParams& p, cudaStream_t stream) {
+cudaError_t launch_prefill_fp32(const AttnParams& p, cudaStream_t stream, int max_sms) {
     switch (p.g.head_dim) {
-        case 32: return launch_prefill_t<32>(p, stream);
-        case 64: return launch_prefill_t<64>(p, stream);
-        case 128: return launch_prefill_t<128>(p, stream);
-        case 256: return launch_prefill_t<256>(p, stream);
+        case 32: return launch_prefill_t<32>(p, stream, max_sms);
+        case 64: return launch_prefill_t<64>(p, stream, max_sms);
+        case 128: return launch_prefill_t<128>(p, stream, max_sms);
+        case 256: return launch_prefill_t<256>(p, stream, max_sms);
         default: return cudaErrorInvalidValue;
     }
 }

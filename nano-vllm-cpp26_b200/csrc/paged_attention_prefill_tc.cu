@@ -40,6 +40,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -517,7 +518,7 @@ bool prefill_tc_supported(const ArenaGeom& g) { return g.head_dim == kHD && g.bl
 
 int32_t prefill_tc_tile_rows() { return kQT; }
 
-cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream) {
+cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream, int max_sms) {
     CUtensorMap kmap, vmap;
     if (!make_arena_map(&kmap, p.k_arena, p.g) || !make_arena_map(&vmap, p.v_arena, p.g)) {
         return cudaErrorInvalidValue;
@@ -536,7 +537,8 @@ cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         grid_per_device[dev] = sms;  // one CTA per SM (shared memory and TMEM sized for it)
     }
-    prefill_tc_kernel<<<grid_per_device[dev], kThreads, kSmemBytes, stream>>>(p, kmap, vmap);
+    const int grid = max_sms > 0 ? std::min(max_sms, grid_per_device[dev]) : grid_per_device[dev];
+    prefill_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, kmap, vmap);
     return cudaGetLastError();
 }
 

@@ -83,7 +83,9 @@ AttentionEngine::~AttentionEngine() {
         cudaSetDevice(cfg_.device);
         cudaStreamSynchronize(stream_);
     }
-    if (copy_stream_ != nullptr) cudaStreamSynchronize(copy_stream_);
+    for (cudaStream_t cs : {h2d_stream_, d2h_stream_}) {
+        if (cs != nullptr) cudaStreamSynchronize(cs);
+    }
     for (int i = 0; i < 2; ++i) {
         if (meta_done_[i]) cudaEventDestroy(meta_done_[i]);
         if (h_meta_[i]) cudaFreeHost(h_meta_[i]);
@@ -95,7 +97,8 @@ AttentionEngine::~AttentionEngine() {
         }
         if (d_rows_[i]) cudaFree(d_rows_[i]);
     }
-    if (copy_stream_) cudaStreamDestroy(copy_stream_);
+    if (h2d_stream_) cudaStreamDestroy(h2d_stream_);
+    if (d2h_stream_) cudaStreamDestroy(d2h_stream_);
     if (d_meta_) cudaFree(d_meta_);
     if (d_ws_) cudaFree(d_ws_);
     if (d_k_) cudaFree(d_k_);
@@ -208,8 +211,9 @@ std::expected<void, EngineError> AttentionEngine::submit(int32_t layer, int32_t 
     }
     NVLLM_CUDA_TRY(cudaSetDevice(cfg_.device));
     if (auto r = init_slot(slot); !r) return r;
-    if (copy_stream_ == nullptr) {
-        NVLLM_CUDA_TRY(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+    if (h2d_stream_ == nullptr) {
+        NVLLM_CUDA_TRY(cudaStreamCreateWithFlags(&h2d_stream_, cudaStreamNonBlocking));
+        NVLLM_CUDA_TRY(cudaStreamCreateWithFlags(&d2h_stream_, cudaStreamNonBlocking));
         for (int i = 0; i < 2; ++i) {
             for (cudaEvent_t* ev : {&in_ready_[i], &out_ready_[i], &out_done_[i]}) {
                 NVLLM_CUDA_TRY(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
@@ -223,26 +227,28 @@ std::expected<void, EngineError> AttentionEngine::submit(int32_t layer, int32_t 
     float* dk = dq + stride;
     float* dv = dq + 2 * stride;
     float* dout = dq + 3 * stride;
-    // The slot's device rows were last read by its previous kernels and its
-    // output copied out after them, both ordered before these copies (the
-    // previous D2H is on this copy stream, after that step's out_ready).
+    // The slot's device rows were last read by its previous kernels, and its
+    // output copied out after them; the uploads wait for that download (already
+    // complete when the slot was collected, as it must have been).
+    if (slot_used_[slot]) NVLLM_CUDA_TRY(cudaStreamWaitEvent(h2d_stream_, out_done_[slot], 0));
     if (n > 0) {
-        NVLLM_CUDA_TRY(cudaMemcpyAsync(dq, h_q_[slot], bytes, cudaMemcpyHostToDevice, copy_stream_));
-        NVLLM_CUDA_TRY(cudaMemcpyAsync(dk, h_k_[slot], bytes, cudaMemcpyHostToDevice, copy_stream_));
-        NVLLM_CUDA_TRY(cudaMemcpyAsync(dv, h_v_[slot], bytes, cudaMemcpyHostToDevice, copy_stream_));
+        NVLLM_CUDA_TRY(cudaMemcpyAsync(dq, h_q_[slot], bytes, cudaMemcpyHostToDevice, h2d_stream_));
+        NVLLM_CUDA_TRY(cudaMemcpyAsync(dk, h_k_[slot], bytes, cudaMemcpyHostToDevice, h2d_stream_));
+        NVLLM_CUDA_TRY(cudaMemcpyAsync(dv, h_v_[slot], bytes, cudaMemcpyHostToDevice, h2d_stream_));
     }
-    NVLLM_CUDA_TRY(cudaEventRecord(in_ready_[slot], copy_stream_));
+    NVLLM_CUDA_TRY(cudaEventRecord(in_ready_[slot], h2d_stream_));
     NVLLM_CUDA_TRY(cudaStreamWaitEvent(stream_, in_ready_[slot], 0));
     if (n > 0) {
         if (auto r = attention_device(layer, dq, dk, dv, dout, precision); !r) return r;
     }
     NVLLM_CUDA_TRY(cudaEventRecord(out_ready_[slot], stream_));
-    NVLLM_CUDA_TRY(cudaStreamWaitEvent(copy_stream_, out_ready_[slot], 0));
+    NVLLM_CUDA_TRY(cudaStreamWaitEvent(d2h_stream_, out_ready_[slot], 0));
     if (n > 0) {
         NVLLM_CUDA_TRY(cudaMemcpyAsync(h_out_[slot], dout, bytes, cudaMemcpyDeviceToHost,
-                                       copy_stream_));
+                                       d2h_stream_));
     }
-    NVLLM_CUDA_TRY(cudaEventRecord(out_done_[slot], copy_stream_));
+    NVLLM_CUDA_TRY(cudaEventRecord(out_done_[slot], d2h_stream_));
+    slot_used_[slot] = true;
     in_flight_[slot] = true;
     return {};
 }

@@ -90,10 +90,10 @@ public:
                                                       float* d_out, int32_t precision);
 
     // Pipelined host rows, two slots. submit(layer, slot) queues, for the step
-    // begun last, the H2D of the slot's pinned Q/K/V rows on a copy stream, the
-    // KV write + attention on stream() once they have landed, and the D2H of the
-    // output into the slot's pinned output buffer on the copy stream once the
-    // kernels are done; it returns without waiting. collect(slot) waits for that
+    // begun last, the H2D of the slot's pinned Q/K/V rows on an upload stream,
+    // the KV write + attention on stream() once they have landed, and the D2H of
+    // the output into the slot's pinned output buffer on a download stream once
+    // the kernels are done; it returns without waiting. collect(slot) waits for that
     // output. While one slot's kernels run, the other slot's copies proceed, so
     // the copies of consecutive steps overlap the kernels. A slot must be
     // collected before it is submitted again (its pinned rows stay in use until
@@ -132,11 +132,16 @@ private:
     float* h_k_[2] = {nullptr, nullptr};
     float* h_v_[2] = {nullptr, nullptr};
     float* h_out_[2] = {nullptr, nullptr};
-    cudaStream_t copy_stream_ = nullptr;  // the pipelined path's H2D and D2H
+    // the pipelined path's copies: H2D on one stream, D2H on another, so that a
+    // step's uploads never queue behind the previous step's download (which
+    // waits for that step's kernels)
+    cudaStream_t h2d_stream_ = nullptr;
+    cudaStream_t d2h_stream_ = nullptr;
     cudaEvent_t in_ready_[2] = {nullptr, nullptr};   // slot's rows landed
     cudaEvent_t out_ready_[2] = {nullptr, nullptr};  // slot's kernels done
     cudaEvent_t out_done_[2] = {nullptr, nullptr};   // slot's output back on the host
     bool in_flight_[2] = {false, false};
+    bool slot_used_[2] = {false, false};  // out_done_ recorded at least once
 };
 
 }  // namespace nvllm
