@@ -761,6 +761,22 @@ def headsplit_leg(args, nvllm, dev, stream, ranks: Ranks, sampler, rank: int,
         t, _, clk = timed_leg(lambda i: db.step(), args.steps, warm, stream, ranks, sampler)
         res["fused"] = {"ms_per_step": t / args.steps * 1e3, "clocks": clk}
         res["gpu_launches"] = db.launches() * args.steps
+        # one rank's share of an N-way split on this GPU (its heads' KV write +
+        # attention, no exchange): the floor of the split's step time at N
+        shares = {}
+        for n in (2, 4, 8):
+            sl = nvllm.KVLayout(spec.num_blocks, 1, spec.block_size, H // n, hd)
+            cols = (H // n) * hd
+            shape = (spec.num_blocks, 1, spec.block_size, cols)
+            ks = ka.view(-1, H * hd)[:, :cols].contiguous().view(shape)
+            vs = va.view(-1, H * hd)[:, :cols].contiguous().view(shape)
+            part = DeviceBatch(nvllm, spec, sl, ks, vs, gen, dev, stream, nvllm.PRECISION_FP32)
+            tn, _, _ = timed_leg(lambda i: part.step(), args.steps, warm, stream, ranks,
+                                 sampler)
+            shares[str(n)] = {"heads": H // n, "ms_per_step": tn / args.steps * 1e3,
+                              "hbm_gbs": spec.kv_bytes() / n / (tn / args.steps) / 1e9}
+            del part, ks, vs
+        res["one_rank_share_alone"] = shares
     else:
         from nvllm.headsplit import HeadSplitGroup
         dist = ranks.dist

@@ -72,8 +72,9 @@ struct WorkspaceLayout {
     int32_t max_splits, split_tokens, prefill_tile;
 };
 
+// split_tokens 0: the size decode_split_tokens picks for the batch.
 WorkspaceLayout workspace_layout(int32_t num_seqs, int32_t max_query_len, int32_t max_context_len,
-                                 int32_t num_heads, int32_t head_dim);
+                                 int32_t num_heads, int32_t head_dim, int32_t split_tokens = 0);
 
 cudaError_t launch_reshape_and_cache(const float* key, const float* value, float* k_arena,
                                      float* v_arena, const int32_t* slot_mapping,
@@ -85,7 +86,10 @@ cudaError_t launch_plan(const AttnParams& p, cudaStream_t stream);
 cudaError_t launch_signal(uint32_t* const* flags, int n, cudaStream_t stream);
 // Waits (bounded) until *flag >= target; one thread.
 cudaError_t launch_flag_wait(const uint32_t* flag, uint32_t target, cudaStream_t stream);
-cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream);
+// overlap_previous: launch the decode kernel as a programmatic dependent of the
+// kernel before it in the stream (a prefill kernel, which releases it at its
+// start), so that it runs beside that kernel on the SMs it leaves free.
+cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream, bool overlap_previous = false);
 // max_sms > 0 bounds the persistent grid to that many SMs' worth of CTAs (the
 // rest of the GPU is left to a decode kernel running beside it); 0 = all SMs.
 cudaError_t launch_prefill_fp32(const AttnParams& p, cudaStream_t stream, int max_sms = 0);
@@ -93,7 +97,14 @@ cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream, int max_
 bool prefill_tc_supported(const ArenaGeom& g);
 int32_t prefill_tc_tile_rows();
 
-int32_t decode_split_tokens(int32_t head_dim);
+// Positions per decode work item: 16 chunks of 2048/hd positions (256 KiB of
+// K+V), halved (down to 4 chunks) while a batch of num_seqs sequences of up to
+// max_context_len positions and num_heads heads would give the persistent
+// decode grid fewer than kDecodeUnitsTarget (sequence, head, split) units; a
+// zero argument gives the coarsest size.
+constexpr int64_t kDecodeUnitsTarget = 16384;
+int32_t decode_split_tokens(int32_t head_dim, int32_t num_seqs, int32_t num_heads,
+                            int32_t max_context_len);
 int32_t prefill_tile_rows(int32_t head_dim);
 
 }  // namespace nvllm

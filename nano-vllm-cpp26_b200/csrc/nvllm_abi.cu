@@ -6,7 +6,6 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
-#include <vector>
 
 #include "../../include/nvllm.h"
 #include "common.cuh"
@@ -54,9 +53,11 @@ ArenaGeom make_geom(const nvllm_kv_layout* lay) {
 }  // namespace
 
 WorkspaceLayout workspace_layout(int32_t num_seqs, int32_t max_query_len, int32_t max_context_len,
-                                 int32_t num_heads, int32_t head_dim) {
+                                 int32_t num_heads, int32_t head_dim, int32_t split_tokens) {
     WorkspaceLayout w{};
-    w.split_tokens = decode_split_tokens(head_dim);
+    w.split_tokens = split_tokens > 0
+                         ? split_tokens
+                         : decode_split_tokens(head_dim, num_seqs, num_heads, max_context_len);
     w.prefill_tile = prefill_tile_rows(head_dim);
     w.max_splits = (max_context_len + w.split_tokens - 1) / w.split_tokens;
     if (w.max_splits < 1) w.max_splits = 1;
@@ -138,8 +139,17 @@ int prepare_attention(AttnParams& p, const float* query, const float* k_arena,
     if (!aligned16(query) || !aligned16(k_arena) || !aligned16(v_arena)) return NVLLM_ERR_INVALID;
     if (!(scale > 0.0f) || scale != scale) return NVLLM_ERR_INVALID;
 
-    const WorkspaceLayout w = workspace_layout(num_seqs, max_query_len, max_context_len,
-                                               layout->num_heads, layout->head_dim);
+    // The split size the batch asks for; a coarser one (fewer partials) when the
+    // workspace is too small for that layout. A workspace sized by
+    // nvllm_paged_attention_workspace_size for larger maxima always holds at
+    // least the coarsest layout of this call.
+    WorkspaceLayout w = workspace_layout(num_seqs, max_query_len, max_context_len,
+                                         layout->num_heads, layout->head_dim);
+    const int32_t coarsest = decode_split_tokens(layout->head_dim, 0, 0, 0);
+    while (w.total > workspace_bytes && w.split_tokens < coarsest) {
+        w = workspace_layout(num_seqs, max_query_len, max_context_len, layout->num_heads,
+                             layout->head_dim, w.split_tokens * 2);
+    }
     if (workspace == nullptr || workspace_bytes < w.total ||
         (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0) {
         return NVLLM_ERR_WORKSPACE;
@@ -170,45 +180,7 @@ int prepare_attention(AttnParams& p, const float* query, const float* k_arena,
     return NVLLM_OK;
 }
 
-// The prefill beside the decode: a high-priority stream per in-flight call
-// with the events that fork it from and join it back into the caller's stream.
-// Lanes are pooled per device; a lane goes back to the pool as soon as its
-// launches are queued (a later call that takes it queues behind them).
-struct SideLane {
-    int device = -1;
-    cudaStream_t stream = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-};
-std::mutex g_lanes_mu;
-std::vector<SideLane> g_lanes;  // idle lanes
-
-cudaError_t take_lane(int dev, SideLane& out) {
-    {
-        std::lock_guard<std::mutex> lk(g_lanes_mu);
-        for (std::size_t i = 0; i < g_lanes.size(); ++i) {
-            if (g_lanes[i].device == dev) {
-                out = g_lanes[i];
-                g_lanes.erase(g_lanes.begin() + std::ptrdiff_t(i));
-                return cudaSuccess;
-            }
-        }
-    }
-    int least = 0, greatest = 0;
-    cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
-    if (e != cudaSuccess) return e;
-    out.device = dev;
-    e = cudaStreamCreateWithPriority(&out.stream, cudaStreamNonBlocking, greatest);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&out.fork, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&out.join, cudaEventDisableTiming);
-    return e;
-}
-
-void give_lane(const SideLane& lane) {
-    std::lock_guard<std::mutex> lk(g_lanes_mu);
-    g_lanes.push_back(lane);
-}
-
-// SMs given to the prefill when it runs beside the decode (NVLLM_PREFILL_SMS:
+// SMs given to the prefill when the decode runs beside it (NVLLM_PREFILL_SMS:
 // a count of SMs; 0 = the prefill first on the whole GPU, then the decode).
 int prefill_beside_sms() {
     static const int v = [] {
@@ -219,10 +191,12 @@ int prefill_beside_sms() {
 }
 
 // plan -> prefill (if any multi-row sequence) and decode + merge. With a
-// prefill share configured, the prefill runs on a bounded persistent grid on a
-// high-priority side stream while the decode's persistent grid takes the other
-// SMs and, as the prefill's CTAs retire, theirs: the HBM-bound decode and the
-// tensor-bound prefill overlap instead of running one after the other.
+// prefill share configured, the prefill's persistent grid is bounded to that
+// many SMs and the decode is launched as its programmatic dependent: the
+// decode's CTAs start on the other SMs as soon as every prefill CTA is
+// resident, and take the prefill's SMs as they retire, so that the HBM-bound
+// decode and the tensor-bound prefill overlap. The merge and everything after
+// the call are ordinary stream successors and wait for both.
 cudaError_t launch_attention(AttnParams& p, int32_t precision, cudaStream_t st) {
     // TF32 prefill runs on the tensor cores where the kernel's geometry allows
     // (hd 128, block size 16); elsewhere the fp32 FFMA kernel serves it, whose
@@ -233,30 +207,11 @@ cudaError_t launch_attention(AttnParams& p, int32_t precision, cudaStream_t st) 
     cudaError_t e = launch_plan(p, st);
     if (e != cudaSuccess) return e;
     const int beside = p.max_query_len > 1 ? prefill_beside_sms() : 0;
-    if (beside <= 0) {
-        if (p.max_query_len > 1) {
-            e = tc_prefill ? launch_prefill_tc(p, st) : launch_prefill_fp32(p, st);
-            if (e != cudaSuccess) return e;
-        }
-        return launch_decode(p, st);
+    if (p.max_query_len > 1) {
+        e = tc_prefill ? launch_prefill_tc(p, st, beside) : launch_prefill_fp32(p, st, beside);
+        if (e != cudaSuccess) return e;
     }
-    int dev = 0;
-    e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    SideLane lane;
-    e = take_lane(dev, lane);
-    if (e != cudaSuccess) return e;
-    e = cudaEventRecord(lane.fork, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(lane.stream, lane.fork, 0);
-    if (e == cudaSuccess) {
-        e = tc_prefill ? launch_prefill_tc(p, lane.stream, beside)
-                       : launch_prefill_fp32(p, lane.stream, beside);
-    }
-    if (e == cudaSuccess) e = cudaEventRecord(lane.join, lane.stream);
-    if (e == cudaSuccess) e = launch_decode(p, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, lane.join, 0);
-    give_lane(lane);
-    return e;
+    return launch_decode(p, st, /*overlap_previous=*/beside > 0);
 }
 
 }  // namespace

@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const AttnParams p) 
 }
 
 template <int HD, int NW, int NS, bool kB16>
-cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream) {
+cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream, bool overlap_previous) {
     constexpr size_t smem = decode_smem_bytes<HD, NW, NS>();
     static int grid_per_device[64] = {0};
     int dev = 0;
@@ -600,8 +600,22 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         grid_per_device[dev] = sms * (per_sm > 0 ? per_sm : 1);
     }
-    decode_kernel<HD, NW, NS, kB16><<<grid_per_device[dev], NW * 32, smem, stream>>>(p);
-    e = cudaGetLastError();
+    if (overlap_previous) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(unsigned(grid_per_device[dev]));
+        cfg.blockDim = dim3(NW * 32);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, decode_kernel<HD, NW, NS, kB16>, p);
+    } else {
+        decode_kernel<HD, NW, NS, kB16><<<grid_per_device[dev], NW * 32, smem, stream>>>(p);
+        e = cudaGetLastError();
+    }
     if (e != cudaSuccess) return e;
     const int warps = p.num_seqs * p.g.num_heads;
     merge_kernel<HD><<<(warps + 7) / 8, 256, 0, stream>>>(p);
@@ -610,9 +624,20 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream) {
 
 }  // namespace
 
-int32_t decode_split_tokens(int32_t head_dim) {
+int32_t decode_split_tokens(int32_t head_dim, int32_t num_seqs, int32_t num_heads,
+                            int32_t max_context_len) {
     // 16 chunks of 2048/hd positions: 256 KiB of K+V per item at any head_dim.
-    return 16 * (2048 / head_dim);
+    // With few (sequence, head) pairs, as on one rank of a head split, that
+    // leaves some warps of the persistent grid a second 256 KiB item while the
+    // rest idle; finer items (64 KiB at the least) even the load out.
+    const int32_t chunk = 2048 / head_dim;
+    int32_t p = 16 * chunk;
+    if (num_seqs <= 0 || num_heads <= 0 || max_context_len <= 0) return p;
+    auto units = [&](int32_t split) {
+        return int64_t(num_seqs) * num_heads * ((int64_t(max_context_len) + split - 1) / split);
+    };
+    while (p > 4 * chunk && units(p) < kDecodeUnitsTarget) p /= 2;
+    return p;
 }
 
 cudaError_t launch_signal(uint32_t* const* flags, int n, cudaStream_t stream) {
@@ -641,16 +666,17 @@ cudaError_t launch_plan(const AttnParams& p, cudaStream_t stream) {
 #define NVLLM_DECODE_NS 2
 #endif
 
-cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream) {
+cudaError_t launch_decode(const AttnParams& p, cudaStream_t stream, bool overlap_previous) {
     constexpr int NW = NVLLM_DECODE_NW;
     constexpr int NS = NVLLM_DECODE_NS;
+    const bool o = overlap_previous;
     switch (p.g.head_dim) {
-        case 32: return launch_decode_t<32, NW, NS, false>(p, stream);
-        case 64: return launch_decode_t<64, NW, NS, false>(p, stream);
+        case 32: return launch_decode_t<32, NW, NS, false>(p, stream, o);
+        case 64: return launch_decode_t<64, NW, NS, false>(p, stream, o);
         case 128:
-            return p.g.block_size == 16 ? launch_decode_t<128, NW, NS, true>(p, stream)
-                                        : launch_decode_t<128, NW, NS, false>(p, stream);
-        case 256: return launch_decode_t<256, NW, NS, false>(p, stream);
+            return p.g.block_size == 16 ? launch_decode_t<128, NW, NS, true>(p, stream, o)
+                                        : launch_decode_t<128, NW, NS, false>(p, stream, o);
+        case 256: return launch_decode_t<256, NW, NS, false>(p, stream, o);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -45,6 +45,9 @@ template <int HD>
 __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_fp32_kernel(const AttnParams p) {
     using S = PrefillShape<HD>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // a decode kernel launched as this kernel's programmatic dependent may start
+    // on the SMs this grid leaves free (it reads nothing this kernel writes)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);  // 2 stages
     __shared__ int s_item;
     float* sQ = reinterpret_cast<float*>(smem_raw + 128);

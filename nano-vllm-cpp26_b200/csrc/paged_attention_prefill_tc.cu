@@ -125,6 +125,9 @@ __device__ __forceinline__ uint32_t stage_parity(uint32_t n) { return (n / kStag
 __global__ void __launch_bounds__(kThreads, 1)
 prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap) {
+    // a decode kernel launched as this kernel's programmatic dependent may start
+    // on the SMs this grid leaves free (it reads nothing this kernel writes)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

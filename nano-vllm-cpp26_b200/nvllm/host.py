@@ -376,13 +376,20 @@ class Model:
     """The reference TransformerModel on the engine's GPU (nvllm_model_*):
     LCG weights generated on the device, forward_batch as device kernels.
     ``cfg`` holds vocab, hidden, layers, heads, head_dim, ffn; ``scales`` the
-    optional [emb_scale, ffn_scale] of the weights; ``gemm_math`` GEMM_FP32
-    (FFMA) or GEMM_BF16X9 (fp32 emulated on the tensor cores); ``head_ranks``
-    > 1 makes it one rank of a head-parallel model (the engine holding heads /
-    head_ranks heads; see nvllm.headsplit.ModelHeads)."""
+    optional [emb_scale, ffn_scale] of the weights; ``gemm_math`` GEMM_TF32X3
+    (this library's tcgen05 / FFMA GEMMs at fp32 quality; the default where
+    hidden, ffn, vocab and hidden / head_ranks are multiples of 128), GEMM_FP32
+    (cuBLAS FFMA; the default elsewhere) or GEMM_BF16X9 (cuBLAS's fp32 emulation
+    on the tensor cores); ``head_ranks`` > 1 makes it one rank of a
+    head-parallel model (the engine holding heads / head_ranks heads; see
+    nvllm.headsplit.ModelHeads)."""
 
-    def __init__(self, cfg: dict, engine: Engine, scales=None, gemm_math: int = GEMM_FP32,
+    def __init__(self, cfg: dict, engine: Engine, scales=None, gemm_math: int | None = None,
                  graph_max_tokens: int = 0, head_ranks: int = 1):
+        if gemm_math is None:
+            dims = (cfg["hidden"], cfg["ffn"], cfg["vocab"], cfg["hidden"] // max(head_ranks, 1))
+            gemm_math = GEMM_TF32X3 if all(d % 128 == 0 for d in dims) else GEMM_FP32
+        self.gemm_math = gemm_math
         self.L = host_lib()
         self.engine = engine  # the model uses the engine's arenas and stream
         self.cfg = dict(cfg)
