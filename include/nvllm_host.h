@@ -294,6 +294,28 @@ int nvllm_router_metrics(nvllm_router* r, int32_t gpu, nvllm_metrics* out);
 /* Requests placed on a GPU so far (-1 for a bad index). */
 int64_t nvllm_router_placed(const nvllm_router* r, int32_t gpu);
 
+/* ---- HTTP/SSE front end (the reference's HttpSseServer, src/server.cpp) ----
+ * Serves GET /health, GET /v1/metrics (the MetricsSnapshot JSON of
+ * src/engine.cpp:8-38 summed over the router's GPUs, plus a "gpus" list with
+ * each GPU's arena use, iterations, bytes copied and kernel launches) and
+ * POST /v1/generate {"prompt": "...", "max_tokens": n}, answered as a
+ * text/event-stream with one frame per generated token in the reference's
+ * format: data: {"seq_id":S,"token_id":T,"text":"...","finished":B[,"ttft_us":U]}.
+ * Prompts are tokenised and tokens named as the reference does
+ * (src/engine.cpp:40-64, src/model.cpp:114-121). nvllm_server_start binds
+ * bind_address:port (NULL: 127.0.0.1; port 0: any free port) and accepts on a
+ * background thread; stop it before destroying the router. */
+typedef struct nvllm_server nvllm_server;
+int nvllm_server_start(nvllm_router* r, int64_t vocab_size, const char* bind_address,
+                       int32_t port, nvllm_server** out);
+/* The port the server listens on. */
+int32_t nvllm_server_port(const nvllm_server* s);
+/* Stops accepting, ends the open streams and joins the server's threads. */
+void nvllm_server_stop(nvllm_server* s);
+/* The reference engine's prompt tokenisation; returns the token count,
+ * writing the ids when they fit in cap. */
+int64_t nvllm_tokenize_prompt(const char* text, int64_t vocab_size, int64_t* out, int64_t cap);
+
 /* ---- cross-process device buffers (head split) ---------------------------
  * nvllm_ipc_alloc: cudaMalloc of `bytes` on the current device, zero-filled,
  * and its 64-byte CUDA IPC handle. nvllm_ipc_open maps a peer process's buffer

@@ -163,9 +163,30 @@ std::expected<StepSummary, EngineError> Generator::step() {
     }
     ++step_index_;
 
+    if (sink_) {
+        ev_ids_.resize(n);
+        ev_first_.resize(n);
+        for (std::size_t i = 0; i < n; ++i) {
+            ev_ids_[i] = run[i].id;
+            ev_first_[i] = run[i].first_token.has_value() ? 0 : 1;
+        }
+    }
     retired_.clear();
     std::vector<uint64_t> ttfts;
     sum.retired = sched_.process_step_outputs(sampled_, blocks, &retired_, &ttfts);
+    if (sink_) {
+        std::size_t k = 0;
+        for (std::size_t i = 0; i < n; ++i) {
+            TokenEvent ev;
+            ev.seq_id = ev_ids_[i];
+            ev.token = sampled_[i];
+            for (const Sequence& r : retired_) {
+                if (r.id == ev.seq_id) ev.finished = true;
+            }
+            if (ev_first_[i] && k < ttfts.size()) ev.ttft_us = ttfts[k++];
+            sink_(ev);
+        }
+    }
     for (Sequence& seq : retired_) done_[seq.id] = std::move(seq.tokens);
     for (const uint64_t t : ttfts) {
         ttft_us_ += double(t);

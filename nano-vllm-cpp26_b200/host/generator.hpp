@@ -14,6 +14,8 @@
 #include <cstdint>
 #include <cstdio>
 #include <expected>
+#include <functional>
+#include <optional>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -51,6 +53,17 @@ struct Metrics {
 //   seq_id, num_computed, total_len, last token, table_len, table..., n_uncomputed, uncomputed...
 void append_batch_record(const Scheduler& s, int64_t step, std::vector<int64_t>& out);
 
+// One sampled token of one sequence, as the reference streams it to its client
+// (TokenStreamEvent, include/nano_vllm/scheduler.hpp:24-30): finished on the
+// sequence's last token, the time to first token (from arrival) on its first.
+struct TokenEvent {
+    SeqId seq_id = 0;
+    int64_t token = 0;
+    bool finished = false;
+    std::optional<uint64_t> ttft_us{};
+};
+using TokenSink = std::function<void(const TokenEvent&)>;
+
 class Generator {
 public:
     Generator(AttentionEngine& eng, DeviceModel& model, const SchedulerConfig& cfg,
@@ -78,6 +91,9 @@ public:
     // margin and the 8 largest logits as (index, float bits)); "" stops.
     bool set_trace(const std::string& path);
     const Scheduler& scheduler() const noexcept { return sched_; }
+    // Called after every step with each sampled token, in batch order (the
+    // reference pushes them from process_step_outputs, src/scheduler.cpp:132-165).
+    void set_token_sink(TokenSink sink) { sink_ = std::move(sink); }
 
 private:
     AttentionEngine& eng_;
@@ -94,6 +110,9 @@ private:
     std::vector<Sequence> retired_;
     std::vector<int64_t> record_;
     std::FILE* trace_ = nullptr;
+    TokenSink sink_;
+    std::vector<SeqId> ev_ids_;
+    std::vector<uint8_t> ev_first_;
     int64_t step_index_ = 0;
     // telemetry
     uint64_t received_ = 0, tokens_generated_ = 0, iterations_ = 0, ttft_samples_ = 0;

@@ -13,6 +13,7 @@
 #include "model.hpp"
 #include "router.hpp"
 #include "scheduler.hpp"
+#include "server.hpp"
 
 struct nvllm_block_allocator {
     nvllm::BlockAllocator impl;
@@ -37,6 +38,10 @@ struct nvllm_generator {
 
 struct nvllm_router {
     std::unique_ptr<nvllm::Router> impl;
+};
+
+struct nvllm_server {
+    std::unique_ptr<nvllm::HttpServer> impl;
 };
 
 namespace {
@@ -632,3 +637,33 @@ int nvllm_ipc_free(void* dev_ptr) {
 }
 
 }  // extern "C"
+
+int nvllm_server_start(nvllm_router* r, int64_t vocab_size, const char* bind_address,
+                       int32_t port, nvllm_server** out) {
+    if (r == nullptr || out == nullptr || vocab_size < 2 || port < 0 || port > 65535) {
+        return NVLLM_ERR_INVALID;
+    }
+    nvllm::ServerConfig cfg;
+    if (bind_address != nullptr && bind_address[0] != '\0') cfg.bind_address = bind_address;
+    cfg.port = uint16_t(port);
+    cfg.vocab_size = std::size_t(vocab_size);
+    auto s = nvllm::HttpServer::start(*r->impl, cfg);
+    if (!s) return NVLLM_ERR_INVALID;
+    auto* h = new (std::nothrow) nvllm_server{std::move(*s)};
+    if (h == nullptr) return NVLLM_ERR_INVALID;
+    *out = h;
+    return NVLLM_OK;
+}
+
+int32_t nvllm_server_port(const nvllm_server* s) { return s ? int32_t(s->impl->port()) : -1; }
+
+void nvllm_server_stop(nvllm_server* s) { delete s; }
+
+int64_t nvllm_tokenize_prompt(const char* text, int64_t vocab_size, int64_t* out, int64_t cap) {
+    if (text == nullptr || vocab_size < 2) return -1;
+    const auto t = nvllm::tokenize_prompt(text, std::size_t(vocab_size));
+    if (out != nullptr && int64_t(t.size()) <= cap) {
+        std::memcpy(out, t.data(), t.size() * sizeof(int64_t));
+    }
+    return int64_t(t.size());
+}

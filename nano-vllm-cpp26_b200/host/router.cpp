@@ -6,6 +6,47 @@
 
 namespace nvllm {
 
+void TokenStream::push(const TokenEvent& ev) {
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        if (closed_) return;
+        q_.push_back(ev);
+        if (ev.finished) closed_ = true;
+    }
+    cv_.notify_all();
+}
+
+std::optional<TokenEvent> TokenStream::pop_wait() {
+    std::unique_lock<std::mutex> lk(mu_);
+    cv_.wait(lk, [&] { return !q_.empty() || closed_; });
+    if (q_.empty()) return std::nullopt;
+    TokenEvent ev = q_.front();
+    q_.pop_front();
+    return ev;
+}
+
+std::optional<TokenEvent> TokenStream::pop_wait_for(std::chrono::milliseconds timeout) {
+    std::unique_lock<std::mutex> lk(mu_);
+    cv_.wait_for(lk, timeout, [&] { return !q_.empty() || closed_; });
+    if (q_.empty()) return std::nullopt;
+    TokenEvent ev = q_.front();
+    q_.pop_front();
+    return ev;
+}
+
+void TokenStream::close() {
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        closed_ = true;
+    }
+    cv_.notify_all();
+}
+
+bool TokenStream::closed() const {
+    std::lock_guard<std::mutex> lk(mu_);
+    return closed_;
+}
+
 Router::Router(std::span<Generator* const> gens) {
     lanes_.reserve(gens.size());
     for (Generator* g : gens) {
@@ -31,7 +72,8 @@ Router::~Router() {
 }
 
 std::expected<int32_t, EngineError> Router::add_request(SeqId id, std::vector<int64_t> prompt,
-                                                        std::size_t max_new_tokens) {
+                                                        std::size_t max_new_tokens,
+                                                        std::shared_ptr<TokenStream> stream) {
     if (prompt.empty()) prompt.push_back(1);  // as Sequence does (src/scheduler.cpp:8-20)
     max_new_tokens = std::max<std::size_t>(max_new_tokens, 1);
     const uint64_t rows = prompt.size() + max_new_tokens;
@@ -56,7 +98,7 @@ std::expected<int32_t, EngineError> Router::add_request(SeqId id, std::vector<in
         l.placed += 1;
         {
             std::lock_guard<std::mutex> lq(l.mu);
-            l.ingress.push_back(Pending{id, std::move(prompt), max_new_tokens});
+            l.ingress.push_back(Pending{id, std::move(prompt), max_new_tokens, std::move(stream)});
             l.busy = true;
         }
         l.cv.notify_one();
@@ -75,9 +117,18 @@ void Router::signal_idle() {
 void Router::engine_loop(std::stop_token stop, Lane& l) {
     cudaSetDevice(l.gen->device());
     std::deque<Pending> batch;
+    // tokens go to the streams of the requests that asked for them
+    l.gen->set_token_sink([&l](const TokenEvent& ev) {
+        auto it = l.streams.find(ev.seq_id);
+        if (it == l.streams.end()) return;
+        it->second->push(ev);
+        if (ev.finished) l.streams.erase(it);
+    });
     // no lock is held while idle_mu_ is taken (wait_idle takes the lanes'
     // locks while it holds none either)
     auto stop_with = [&](EngineError e) {
+        for (auto& [id, st] : l.streams) st->close();
+        l.streams.clear();
         {
             std::lock_guard<std::mutex> lk(l.mu);
             l.failed = true;
@@ -109,6 +160,7 @@ void Router::engine_loop(std::stop_token stop, Lane& l) {
         uint64_t moved = 0;
         for (Pending& p : batch) {
             moved += p.prompt.size() + p.max_new;
+            if (p.stream) l.streams[p.id] = std::move(p.stream);
             l.gen->add_request(p.id, std::move(p.prompt), p.max_new);
         }
         batch.clear();
@@ -128,7 +180,14 @@ void Router::engine_loop(std::stop_token stop, Lane& l) {
             return;
         }
         l.load = l.gen->outstanding_tokens();
+        {
+            std::lock_guard<std::mutex> lk(l.mu);
+            l.snapshot = l.gen->metrics();
+        }
     }
+    // stopped: no further tokens will come for the requests still held here
+    for (auto& [id, st] : l.streams) st->close();
+    l.streams.clear();
 }
 
 std::expected<void, EngineError> Router::wait_idle() {

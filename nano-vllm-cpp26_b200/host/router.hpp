@@ -17,6 +17,7 @@
 #pragma once
 
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdint>
 #include <deque>
@@ -33,6 +34,26 @@
 
 namespace nvllm {
 
+// Thread-safe channel of one request's tokens, from its GPU's engine thread to
+// a client (the reference's TokenStreamQueue, include/nano_vllm/scheduler.hpp:
+// 33-74): closed by the sequence's last token, or by the client going away.
+class TokenStream {
+public:
+    void push(const TokenEvent& ev);
+    // The next event; empty once the stream is closed and drained.
+    std::optional<TokenEvent> pop_wait();
+    // As pop_wait, giving up after `timeout` (empty; check closed()).
+    std::optional<TokenEvent> pop_wait_for(std::chrono::milliseconds timeout);
+    void close();
+    bool closed() const;
+
+private:
+    mutable std::mutex mu_;
+    std::condition_variable cv_;
+    std::deque<TokenEvent> q_;
+    bool closed_ = false;
+};
+
 class Router {
 public:
     // gens[i] drives GPU gens[i]->device(); the router starts one engine
@@ -45,14 +66,15 @@ public:
     // Places the request on the least-loaded GPU; returns that GPU's index in
     // gens, or an error when seq_id is already in use.
     std::expected<int32_t, EngineError> add_request(SeqId id, std::vector<int64_t> prompt,
-                                                    std::size_t max_new_tokens);
+                                                    std::size_t max_new_tokens,
+                                                    std::shared_ptr<TokenStream> stream = {});
     // Blocks until every GPU is idle with an empty ingress queue (or one has
     // failed: its error is returned).
     std::expected<void, EngineError> wait_idle();
     // The finished token list of a request; empty while its GPU is busy or when
     // the request is unknown or unfinished.
     std::optional<std::vector<int64_t>> output(SeqId id);
-    // Per-GPU telemetry, taken by each engine thread after its last step.
+    // Per-GPU telemetry, taken by each engine thread after every step.
     Metrics metrics(int32_t gpu);
     int32_t num_gpus() const noexcept { return int32_t(lanes_.size()); }
     // Requests placed on each GPU so far.
@@ -63,6 +85,7 @@ private:
         SeqId id;
         std::vector<int64_t> prompt;
         std::size_t max_new;
+        std::shared_ptr<TokenStream> stream;
     };
     struct Lane {
         Generator* gen = nullptr;
@@ -73,7 +96,9 @@ private:
         std::atomic<uint64_t> queued_rows{0};  // rows waiting in ingress
         std::atomic<bool> busy{false};        // ingress non-empty or work pending
         std::atomic<uint64_t> placed{0};
-        Metrics snapshot;                      // guarded by mu
+        Metrics snapshot;                      // guarded by mu, refreshed every step
+        // streams of the requests on this GPU (engine thread only)
+        std::unordered_map<SeqId, std::shared_ptr<TokenStream>> streams;
         EngineError error{};
         bool failed = false;                   // guarded by mu
         std::jthread thread;

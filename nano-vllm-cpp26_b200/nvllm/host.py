@@ -137,6 +137,13 @@ def host_lib() -> ctypes.CDLL:
     L.nvllm_router_metrics.argtypes = [_vp, ctypes.c_int32, ctypes.POINTER(Metrics)]
     L.nvllm_router_placed.restype = ctypes.c_int64
     L.nvllm_router_placed.argtypes = [_vp, ctypes.c_int32]
+    L.nvllm_server_start.argtypes = [_vp, ctypes.c_int64, ctypes.c_char_p, ctypes.c_int32,
+                                     ctypes.POINTER(_vp)]
+    L.nvllm_server_port.restype = ctypes.c_int32
+    L.nvllm_server_port.argtypes = [_vp]
+    L.nvllm_server_stop.argtypes = [_vp]
+    L.nvllm_tokenize_prompt.restype = ctypes.c_int64
+    L.nvllm_tokenize_prompt.argtypes = [ctypes.c_char_p, ctypes.c_int64, _i64p, ctypes.c_int64]
     L.nvllm_engine_arenas.argtypes = [_vp, ctypes.POINTER(_f32p), ctypes.POINTER(_f32p)]
     L.nvllm_engine_stream.restype = _vp
     L.nvllm_engine_stream.argtypes = [_vp]
@@ -643,3 +650,41 @@ class Router:
 
     def placed(self, gpu: int) -> int:
         return self.L.nvllm_router_placed(self.h, gpu)
+
+
+def tokenize_prompt(text: str, vocab_size: int) -> np.ndarray:
+    """The reference engine's prompt tokenisation (nvllm_tokenize_prompt)."""
+    L = host_lib()
+    raw = text.encode()
+    n = L.nvllm_tokenize_prompt(raw, vocab_size, None, 0)
+    if n < 0:
+        raise NvllmError(1, "nvllm_tokenize_prompt")
+    out = np.zeros(n, np.int64)
+    L.nvllm_tokenize_prompt(raw, vocab_size, _ptr(out, _i64p), n)
+    return out
+
+
+class Server:
+    """The HTTP/SSE front end over a router (nvllm_server_*): GET /health,
+    GET /v1/metrics, POST /v1/generate streaming one SSE frame per token.
+    Stop it (close) before the router."""
+
+    def __init__(self, router: Router, vocab_size: int, port: int = 0,
+                 bind_address: str = "127.0.0.1"):
+        self.L = host_lib()
+        self.router = router
+        h = _vp()
+        rc = self.L.nvllm_server_start(router.h, vocab_size, bind_address.encode(), port,
+                                       ctypes.byref(h))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_server_start")
+        self.h = h
+        self.port = self.L.nvllm_server_port(h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.nvllm_server_stop(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()

@@ -141,3 +141,28 @@ def test_packer_padding_to_a_bucket(host, oracle):
         assert (m["block_tables"][S:] == 0).all()
     with pytest.raises(NvllmError):  # a bucket smaller than the batch
         host.pack_metadata([0, 0], [3, 3], [[1], [2]], 16, 2, pad_seqs=1, pad_tokens=8)
+
+
+def _reference_tokenize(text: str, vocab: int) -> list[int]:
+    """The reference engine's tokenize_prompt (src/engine.cpp:40-64), restated:
+    whitespace-separated words, each djb2-hashed into [1, vocab)."""
+    out = []
+    for word in text.replace("\t", " ").replace("\n", " ").replace("\r", " ").split(" "):
+        if not word:
+            continue
+        h = 5381
+        for b in word.encode():
+            h = (h * 33 + b) & 0xFFFFFFFFFFFFFFFF
+        out.append(h % (vocab - 1) + 1)
+    return out or [1]
+
+
+def test_prompt_tokenisation_follows_the_reference():
+    from nvllm.host import tokenize_prompt
+    cases = ["paged attention on blackwell", "", "   ", "a", "cpp26\tkernel\nstream\r\nx",
+             "a-very-long-word-" * 40, "ünïcödé words"]
+    for vocab in (2, 512, 32000):
+        for text in cases:
+            assert tokenize_prompt(text, vocab).tolist() == _reference_tokenize(text, vocab), text
+    # djb2("a") = 5381 * 33 + 97
+    assert tokenize_prompt("a", 512).tolist() == [(5381 * 33 + 97) % 511 + 1]
