@@ -476,7 +476,11 @@ def nvllm_main(args, spec):
 
     # per-rank batch (sequence partitioning): the same context lengths on every
     # GPU, in a rank-seeded order with rank-seeded block tables and values
+    heads = spec.num_heads  # fewer than the workload's with --head-slice
     spec = make_batch(args.workload, seed=args.seed, rank=rank)
+    if heads != spec.num_heads:
+        import dataclasses
+        spec = dataclasses.replace(spec, num_heads=heads)
     lay = nvllm.KVLayout(spec.num_blocks, 1, spec.block_size, spec.num_heads, spec.head_dim)
     D = spec.hidden
     # The arenas belong to the host engine (libnvllm_host: allocator, pinned
@@ -1655,6 +1659,9 @@ def main() -> int:
                     help="skip the oracle check of the timed batch after the timed regions")
     ap.add_argument("--head-split", action="store_true",
                     help="split the batch's heads over the ranks (long-context decode)")
+    ap.add_argument("--head-slice", type=int, default=1,
+                    help="attention workloads: keep 1/N of the heads (one rank's share of an "
+                         "N-way head split, run alone on one GPU)")
     ap.add_argument("--shapes", nargs="*", default=None,
                     help="gemm workloads: m,k,n (gemm) or m,k,n,batch (gemm_skinny) per shape")
     ap.add_argument("--reps", type=int, default=10, help="gemm workloads: timed calls per shape")
@@ -1701,6 +1708,9 @@ def main() -> int:
         args.precision = "fp32"
     from nvllm.workload import make_batch
     spec = make_batch(args.workload, seed=args.seed)
+    if args.head_slice > 1:
+        import dataclasses
+        spec = dataclasses.replace(spec, num_heads=spec.num_heads // args.head_slice)
     if args.impl == "reference":
         return reference_main(args, spec)
     if args.head_split:

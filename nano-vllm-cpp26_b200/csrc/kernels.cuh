@@ -102,7 +102,10 @@ int32_t prefill_tc_tile_rows();
 // max_context_len positions and num_heads heads would give the persistent
 // decode grid fewer than kDecodeUnitsTarget (sequence, head, split) units; a
 // zero argument gives the coarsest size.
-constexpr int64_t kDecodeUnitsTarget = 16384;
+#ifndef NVLLM_DECODE_UNITS_TARGET
+#define NVLLM_DECODE_UNITS_TARGET 16384
+#endif
+constexpr int64_t kDecodeUnitsTarget = NVLLM_DECODE_UNITS_TARGET;
 int32_t decode_split_tokens(int32_t head_dim, int32_t num_seqs, int32_t num_heads,
                             int32_t max_context_len);
 int32_t prefill_tile_rows(int32_t head_dim);
