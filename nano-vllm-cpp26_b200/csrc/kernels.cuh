@@ -103,7 +103,7 @@ int32_t prefill_tc_tile_rows();
 // decode grid fewer than kDecodeUnitsTarget (sequence, head, split) units; a
 // zero argument gives the coarsest size.
 #ifndef NVLLM_DECODE_UNITS_TARGET
-#define NVLLM_DECODE_UNITS_TARGET 16384
+#define NVLLM_DECODE_UNITS_TARGET 0
 #endif
 constexpr int64_t kDecodeUnitsTarget = NVLLM_DECODE_UNITS_TARGET;
 int32_t decode_split_tokens(int32_t head_dim, int32_t num_seqs, int32_t num_heads,
