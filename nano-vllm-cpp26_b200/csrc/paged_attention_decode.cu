@@ -416,45 +416,100 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const AttnParams p) 
 
 // Combines the split partials of each (decode sequence, head):
 // M = max m_j, L = sum l_j 2^(m_j - M), out = sum acc_j 2^(m_j - M) / L.
+// A CTA of 8 warps serves 8 / wpr rows; the wpr warps of a row take
+// contiguous runs of its splits (loads unrolled four deep, so that a long run
+// is not a chain of dependent global loads) and combine their sums through
+// shared memory. wpr grows with the split count (merge_warps_per_row), and
+// the arithmetic depends only on it and the split size, not on the number of
+// heads or sequences in the batch.
 template <int HD>
-__global__ void __launch_bounds__(256) merge_kernel(const AttnParams p) {
-    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+__global__ void __launch_bounds__(256) merge_kernel(const AttnParams p, int wpr) {
+    constexpr int PER_LANE = HD / 32;
+    __shared__ float sm_m[8], sm_l[8];
+    __shared__ float sm_o[8][HD];
+    const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int H = p.g.num_heads;
-    if (gw >= p.num_seqs * H) return;
-    const int s = gw / H;
-    const int h = gw % H;
-    const int q0 = p.cu_seqlens_q[s];
-    if (q0 < 0 || p.cu_seqlens_q[s + 1] - q0 != 1) return;
-    const int ctx = p.context_lens[s];
-    if (ctx < 1 || ctx > p.max_context_len ||
-        int64_t(ctx) > int64_t(p.max_blocks) * p.g.block_size) {
-        return;
+    const int row = blockIdx.x * (8 / wpr) + warp / wpr;
+    const int sub = warp % wpr;
+    const int lead = warp - sub;  // first warp of this row
+    bool active = row < p.num_seqs * H;
+    int s = 0, h = 0, q0 = 0, nsplit = 0;
+    if (active) {
+        s = row / H;
+        h = row % H;
+        q0 = p.cu_seqlens_q[s];
+        const int ctx = p.context_lens[s];
+        active = q0 >= 0 && p.cu_seqlens_q[s + 1] - q0 == 1 && ctx >= 1 &&
+                 ctx <= p.max_context_len &&
+                 int64_t(ctx) <= int64_t(p.max_blocks) * p.g.block_size;
+        if (active) nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+        // one split: the decode kernel wrote the row itself, unless it must go to peers
+        if (nsplit <= 1 && p.num_outs == 0) active = false;
     }
-    const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
-    // one split: the decode kernel wrote the row itself, unless it must go to peers
-    if (nsplit <= 1 && p.num_outs == 0) return;
+    const int per = (nsplit + wpr - 1) / wpr;
+    const int j0 = min(nsplit, sub * per);
+    const int j1 = min(nsplit, j0 + per);
     const int64_t pbase = (int64_t(s) * H + h) * p.max_splits;
     float M = -INFINITY;
-    for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, p.part_ml[pbase + j].x);
-    M = warp_max_xor(M, 32);
-    float L = 0.f;
-    for (int j = lane; j < nsplit; j += 32) {
-        const float2 ml = p.part_ml[pbase + j];
-        L += ml.y * exp2f(ml.x - M);
+    if (active) {
+        for (int j = j0 + lane; j < j1; j += 32) M = fmaxf(M, __ldcg(&p.part_ml[pbase + j].x));
+        M = warp_max_xor(M, 32);
     }
-    L = warp_sum_xor(L, 32);
-    const float inv = 1.0f / fmaxf(L, 1e-12f);
-    constexpr int PER_LANE = HD / 32;
+    if (lane == 0) sm_m[warp] = M;
+    __syncthreads();
+    if (active) {
+        for (int w = lead; w < lead + wpr; ++w) M = fmaxf(M, sm_m[w]);
+    }
+    float L = 0.f;
     float o[PER_LANE];
 #pragma unroll
     for (int k = 0; k < PER_LANE; ++k) o[k] = 0.f;
-    for (int j = 0; j < nsplit; ++j) {
-        const float w = exp2f(p.part_ml[pbase + j].x - M);
-        const float* ap = p.part_acc + (pbase + j) * HD;
+    if (active) {
+        for (int j = j0 + lane; j < j1; j += 32) {
+            const float2 ml = __ldcg(&p.part_ml[pbase + j]);
+            L += ml.y * exp2f(ml.x - M);
+        }
+        L = warp_sum_xor(L, 32);
+        int j = j0;
+        for (; j + 4 <= j1; j += 4) {
+            float w[4];
+            float a[4][PER_LANE];
 #pragma unroll
-        for (int k = 0; k < PER_LANE; ++k) o[k] = fmaf(w, ap[lane + 32 * k], o[k]);
+            for (int u = 0; u < 4; ++u) {
+                w[u] = __ldcg(&p.part_ml[pbase + j + u].x);
+                const float* ap = p.part_acc + (pbase + j + u) * HD;
+#pragma unroll
+                for (int k = 0; k < PER_LANE; ++k) a[u][k] = __ldcg(ap + lane + 32 * k);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float wu = exp2f(w[u] - M);
+#pragma unroll
+                for (int k = 0; k < PER_LANE; ++k) o[k] = fmaf(wu, a[u][k], o[k]);
+            }
+        }
+        for (; j < j1; ++j) {
+            const float wu = exp2f(__ldcg(&p.part_ml[pbase + j].x) - M);
+            const float* ap = p.part_acc + (pbase + j) * HD;
+#pragma unroll
+            for (int k = 0; k < PER_LANE; ++k) o[k] = fmaf(wu, __ldcg(ap + lane + 32 * k), o[k]);
+        }
     }
+    if (wpr > 1) {
+        if (lane == 0) sm_l[warp] = L;
+#pragma unroll
+        for (int k = 0; k < PER_LANE; ++k) sm_o[warp][lane + 32 * k] = o[k];
+        __syncthreads();
+        if (sub != 0) return;
+        for (int w = lead + 1; w < lead + wpr; ++w) {
+            L += sm_l[w];
+#pragma unroll
+            for (int k = 0; k < PER_LANE; ++k) o[k] += sm_o[w][lane + 32 * k];
+        }
+    }
+    if (!active) return;
+    const float inv = 1.0f / fmaxf(L, 1e-12f);
     if (p.num_outs == 0) {
         float* op = p.out + int64_t(q0) * p.g.row + int64_t(h) * HD;
 #pragma unroll
@@ -477,6 +532,14 @@ __global__ void __launch_bounds__(256) merge_kernel(const AttnParams p) {
             for (int r = 0; r < p.num_outs; ++r) atomicAdd_system(p.flags[r], 1u);
         }
     }
+}
+
+// Warps that share one row's partials in the merge: 1 up to 16 splits, then
+// doubling up to 8 (a CTA's warps) from 128 splits.
+int merge_warps_per_row(int max_splits) {
+    int w = 1;
+    while (w < 8 && max_splits > 16 * w) w *= 2;
+    return w;
 }
 
 // Head split with nothing to store: signal every rank directly.
@@ -617,8 +680,10 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream, bool overl
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) return e;
-    const int warps = p.num_seqs * p.g.num_heads;
-    merge_kernel<HD><<<(warps + 7) / 8, 256, 0, stream>>>(p);
+    const int rows = p.num_seqs * p.g.num_heads;
+    const int wpr = merge_warps_per_row(p.max_splits);
+    const int rows_per_cta = 8 / wpr;
+    merge_kernel<HD><<<(rows + rows_per_cta - 1) / rows_per_cta, 256, 0, stream>>>(p, wpr);
     return cudaGetLastError();
 }
 
