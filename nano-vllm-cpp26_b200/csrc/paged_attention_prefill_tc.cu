@@ -335,7 +335,12 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             const int vt_dd = d & 31;     // dimension within its V atom
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
-                if (!wait_or_abort(&ctl->kv_full[stage_of(n)], stage_parity(n), ctl)) break;
+                // wait outcomes are made warp-uniform, so that no lane is left
+                // alone in a warp-collective step after another gave up
+                if (!__all_sync(0xffffffffu,
+                                wait_or_abort(&ctl->kv_full[stage_of(n)], stage_parity(n), ctl))) {
+                    break;
+                }
                 unsigned char* stage = sKV + stage_of(n) * kStageBytes;
                 {
                     const float4* kp = reinterpret_cast<const float4*>(stage);
@@ -347,7 +352,10 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                         klp[j] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
                     }
                 }
-                if (n >= 2 && !wait_or_abort(&ctl->vt_free[n & 1u], ((n >> 1) - 1) & 1u, ctl)) break;
+                if (n >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&ctl->vt_free[n & 1u],
+                                                                     ((n >> 1) - 1) & 1u, ctl))) {
+                    break;
+                }
                 unsigned char* vt = sVt + (n & 1u) * kVtBufBytes;
                 const int nvk = nk - t * kKT;
                 const unsigned char* sV = stage + 2 * kKBytes + (d >> 5) * kKVAtom + (vt_dd & 3) * 4;
@@ -381,7 +389,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             bool ok = true;
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
-                if (!wait_or_abort(&ctl->s_full[n & 1u], (n >> 1) & 1u, ctl)) {
+                if (!__all_sync(0xffffffffu, wait_or_abort(&ctl->s_full[n & 1u], (n >> 1) & 1u, ctl))) {
                     ok = false;
                     break;
                 }
@@ -410,7 +418,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 if (t > 0) {
                     // previous tile's P.V is in O: P's TMEM columns are free, and O
                     // can be rescaled to the new maximum before this tile's P.V
-                    if (!wait_or_abort(&ctl->o_full, (n - 1) & 1u, ctl)) {
+                    if (!__all_sync(0xffffffffu, wait_or_abort(&ctl->o_full, (n - 1) & 1u, ctl))) {
                         ok = false;
                         break;
                     }
@@ -441,7 +449,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             }
             if (ok && ntiles > 0) {
                 const uint32_t n = n0 + ntiles - 1;
-                if (wait_or_abort(&ctl->o_full, n & 1u, ctl)) {
+                if (__all_sync(0xffffffffu, wait_or_abort(&ctl->o_full, n & 1u, ctl))) {
                     tc::fence_after_sync();
                     const float inv = 1.0f / fmaxf(l_run, 1e-12f);
                     float4* op = reinterpret_cast<float4*>(p.out + int64_t(q0 + r0 + row) * g.row +
