@@ -72,9 +72,8 @@ struct WorkspaceLayout {
     int32_t max_splits, split_tokens, prefill_tile;
 };
 
-// split_tokens 0: the size decode_split_tokens picks for the batch.
 WorkspaceLayout workspace_layout(int32_t num_seqs, int32_t max_query_len, int32_t max_context_len,
-                                 int32_t num_heads, int32_t head_dim, int32_t split_tokens = 0);
+                                 int32_t num_heads, int32_t head_dim);
 
 cudaError_t launch_reshape_and_cache(const float* key, const float* value, float* k_arena,
                                      float* v_arena, const int32_t* slot_mapping,
@@ -101,16 +100,8 @@ cudaError_t launch_prefill_tc2(const AttnParams& p, cudaStream_t stream, int max
 int32_t prefill_tc2_tile_rows();
 
 // Positions per decode work item: 16 chunks of 2048/hd positions (256 KiB of
-// K+V), halved (down to 4 chunks) while a batch of num_seqs sequences of up to
-// max_context_len positions and num_heads heads would give the persistent
-// decode grid fewer than kDecodeUnitsTarget (sequence, head, split) units; a
-// zero argument gives the coarsest size.
-#ifndef NVLLM_DECODE_UNITS_TARGET
-#define NVLLM_DECODE_UNITS_TARGET 0
-#endif
-constexpr int64_t kDecodeUnitsTarget = NVLLM_DECODE_UNITS_TARGET;
-int32_t decode_split_tokens(int32_t head_dim, int32_t num_seqs, int32_t num_heads,
-                            int32_t max_context_len);
+// K+V at any head_dim).
+int32_t decode_split_tokens(int32_t head_dim);
 int32_t prefill_tile_rows(int32_t head_dim);
 
 }  // namespace nvllm

@@ -55,11 +55,9 @@ ArenaGeom make_geom(const nvllm_kv_layout* lay) {
 }  // namespace
 
 WorkspaceLayout workspace_layout(int32_t num_seqs, int32_t max_query_len, int32_t max_context_len,
-                                 int32_t num_heads, int32_t head_dim, int32_t split_tokens) {
+                                 int32_t num_heads, int32_t head_dim) {
     WorkspaceLayout w{};
-    w.split_tokens = split_tokens > 0
-                         ? split_tokens
-                         : decode_split_tokens(head_dim, num_seqs, num_heads, max_context_len);
+    w.split_tokens = decode_split_tokens(head_dim);
     w.prefill_tile = prefill_tile_rows(head_dim);
     w.max_splits = (max_context_len + w.split_tokens - 1) / w.split_tokens;
     if (w.max_splits < 1) w.max_splits = 1;
@@ -141,17 +139,8 @@ int prepare_attention(AttnParams& p, const float* query, const float* k_arena,
     if (!aligned16(query) || !aligned16(k_arena) || !aligned16(v_arena)) return NVLLM_ERR_INVALID;
     if (!(scale > 0.0f) || scale != scale) return NVLLM_ERR_INVALID;
 
-    // The split size the batch asks for; a coarser one (fewer partials) when the
-    // workspace is too small for that layout. A workspace sized by
-    // nvllm_paged_attention_workspace_size for larger maxima always holds at
-    // least the coarsest layout of this call.
-    WorkspaceLayout w = workspace_layout(num_seqs, max_query_len, max_context_len,
-                                         layout->num_heads, layout->head_dim);
-    const int32_t coarsest = decode_split_tokens(layout->head_dim, 0, 0, 0);
-    while (w.total > workspace_bytes && w.split_tokens < coarsest) {
-        w = workspace_layout(num_seqs, max_query_len, max_context_len, layout->num_heads,
-                             layout->head_dim, w.split_tokens * 2);
-    }
+    const WorkspaceLayout w = workspace_layout(num_seqs, max_query_len, max_context_len,
+                                               layout->num_heads, layout->head_dim);
     if (workspace == nullptr || workspace_bytes < w.total ||
         (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0) {
         return NVLLM_ERR_WORKSPACE;

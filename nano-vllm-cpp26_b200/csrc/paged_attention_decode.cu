@@ -689,20 +689,11 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream, bool overl
 
 }  // namespace
 
-int32_t decode_split_tokens(int32_t head_dim, int32_t num_seqs, int32_t num_heads,
-                            int32_t max_context_len) {
+int32_t decode_split_tokens(int32_t head_dim) {
     // 16 chunks of 2048/hd positions: 256 KiB of K+V per item at any head_dim.
-    // With few (sequence, head) pairs, as on one rank of a head split, that
-    // leaves some warps of the persistent grid a second 256 KiB item while the
-    // rest idle; finer items (64 KiB at the least) even the load out.
-    const int32_t chunk = 2048 / head_dim;
-    int32_t p = 16 * chunk;
-    if (num_seqs <= 0 || num_heads <= 0 || max_context_len <= 0) return p;
-    auto units = [&](int32_t split) {
-        return int64_t(num_seqs) * num_heads * ((int64_t(max_context_len) + split - 1) / split);
-    };
-    while (p > 4 * chunk && units(p) < kDecodeUnitsTarget) p /= 2;
-    return p;
+    // (Finer items for batches with few (sequence, head) pairs measured no
+    // faster: the longer plan and merge ate what the better balance gained.)
+    return 16 * (2048 / head_dim);
 }
 
 cudaError_t launch_signal(uint32_t* const* flags, int n, cudaStream_t stream) {

@@ -4,10 +4,8 @@ Every rank builds the same long-context decode batch (32 heads x hd 128,
 block size 16) on its own GPU, computes the full-head reference with
 nvllm_paged_attention, then computes its slice of the heads with
 nvllm_paged_attention_head_split over three epochs. Each rank's gathered
-output must equal the full-head result bit for bit, and so must the NCCL
-all-gather of the local outputs: the per-head arithmetic is the same, since
-this batch (6 sequences of up to 8192 positions) gets the finest decode items
-both with all 32 heads and with any rank's share of them.
+output must equal the full-head result bit for bit (the per-head arithmetic
+is the same), and so must the NCCL all-gather of the local outputs.
 """
 import datetime
 import math
