@@ -32,6 +32,7 @@
 //  * An item that covers the whole context writes the normalised output; other
 //    items write (m, l, acc) partials that the merge kernel combines with the
 //    usual max-rescaled sum.
+#include <algorithm>
 #include <cfloat>
 
 #include "common.cuh"
@@ -663,9 +664,23 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream, bool overl
         if (e != cudaSuccess) return e;
         grid_per_device[dev] = sms * (per_sm > 0 ? per_sm : 1);
     }
+    // Equal rounds: at most U = sequences x heads x splits units, which the
+    // full grid's W warps would take in k = ceil(U / W) rounds, some warps one
+    // round short; ceil(U / k) warps take the same k rounds with every warp
+    // busy in each (a batch with few (sequence, head) pairs otherwise leaves
+    // most warps idle during its last round).
+    int grid = grid_per_device[dev];
+    {
+        const int64_t units = int64_t(p.num_seqs) * p.g.num_heads *
+                              ((int64_t(p.max_context_len) + p.split_tokens - 1) / p.split_tokens);
+        const int64_t full = int64_t(grid) * NW;
+        const int64_t rounds = std::max<int64_t>(1, (units + full - 1) / full);
+        const int64_t warps = (units + rounds - 1) / rounds;
+        grid = int(std::clamp<int64_t>((warps + NW - 1) / NW, 1, grid));
+    }
     if (overlap_previous) {
         cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(unsigned(grid_per_device[dev]));
+        cfg.gridDim = dim3(unsigned(grid));
         cfg.blockDim = dim3(NW * 32);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = stream;
@@ -676,7 +691,7 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream, bool overl
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, decode_kernel<HD, NW, NS, kB16>, p);
     } else {
-        decode_kernel<HD, NW, NS, kB16><<<grid_per_device[dev], NW * 32, smem, stream>>>(p);
+        decode_kernel<HD, NW, NS, kB16><<<grid, NW * 32, smem, stream>>>(p);
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) return e;
