@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N --steps K --warmup W] [--impl nvllm|reference]
                     [--workload decode|mixed|longctx|serve|serve_toy|serve_toy_seeded|
-                                longctx_model|gemm|gemm_skinny]
+                                serve_router|longctx_model|gemm|gemm_skinny]
 
 One step = one pass of the hot path over one batch: nvllm_reshape_and_cache of
 the step's new K/V rows, then nvllm_paged_attention (plan, split-K decode and
@@ -11,15 +11,32 @@ merge kernels; the causal prefill kernel too for multi-row sequences). The
 default workload is the decode microbenchmark: 64 sequences, contexts
 U[512, 4096], 32 heads x head_dim 128, block size 16, 65536-block arena, fp32.
 
+The default line also carries, outside `value`:
+  * `e2e`: the same steps through the engine's C ABI with host rows (pinned
+    uploads of Q/K/V and metadata, download of the output, two pipeline slots);
+  * `sustained`: the step back to back for >= 1.5 s, with its clock record;
+  * `parity`: the timed batch's output against the oracle (the C restatement of
+    the reference's attention loop), after the timed regions;
+  * `extra.mixed`: the mixed prefill + decode super-batch (8 causal prefills
+    U[512, 2048] + 120 decodes U[256, 8192]) and its two parts alone;
+  * `extra.head_split`: the long-context batch (4 x 32768) with its heads split
+    over the ranks (NVLink peer stores) beside the NCCL all-gather variant; at
+    N = 1, one rank's share of an N-way split alone for N = 2, 4, 8.
+Every timed region has its own clock record (nvidia-smi, the GPU named by UUID).
+
 Under torchrun each rank runs its own batch on its own GPU (sequence
-partitioning: no collective on the data path, weak scaling); the timed region
-is bracketed by a barrier and torch.cuda.synchronize(), timed with CUDA events
-on the launching stream, and the maximum over ranks is reported.
+partitioning: the same context lengths in a rank-seeded order and blocks, so
+every GPU moves the same bytes; no collective on the data path, weak scaling);
+the timed region is bracketed by a barrier and torch.cuda.synchronize(), timed
+with CUDA events on the launching stream, and the maximum over ranks is
+reported, with every rank's own figures under `per_rank`.
 
 The serving workloads (``serve``, ``serve_toy``, ``serve_toy_seeded``) time the
 whole engine loop instead: one step is a complete run of the workload's
 requests through the generator (continuous-batching scheduler + device
-forward_batch + sampling), reported as output tokens/s.
+forward_batch + sampling), reported as output tokens/s; ``serve_router`` runs
+one stream of 128 x N requests through the router over N GPUs from one process.
+``gemm`` / ``gemm_skinny`` time the model's projection GEMMs (tables on stderr).
 
 ``--impl reference`` times the reference's own CPU implementation of the path
 (TransformerModel::forward_batch's KV write + paged attention on its

@@ -31,7 +31,9 @@
 //              on the barriers of both CTAs (tcgen05.commit multicast);
 //   warps 5-12 converters: K_lo, and V^T hi / lo of this CTA's dimensions.
 // Cross-CTA hand-offs: every converter and softmax thread of both CTAs
-// arrives (at cluster scope) on CTA 0's cv_full / p_full; the MMA commits come
+// arrives (at cluster scope) on CTA 0's kc_full / vc_full / p_full (K_lo for S,
+// V^T for O, P for O, kept apart so that S never waits on a V^T conversion,
+// which itself waits for the previous O); the MMA commits come
 // back to both CTAs' barriers. No named barrier is used: a thread that gives
 // up on a wait must not leave the rest of its group blocked. Every wait is
 // bounded (2 s);
@@ -94,8 +96,10 @@ constexpr uint16_t kBoth = 0x3;  // commit to the barriers of both CTAs
 
 struct Control {
     uint64_t kv_full[kStages];  // this CTA's TMA boxes of the stage landed
-    uint64_t cv_full[kStages];  // CTA 0: every converter thread of both CTAs done
-    uint64_t pv_done[kStages];  // both: S of the stage's tile done (stage reusable)
+    uint64_t kc_full[kStages];  // CTA 0: K_lo of the stage written by every converter of both CTAs
+    uint64_t vread[kStages];    // this CTA's converters done reading the stage's V
+    uint64_t pv_done[kStages];  // both: S of the stage's tile done (its K read)
+    uint64_t vc_full[2];        // CTA 0: V^T of the buffer written by every converter of both CTAs
     uint64_t vt_free[2];        // both: O done with the V^T buffer
     uint64_t s_full[2];         // both: S tile in TMEM
     uint64_t p_full;            // CTA 0: every softmax thread of both CTAs wrote P
@@ -159,10 +163,12 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&ctl->kv_full[i], 1);
-            mbar_init(&ctl->cv_full[i], 2 * kConvThreads);
+            mbar_init(&ctl->kc_full[i], 2 * kConvThreads);
+            mbar_init(&ctl->vread[i], kConvThreads);
             mbar_init(&ctl->pv_done[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
+            mbar_init(&ctl->vc_full[i], 2 * kConvThreads);
             mbar_init(&ctl->vt_free[i], 1);
             mbar_init(&ctl->s_full[i], 1);
         }
@@ -252,10 +258,13 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             };
             // This CTA's boxes of key tile t: K of keys [64 t + 32 r, +32) (all
             // dims), V of keys [64 t, +64) (dims [64 r, 64 r + 64)).
+            // The stage is free once S read the previous tile's K and this CTA's
+            // converters read its V.
             auto load = [&](uint32_t n, int t) -> bool {
                 const uint32_t st = stage_of(n);
                 if (n >= uint32_t(kStages)) {
                     if (!wait_all(&ctl->pv_done[st], stage_parity(n - kStages))) return false;
+                    if (!wait_all(&ctl->vread[st], stage_parity(n - kStages))) return false;
                     next_wait = n - kStages + 1;  // its load had landed (S read it)
                 }
                 if (lane == 0) {
@@ -306,10 +315,10 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 next_load = n + 1;
                 return true;
             };
-            // S(n) = Q_lo K_hi + Q_hi K_lo + Q_hi K_hi, once both CTAs converted
-            // tile n's stage
+            // S(n) = Q_lo K_hi + Q_hi K_lo + Q_hi K_hi, once both CTAs wrote tile
+            // n's K_lo (the V^T conversion runs on beside it)
             auto issue_s = [&](uint32_t n) -> bool {
-                if (!wait_all(&ctl->cv_full[stage_of(n)], stage_parity(n))) return false;
+                if (!wait_all(&ctl->kc_full[stage_of(n)], stage_parity(n))) return false;
                 if (lane == 0) {
                     tc::fence_after_sync();
                     const uint32_t qa = smem_addr(sQ);
@@ -359,6 +368,9 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             bool ok = true;
             for (int t = 0; ok && t < min(ntiles, kStages); ++t) ok = load(n0 + t, t);
             if (lead) {
+                // S(n+1) is queued behind S(n), the load of tile n+2 goes out as
+                // soon as its stage is free (while the softmax works on S(n)),
+                // then O(n) once P(n) and V^T(n) are in place.
                 if (ok) ok = issue_s(n0);
                 for (int t = 0; ok && t < ntiles; ++t) {
                     const uint32_t n = n0 + t;
@@ -366,10 +378,14 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                         ok = issue_s(n + 1);
                         if (!ok) break;
                     }
-                    ok = wait_all(&ctl->p_full, n & 1u);
+                    if (t + kStages < ntiles) {
+                        ok = load(n + kStages, t + kStages);
+                        if (!ok) break;
+                    }
+                    ok = wait_all(&ctl->vc_full[n & 1u], (n >> 1) & 1u) &&
+                         wait_all(&ctl->p_full, n & 1u);
                     if (!ok) break;
                     issue_o(n, t == 0);
-                    if (t + kStages < ntiles) ok = load(n + kStages, t + kStages);
                 }
             } else {
                 for (int t = kStages; ok && t < ntiles; ++t) ok = load(n0 + t, t);
@@ -404,6 +420,8 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                         klp[j] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
                     }
                 }
+                tc::fence_async_smem();
+                tc::mbar_arrive_rank(&ctl->kc_full[stage_of(n)], 0);
                 if (n >= 2 && !__all_sync(0xffffffffu, wait_pair(&ctl->vt_free[n & 1u],
                                                                   ((n >> 1) - 1) & 1u, ctl, rank))) {
                     ok = false;
@@ -430,8 +448,9 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     *reinterpret_cast<float4*>(row + kVtBytes + pos * 16) =
                         make_float4(lo[0], lo[1], lo[2], lo[3]);
                 }
+                mbar_arrive(&ctl->vread[stage_of(n)]);  // this stage's V is no longer read
                 tc::fence_async_smem();
-                tc::mbar_arrive_rank(&ctl->cv_full[stage_of(n)], 0);
+                tc::mbar_arrive_rank(&ctl->vc_full[n & 1u], 0);
             }
             (void)ok;
         } else {
