@@ -30,8 +30,9 @@
 //              in CTA 0 also the pair's MMAs and their commits, which arrive
 //              on the barriers of both CTAs (tcgen05.commit multicast);
 //   warps 5-12 converters: K_lo, and V^T hi / lo of this CTA's dimensions.
-// Cross-CTA hand-offs: every converter and softmax thread of both CTAs
-// arrives (at cluster scope) on CTA 0's kc_full / vc_full / p_full (K_lo for S,
+// Cross-CTA hand-offs: every converter and softmax warp of both CTAs (one
+// lane, after the warp synchronised, so one cluster-scope release per warp)
+// arrives on CTA 0's kc_full / vc_full / p_full (K_lo for S,
 // V^T for O, P for O, kept apart so that S never waits on a V^T conversion,
 // which itself waits for the previous O); the MMA commits come
 // back to both CTAs' barriers. No named barrier is used: a thread that gives
@@ -96,13 +97,13 @@ constexpr uint16_t kBoth = 0x3;  // commit to the barriers of both CTAs
 
 struct Control {
     uint64_t kv_full[kStages];  // this CTA's TMA boxes of the stage landed
-    uint64_t kc_full[kStages];  // CTA 0: K_lo of the stage written by every converter of both CTAs
+    uint64_t kc_full[kStages];  // CTA 0: K_lo of the stage written by every converter warp of both CTAs
     uint64_t vread[kStages];    // this CTA's converters done reading the stage's V
     uint64_t pv_done[kStages];  // both: S of the stage's tile done (its K read)
-    uint64_t vc_full[2];        // CTA 0: V^T of the buffer written by every converter of both CTAs
+    uint64_t vc_full[2];        // CTA 0: V^T of the buffer written by every converter warp of both CTAs
     uint64_t vt_free[2];        // both: O done with the V^T buffer
     uint64_t s_full[2];         // both: S tile in TMEM
-    uint64_t p_full;            // CTA 0: every softmax thread of both CTAs wrote P
+    uint64_t p_full;            // CTA 0: every softmax warp of both CTAs wrote P
     uint64_t o_full;            // both: O of the tile done
     uint64_t drain;             // CTA 0: teardown
     uint32_t tmem_base;
@@ -163,16 +164,16 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&ctl->kv_full[i], 1);
-            mbar_init(&ctl->kc_full[i], 2 * kConvThreads);
+            mbar_init(&ctl->kc_full[i], 2 * kConvThreads / 32);
             mbar_init(&ctl->vread[i], kConvThreads);
             mbar_init(&ctl->pv_done[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&ctl->vc_full[i], 2 * kConvThreads);
+            mbar_init(&ctl->vc_full[i], 2 * kConvThreads / 32);
             mbar_init(&ctl->vt_free[i], 1);
             mbar_init(&ctl->s_full[i], 1);
         }
-        mbar_init(&ctl->p_full, 2 * kSoftmaxThreads);
+        mbar_init(&ctl->p_full, 2 * kSoftmaxThreads / 32);
         mbar_init(&ctl->o_full, 1);
         mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
@@ -421,7 +422,8 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     }
                 }
                 tc::fence_async_smem();
-                tc::mbar_arrive_rank(&ctl->kc_full[stage_of(n)], 0);
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive_rank(&ctl->kc_full[stage_of(n)], 0);
                 if (n >= 2 && !__all_sync(0xffffffffu, wait_pair(&ctl->vt_free[n & 1u],
                                                                   ((n >> 1) - 1) & 1u, ctl, rank))) {
                     ok = false;
@@ -450,7 +452,8 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 }
                 mbar_arrive(&ctl->vread[stage_of(n)]);  // this stage's V is no longer read
                 tc::fence_async_smem();
-                tc::mbar_arrive_rank(&ctl->vc_full[n & 1u], 0);
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive_rank(&ctl->vc_full[n & 1u], 0);
             }
             (void)ok;
         } else {
@@ -520,7 +523,8 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 }
                 tc::tmem_st_wait();
                 tc::fence_before_sync();
-                tc::mbar_arrive_rank(&ctl->p_full, 0);
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive_rank(&ctl->p_full, 0);
             }
             if (ok && ntiles > 0) {
                 const uint32_t n = n0 + ntiles - 1;
