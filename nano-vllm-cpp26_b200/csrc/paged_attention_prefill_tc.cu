@@ -84,9 +84,10 @@ constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, false);
 
 struct Control {
     uint64_t kv_full[kStages];   // TMA landed (transaction count)
-    uint64_t cv_full[kStages];   // converters done: K_lo and V^T written (256 arrivals)
-    uint64_t pv_done[kStages];   // S of the stage's tile complete: stage reusable (K read
-                                 // by S, V already turned into V^T by the converters)
+    uint64_t kc_full[kStages];   // converters wrote the stage's K_lo (256 arrivals)
+    uint64_t vread[kStages];     // converters done reading the stage's V (256 arrivals)
+    uint64_t pv_done[kStages];   // S of the stage's tile complete (its K read)
+    uint64_t vc_full[2];         // converters wrote the V^T buffer (256 arrivals)
     uint64_t vt_free[2];         // O complete: V^T buffer reusable
     uint64_t s_full[2];
     uint64_t p_full;             // P in TMEM, previous O folded (128 arrivals)
@@ -141,10 +142,12 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&ctl->kv_full[i], 1);
-            mbar_init(&ctl->cv_full[i], kConvThreads);
+            mbar_init(&ctl->kc_full[i], kConvThreads);
+            mbar_init(&ctl->vread[i], kConvThreads);
             mbar_init(&ctl->pv_done[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
+            mbar_init(&ctl->vc_full[i], kConvThreads);
             mbar_init(&ctl->vt_free[i], 1);
             mbar_init(&ctl->s_full[i], 1);
         }
@@ -230,9 +233,13 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 const bool got = wait_or_abort(bar, parity, ctl);
                 return __all_sync(0xffffffffu, got);
             };
+            // the stage is free once S read the earlier tile's K and the
+            // converters read its V
             auto load = [&](uint32_t n, int t) -> bool {
                 const uint32_t st = stage_of(n);
-                if (n >= uint32_t(kStages) && !wait_all(&ctl->pv_done[st], stage_parity(n - kStages))) {
+                if (n >= uint32_t(kStages) &&
+                    (!wait_all(&ctl->pv_done[st], stage_parity(n - kStages)) ||
+                     !wait_all(&ctl->vread[st], stage_parity(n - kStages)))) {
                     return false;
                 }
                 if (lane == 0) {
@@ -266,10 +273,11 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 next_load = n + 1;
                 return true;
             };
-            // once the converters have split tile n's K:
+            // once the converters have split tile n's K (its V^T conversion,
+            // which waits for an earlier O, does not hold S back):
             // S(n) = Q_hi K_hi^T + Q_lo K_hi^T + Q_hi K_lo^T
             auto issue_s = [&](uint32_t n) -> bool {
-                if (!wait_all(&ctl->cv_full[stage_of(n)], stage_parity(n))) return false;
+                if (!wait_all(&ctl->kc_full[stage_of(n)], stage_parity(n))) return false;
                 next_wait = n + 1;
                 if (lane == 0) {
                     tc::fence_after_sync();
@@ -321,7 +329,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     ok = issue_s(n + 1);
                     if (!ok) break;
                 }
-                ok = wait_all(&ctl->p_full, n & 1u);
+                ok = wait_all(&ctl->vc_full[n & 1u], (n >> 1) & 1u) && wait_all(&ctl->p_full, n & 1u);
                 if (!ok) break;
                 issue_o(n, t == 0);
                 if (t + kStages < ntiles) ok = load(n + kStages, t + kStages);
@@ -352,6 +360,8 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                         klp[j] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
                     }
                 }
+                tc::fence_async_smem();
+                mbar_arrive(&ctl->kc_full[stage_of(n)]);
                 if (n >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&ctl->vt_free[n & 1u],
                                                                      ((n >> 1) - 1) & 1u, ctl))) {
                     break;
@@ -377,8 +387,9 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     *reinterpret_cast<float4*>(vt + kVtBytes + d * 128 + pos * 16) =
                         make_float4(lo[0], lo[1], lo[2], lo[3]);
                 }
+                mbar_arrive(&ctl->vread[stage_of(n)]);
                 tc::fence_async_smem();
-                mbar_arrive(&ctl->cv_full[stage_of(n)]);
+                mbar_arrive(&ctl->vc_full[n & 1u]);
             }
         } else {
             // ------------------------------------------------------------ softmax warps
