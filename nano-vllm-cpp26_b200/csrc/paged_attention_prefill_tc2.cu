@@ -139,6 +139,11 @@ __device__ __forceinline__ float tf32_lo(float x) {
     return x - __uint_as_float(__float_as_uint(x) & 0xffffe000u);
 }
 
+#ifndef NVLLM_RESCALE_MARGIN
+#define NVLLM_RESCALE_MARGIN 8.0f
+#endif
+constexpr float kRescaleMargin = NVLLM_RESCALE_MARGIN;
+
 __device__ __forceinline__ uint32_t stage_of(uint32_t n) { return n % kStages; }
 __device__ __forceinline__ uint32_t stage_parity(uint32_t n) { return (n / kStages) & 1u; }
 
@@ -483,7 +488,13 @@ prefill_tc2_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     sc[j] = (kp <= qpos && kp < nk) ? sc[j] * p.qk_scale_log2 : -INFINITY;
                     cm = fmaxf(cm, sc[j]);
                 }
-                const float m_new = fmaxf(m_run, cm);
+                // The row's reference maximum moves only when a score exceeds it
+                // by more than kRescaleMargin (log2 units): until then the
+                // weights exp2(s - m) stay <= 2^margin, O and l keep their
+                // scale, and the rescale of O (a TMEM round trip between one
+                // tile's P.V and the next tile's P) is skipped. The reference
+                // cancels in O / l, so only rounding differs.
+                const float m_new = cm > m_run + kRescaleMargin ? cm : m_run;
                 const float alpha = exp2f(m_run - m_new);
                 float ps = 0.f;
 #pragma unroll
