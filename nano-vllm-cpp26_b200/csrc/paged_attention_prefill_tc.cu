@@ -19,9 +19,9 @@
 //              3-stage ring and all tcgen05.mma: S(t+1) = Q K(t+1)^T is issued
 //              while the softmax warps work on S(t); O(t) = P(t) V(t) once P(t)
 //              is in TMEM, accumulating into O in TMEM.
-//   warps 5-12 converters, working ahead of the MMAs: write the lo part of the
-//              landed K tile, and transpose V into the K-major V^T hi / lo
-//              operand (zero past the visible keys) in one of two V^T buffers.
+//   warps 5-12 converters, working ahead of the MMAs: write the lo parts of the
+//              landed K and V tiles next to them, and zero the V rows of keys
+//              past the visible ones.
 // Both products run as 3xTF32 (A_hi B_hi + A_lo B_hi + A_hi B_lo), which keeps
 // them at fp32 accuracy: a single tf32 pass errs by ~1e-3 in the output at
 // these magnitudes (one visible key => the output is that key's V row, carried
@@ -30,11 +30,12 @@
 // 13 bits cleared), exact in fp32; the terms left out (lo*lo and lo's own low
 // bits) are ~2^-20 of the product. Q_hi and Q_lo live in TMEM as the A operand
 // of S, P_hi and P_lo in TMEM as the A operand of O.
-// The shared-memory operands (K and V^T parts) are K-major in the 128-byte
-// swizzled layout (TMA writes K that way; the converters write V^T in the same
-// pattern). V must be transposed on chip: a tf32 operand can only be consumed
-// K-major here, and V arrives key-major. TMEM (512 columns): S twice (2 x 32),
-// P_hi and P_lo (32 each), O (128), Q_hi and Q_lo (128 each).
+// The shared-memory operands are the tiles as TMA lands them (128-byte
+// swizzle) and their lo parts in the same layout: K read K-major for S (the
+// 32 dims of an atom row contiguous along the reduction), V read MN-major for
+// O (the same rows, the reduction running down the keys), so V needs no
+// transpose on chip. TMEM (512 columns): S twice (2 x 32), P_hi and P_lo (32
+// each), O (128), Q_hi and Q_lo (128 each).
 // Every wait is bounded; on a timeout the CTA records NVLLM_ERR_TIMEOUT, lets
 // its outstanding copies and MMAs finish and frees its TMEM.
 #include <cuda.h>
@@ -70,25 +71,21 @@ constexpr uint32_t kColQlo = 384;
 
 constexpr uint32_t kKVAtom = kKT * 128;         // 32 rows x 32 fp32
 constexpr uint32_t kKBytes = 4 * kKVAtom;       // 16 KiB per tensor tile
-constexpr uint32_t kStageBytes = 3 * kKBytes;   // K (= K_hi), K_lo, V
-constexpr uint32_t kVtBytes = kHD * 128;        // 128 dims x 32 keys (one of hi / lo)
-constexpr uint32_t kVtBufBytes = 2 * kVtBytes;  // hi + lo
+constexpr uint32_t kStageBytes = 4 * kKBytes;   // K (= K_hi), K_lo, V (= V_hi), V_lo
 constexpr uint32_t kOffKV = 0;
-constexpr uint32_t kOffVt = kOffKV + kStages * kStageBytes;
-constexpr uint32_t kOffBar = kOffVt + 2 * kVtBufBytes;
+constexpr uint32_t kOffBar = kOffKV + kStages * kStageBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + control block + alignment slack
 static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
 
 constexpr uint32_t kIdescS = tc::tf32_idesc(kQT, kKT, false, false);
-constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, false);
+// O's B operand is V as TMA lands it: MN-major (the 32 dims of an atom row
+// contiguous, keys down the rows)
+constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, true);
 
 struct Control {
     uint64_t kv_full[kStages];   // TMA landed (transaction count)
-    uint64_t kc_full[kStages];   // converters wrote the stage's K_lo (256 arrivals)
-    uint64_t vread[kStages];     // converters done reading the stage's V (256 arrivals)
-    uint64_t pv_done[kStages];   // S of the stage's tile complete (its K read)
-    uint64_t vc_full[2];         // converters wrote the V^T buffer (256 arrivals)
-    uint64_t vt_free[2];         // O complete: V^T buffer reusable
+    uint64_t cv_full[kStages];   // converters wrote the stage's K_lo and V_lo (256 arrivals)
+    uint64_t st_free[kStages];   // O of the stage's tile complete: its K and V read
     uint64_t s_full[2];
     uint64_t p_full;             // P in TMEM, previous O folded (128 arrivals)
     uint64_t o_full;
@@ -138,7 +135,6 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* sKV = base + kOffKV;
-    unsigned char* sVt = base + kOffVt;
     Control* ctl = reinterpret_cast<Control*>(base + kOffBar);
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -147,13 +143,10 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&ctl->kv_full[i], 1);
-            mbar_init(&ctl->kc_full[i], kConvThreads);
-            mbar_init(&ctl->vread[i], kConvThreads);
-            mbar_init(&ctl->pv_done[i], 1);
+            mbar_init(&ctl->cv_full[i], kConvThreads);
+            mbar_init(&ctl->st_free[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&ctl->vc_full[i], kConvThreads);
-            mbar_init(&ctl->vt_free[i], 1);
             mbar_init(&ctl->s_full[i], 1);
         }
         mbar_init(&ctl->p_full, kSoftmaxThreads);
@@ -238,13 +231,12 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 const bool got = wait_or_abort(bar, parity, ctl);
                 return __all_sync(0xffffffffu, got);
             };
-            // the stage is free once S read the earlier tile's K and the
-            // converters read its V
+            // the stage is free once O of its earlier tile completed (S read
+            // its K before)
             auto load = [&](uint32_t n, int t) -> bool {
                 const uint32_t st = stage_of(n);
                 if (n >= uint32_t(kStages) &&
-                    (!wait_all(&ctl->pv_done[st], stage_parity(n - kStages)) ||
-                     !wait_all(&ctl->vread[st], stage_parity(n - kStages)))) {
+                    !wait_all(&ctl->st_free[st], stage_parity(n - kStages))) {
                     return false;
                 }
                 if (lane == 0) {
@@ -278,11 +270,10 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 next_load = n + 1;
                 return true;
             };
-            // once the converters have split tile n's K (its V^T conversion,
-            // which waits for an earlier O, does not hold S back):
+            // once the converters have split tile n's K and V:
             // S(n) = Q_hi K_hi^T + Q_lo K_hi^T + Q_hi K_lo^T
             auto issue_s = [&](uint32_t n) -> bool {
-                if (!wait_all(&ctl->kc_full[stage_of(n)], stage_parity(n))) return false;
+                if (!wait_all(&ctl->cv_full[stage_of(n)], stage_parity(n))) return false;
                 next_wait = n + 1;
                 if (lane == 0) {
                     tc::fence_after_sync();
@@ -299,32 +290,39 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                         tc::mma_tf32_ts(ts, tmem + kColQhi + 8u * k, bhi, kIdescS, true);
                     }
                     tc::commit(&ctl->s_full[n & 1u]);
-                    tc::commit(&ctl->pv_done[stage_of(n)]);
                     issued_mma = true;
                 }
                 __syncwarp();
                 return true;
             };
-            // O(n) = P_hi V_hi + P_lo V_hi + P_hi V_lo, P from TMEM, V^T from the
-            // buffer the converters filled for tile n
+            // O(n) = P_hi V_hi + P_lo V_hi + P_hi V_lo, P from TMEM, V and V_lo
+            // from the stage, read MN-major: keys 8k..8k+7 are one 8-row group
+            // (1 KiB into each 4 KiB atom), the 128 dims four 32-dim atoms
+            // 4 KiB apart (leading byte offset), 8-row groups 1 KiB apart
+            // (stride byte offset)
             auto issue_o = [&](uint32_t n, bool first) {
                 if (lane == 0) {
                     tc::fence_after_sync();
-                    const uint32_t va = smem_addr(sVt + (n & 1u) * kVtBufBytes);
+                    const uint32_t va = smem_addr(sKV + stage_of(n) * kStageBytes + 2 * kKBytes);
+                    const uint32_t vla = va + kKBytes;
 #pragma unroll
                     for (int k = 0; k < kKT / 8; ++k) {
-                        const uint64_t vhi = tc::sw128_desc(va + k * 32u, 16, 1024);
-                        const uint64_t vlo = tc::sw128_desc(va + kVtBytes + k * 32u, 16, 1024);
+                        const uint64_t vhi = tc::sw128_desc(va + k * 1024u, kKVAtom, 1024);
+                        const uint64_t vlo = tc::sw128_desc(vla + k * 1024u, kKVAtom, 1024);
                         tc::mma_tf32_ts(tO, tmem + kColPlo + 8u * k, vhi, kIdescO, k > 0 || !first);
                         tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vlo, kIdescO, true);
                         tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vhi, kIdescO, true);
                     }
                     tc::commit(&ctl->o_full);
-                    tc::commit(&ctl->vt_free[n & 1u]);
+                    tc::commit(&ctl->st_free[stage_of(n)]);
                 }
                 __syncwarp();
             };
 
+            // S(n+1) is queued while the softmax works on S(n); the stage of
+            // tile n-1 is refilled (with tile n+2) once O(n-1) has completed,
+            // which it has by then or soon, so that the wait never holds back
+            // an MMA that could be queued.
             bool ok = true;
             for (int t = 0; ok && t < min(ntiles, kStages); ++t) ok = load(n0 + t, t);
             if (ok) ok = issue_s(n0);
@@ -334,18 +332,20 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     ok = issue_s(n + 1);
                     if (!ok) break;
                 }
-                ok = wait_all(&ctl->vc_full[n & 1u], (n >> 1) & 1u) && wait_all(&ctl->p_full, n & 1u);
+                if (t >= 1 && t - 1 + kStages < ntiles) {
+                    ok = load(n - 1 + kStages, t - 1 + kStages);
+                    if (!ok) break;
+                }
+                ok = wait_all(&ctl->p_full, n & 1u);
                 if (!ok) break;
                 issue_o(n, t == 0);
-                if (t + kStages < ntiles) ok = load(n + kStages, t + kStages);
             }
         } else if (warp > kProducerWarp) {
             // -------------------------------------------------------------- converters
-            // thread c: 4 float4 of K_lo, then keys 16*(c/128) .. +15 of V^T row c%128
+            // thread c: 4 float4 of K_lo, then 4 float4 of V_lo; V rows of keys
+            // past the visible ones (stale rows of the last block, or blocks
+            // not loaded) are zeroed in V and V_lo
             const int c = tid - (kSoftmaxThreads + 32);
-            const int d = c & (kHD - 1);  // dimension = V^T row
-            const int kh = c >> 7;        // which 16 keys of the tile
-            const int vt_dd = d & 31;     // dimension within its V atom
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
                 // wait outcomes are made warp-uniform, so that no lane is left
@@ -355,46 +355,28 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     break;
                 }
                 unsigned char* stage = sKV + stage_of(n) * kStageBytes;
-                {
-                    const float4* kp = reinterpret_cast<const float4*>(stage);
-                    float4* klp = reinterpret_cast<float4*>(stage + kKBytes);
-#pragma unroll
-                    for (int i = 0; i < int(kKBytes / 16) / kConvThreads; ++i) {
-                        const int j = c + i * kConvThreads;
-                        const float4 v = kp[j];
-                        klp[j] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
-                    }
-                }
-                tc::fence_async_smem();
-                mbar_arrive(&ctl->kc_full[stage_of(n)]);
-                if (n >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&ctl->vt_free[n & 1u],
-                                                                     ((n >> 1) - 1) & 1u, ctl))) {
-                    break;
-                }
-                unsigned char* vt = sVt + (n & 1u) * kVtBufBytes;
                 const int nvk = nk - t * kKT;
-                const unsigned char* sV = stage + 2 * kKBytes + (d >> 5) * kKVAtom + (vt_dd & 3) * 4;
+                const float4* kp = reinterpret_cast<const float4*>(stage);
+                float4* klp = reinterpret_cast<float4*>(stage + kKBytes);
+                float4* vp = reinterpret_cast<float4*>(stage + 2 * kKBytes);
+                float4* vlp = reinterpret_cast<float4*>(stage + 3 * kKBytes);
 #pragma unroll
-                for (int q = 4 * kh; q < 4 * kh + 4; ++q) {
-                    float hi[4], lo[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int k = 4 * q + e;
-                        const float x = k < nvk ? *reinterpret_cast<const float*>(
-                                                      sV + k * 128 + (((vt_dd >> 2) ^ (k & 7)) * 16))
-                                                : 0.f;
-                        hi[e] = x;
-                        lo[e] = tf32_lo(x);
+                for (int i = 0; i < int(kKBytes / 16) / kConvThreads; ++i) {
+                    const int j = c + i * kConvThreads;
+                    const float4 k4 = kp[j];
+                    klp[j] = make_float4(tf32_lo(k4.x), tf32_lo(k4.y), tf32_lo(k4.z), tf32_lo(k4.w));
+                    // float4 j of the V tile: atom j / 256, key row (j % 256) / 8
+                    const int key = (j & 255) >> 3;
+                    if (key < nvk) {
+                        const float4 v4 = vp[j];
+                        vlp[j] = make_float4(tf32_lo(v4.x), tf32_lo(v4.y), tf32_lo(v4.z), tf32_lo(v4.w));
+                    } else {
+                        vp[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        vlp[j] = make_float4(0.f, 0.f, 0.f, 0.f);
                     }
-                    const int pos = q ^ (d & 7);
-                    *reinterpret_cast<float4*>(vt + d * 128 + pos * 16) =
-                        make_float4(hi[0], hi[1], hi[2], hi[3]);
-                    *reinterpret_cast<float4*>(vt + kVtBytes + d * 128 + pos * 16) =
-                        make_float4(lo[0], lo[1], lo[2], lo[3]);
                 }
-                mbar_arrive(&ctl->vread[stage_of(n)]);
                 tc::fence_async_smem();
-                mbar_arrive(&ctl->vc_full[n & 1u]);
+                mbar_arrive(&ctl->cv_full[stage_of(n)]);
             }
         } else {
             // ------------------------------------------------------------ softmax warps
