@@ -30,11 +30,12 @@
 // 13 bits cleared), exact in fp32; the terms left out (lo*lo and lo's own low
 // bits) are ~2^-20 of the product. Q_hi and Q_lo live in TMEM as the A operand
 // of S, P_hi and P_lo in TMEM as the A operand of O.
-// The shared-memory operands are the tiles as TMA lands them (128-byte
-// swizzle) and their lo parts in the same layout: K read K-major for S (the
-// 32 dims of an atom row contiguous along the reduction), V read MN-major for
-// O (the same rows, the reduction running down the keys), so V needs no
-// transpose on chip. TMEM (512 columns): S twice (2 x 32), P_hi and P_lo (32
+// The shared-memory operands are the tiles as TMA lands them and their lo
+// parts in the same layout: K read K-major for S (128-byte swizzle, the 32
+// dims of an atom row contiguous along the reduction), V read MN-major for O
+// (the same rows, the reduction running down the keys; an MN-major tf32
+// operand takes the 128-byte swizzle with 32-byte granules, which V's tensor
+// map asks TMA for), so V needs no transpose on chip. TMEM (512 columns): S twice (2 x 32), P_hi and P_lo (32
 // each), O (128), Q_hi and Q_lo (128 each).
 // Every wait is bounded; on a timeout the CTA records NVLLM_ERR_TIMEOUT, lets
 // its outstanding copies and MMAs finish and frees its TMEM.
@@ -296,10 +297,10 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 return true;
             };
             // O(n) = P_hi V_hi + P_lo V_hi + P_hi V_lo, P from TMEM, V and V_lo
-            // from the stage, read MN-major: keys 8k..8k+7 are one 8-row group
-            // (1 KiB into each 4 KiB atom), the 128 dims four 32-dim atoms
-            // 4 KiB apart (leading byte offset), 8-row groups 1 KiB apart
-            // (stride byte offset)
+            // from the stage, read MN-major (V lands in the 128-byte swizzle
+            // with 32-byte granules): keys 8k..8k+7 start 1 KiB into each
+            // 32-dim atom, the atoms of the 128 dims lie 4 KiB apart (leading
+            // byte offset), rows go in fours 512 bytes apart (stride byte offset)
             auto issue_o = [&](uint32_t n, bool first) {
                 if (lane == 0) {
                     tc::fence_after_sync();
@@ -307,8 +308,8 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     const uint32_t vla = va + kKBytes;
 #pragma unroll
                     for (int k = 0; k < kKT / 8; ++k) {
-                        const uint64_t vhi = tc::sw128_desc(va + k * 1024u, kKVAtom, 1024);
-                        const uint64_t vlo = tc::sw128_desc(vla + k * 1024u, kKVAtom, 1024);
+                        const uint64_t vhi = tc::sw128_32b_desc(va + k * 1024u, kKVAtom, 512);
+                        const uint64_t vlo = tc::sw128_32b_desc(vla + k * 1024u, kKVAtom, 512);
                         tc::mma_tf32_ts(tO, tmem + kColPlo + 8u * k, vhi, kIdescO, k > 0 || !first);
                         tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vlo, kIdescO, true);
                         tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vhi, kIdescO, true);
@@ -513,8 +514,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2D view of an arena: rows (block, layer, slot) x columns H*hd, box = one
-// block's 16 rows x 32 columns, 128-byte swizzle.
-bool make_arena_map(CUtensorMap* map, const float* arena, const ArenaGeom& g) {
+// block's 16 rows x 32 columns, 128-byte swizzle (16-byte granules for K, the
+// K-major operand; 32-byte granules for V, the MN-major one).
+bool make_arena_map(CUtensorMap* map, const float* arena, const ArenaGeom& g,
+                    CUtensorMapSwizzle swizzle) {
     auto fn = encode_fn();
     if (fn == nullptr) return false;
     const cuuint64_t dims[2] = {cuuint64_t(g.row),
@@ -523,7 +526,7 @@ bool make_arena_map(CUtensorMap* map, const float* arena, const ArenaGeom& g) {
     const cuuint32_t box[2] = {32, 16};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(arena), dims, strides,
-              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -535,7 +538,8 @@ int32_t prefill_tc_tile_rows() { return kQT; }
 
 cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream, int max_sms) {
     CUtensorMap kmap, vmap;
-    if (!make_arena_map(&kmap, p.k_arena, p.g) || !make_arena_map(&vmap, p.v_arena, p.g)) {
+    if (!make_arena_map(&kmap, p.k_arena, p.g, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_arena_map(&vmap, p.v_arena, p.g, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) {
         return cudaErrorInvalidValue;
     }
     static int grid_per_device[64] = {0};

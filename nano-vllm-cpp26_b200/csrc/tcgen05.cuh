@@ -54,6 +54,23 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
     return d;
 }
 
+// Descriptor for an MN-major 32-bit operand in the 128-byte swizzle with
+// 32-byte granules (the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+// the only shared-memory layout an MN-major tf32 operand may take): 128 bytes
+// contiguous along MN per row, rows along K in atoms of four; the leading byte
+// offset steps to the next 128 bytes along MN, the stride byte offset to the
+// next four rows along K. Layout type 1.
+__device__ __forceinline__ uint64_t sw128_32b_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                                   uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= uint64_t((saddr >> 4) & 0x3FFFu);
+    d |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= uint64_t(1) << 46;
+    d |= uint64_t(1) << 61;
+    return d;
+}
+
 // Instruction descriptor for kind::tf32 with fp32 accumulation.
 // a_mn / b_mn: operand is MN-major (else K-major).
 __host__ __device__ constexpr uint32_t tf32_idesc(int M, int N, bool a_mn, bool b_mn) {
