@@ -95,9 +95,6 @@ cudaError_t launch_prefill_fp32(const AttnParams& p, cudaStream_t stream, int ma
 cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream, int max_sms = 0);
 bool prefill_tc_supported(const ArenaGeom& g);
 int32_t prefill_tc_tile_rows();
-// The CTA-pair tensor-core prefill (256-row tiles over two SMs, cta_group::2).
-cudaError_t launch_prefill_tc2(const AttnParams& p, cudaStream_t stream, int max_sms = 0);
-int32_t prefill_tc2_tile_rows();
 
 // Positions per decode work item: 16 chunks of 2048/hd positions (256 KiB of
 // K+V at any head_dim).

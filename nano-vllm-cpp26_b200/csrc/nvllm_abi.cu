@@ -18,8 +18,6 @@ namespace {
 constexpr size_t kAlign = 256;
 // SMs for a prefill beside the decode by default (0: one after the other)
 constexpr int kDefaultPrefillSms = 0;
-// the tensor-core prefill on CTA pairs by default
-constexpr bool kDefaultPrefillTcPairs = false;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -181,16 +179,6 @@ int prefill_beside_sms() {
     return v;
 }
 
-// The tensor-core prefill on CTA pairs (NVLLM_PREFILL_TC=2) or one CTA per
-// tile (1).
-bool prefill_tc_pairs() {
-    static const bool v = [] {
-        const char* s = std::getenv("NVLLM_PREFILL_TC");
-        return s != nullptr ? std::atoi(s) == 2 : kDefaultPrefillTcPairs;
-    }();
-    return v;
-}
-
 // plan -> prefill (if any multi-row sequence) and decode + merge. With a
 // prefill share configured, the prefill's persistent grid is bounded to that
 // many SMs and the decode is launched as its programmatic dependent: the
@@ -204,15 +192,12 @@ cudaError_t launch_attention(AttnParams& p, int32_t precision, cudaStream_t st) 
     // error is far inside the TF32 tolerance.
     const bool tc_prefill =
         precision == NVLLM_PRECISION_TF32 && p.max_query_len > 1 && prefill_tc_supported(p.g);
-    const bool pairs = tc_prefill && prefill_tc_pairs();
-    if (tc_prefill) p.prefill_tile = pairs ? prefill_tc2_tile_rows() : prefill_tc_tile_rows();
+    if (tc_prefill) p.prefill_tile = prefill_tc_tile_rows();
     cudaError_t e = launch_plan(p, st);
     if (e != cudaSuccess) return e;
     const int beside = p.max_query_len > 1 ? prefill_beside_sms() : 0;
     if (p.max_query_len > 1) {
-        e = pairs        ? launch_prefill_tc2(p, st, beside)
-            : tc_prefill ? launch_prefill_tc(p, st, beside)
-                         : launch_prefill_fp32(p, st, beside);
+        e = tc_prefill ? launch_prefill_tc(p, st, beside) : launch_prefill_fp32(p, st, beside);
         if (e != cudaSuccess) return e;
     }
     return launch_decode(p, st, /*overlap_previous=*/beside > 0);

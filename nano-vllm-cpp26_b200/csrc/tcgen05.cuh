@@ -177,97 +177,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
         : "memory");
 }
 
-// ---- CTA pairs (a cluster of two CTAs on two SMs, cta_group::2) ------------
-// The pair's MMAs are issued by one thread of CTA 0 and run on both SMs: A and
-// D are split by rows (CTA r holds rows [r*M/2, (r+1)*M/2) in its own TMEM /
-// shared memory), B by columns (CTA r holds columns [r*N/2, (r+1)*N/2) of B at
-// the same shared-memory offset). TMEM is allocated in both CTAs at once by
-// one warp of each (the same warp index).
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// Every thread of both CTAs: release this CTA's prior writes, wait for the
-// other CTA's. Not .aligned: the lanes of a warp may arrive from different
-// paths (a wait that gave up).
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
-    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
-}
-// The shared::cluster address of the same shared-memory object in CTA `rank`.
-__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
-    return r;
-}
-// One arrival on an mbarrier of CTA `rank` (release at cluster scope).
-__device__ __forceinline__ void mbar_arrive_rank(uint64_t* bar, uint32_t rank) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
-                     map_to_rank(bar, rank))
-                 : "memory");
-}
-__device__ __forceinline__ void st_rank_u32(uint32_t* p, uint32_t rank, uint32_t v) {
-    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank(p, rank)), "r"(v)
-                 : "memory");
-}
-// try_wait whose completing arrivals may come from the other CTA of the pair.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_addr(slot)),
-                 "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-                 : "memory");
-}
-
-// Pair MMA, A and B from shared memory.
-__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                              uint32_t idesc, bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
-        : "memory");
-}
-// Pair MMA, A from TMEM (each CTA's rows in its own lanes), B from shared memory.
-__device__ __forceinline__ void mma_tf32_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                                 uint32_t idesc, bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
-        : "memory");
-}
-// One arrival on the mbarrier at this shared-memory offset in each CTA of
-// `cta_mask` once the pair MMAs issued so far have completed.
-__device__ __forceinline__ void commit_pair(uint64_t* bar, uint16_t cta_mask) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%0], %1;" ::"r"(smem_addr(bar)),
-        "h"(cta_mask)
-        : "memory");
-}
-
 // fp32 -> tf32, round to nearest (ties away), kept in an fp32 container.
 __device__ __forceinline__ float to_tf32(float x) {
     uint32_t r;

@@ -476,10 +476,10 @@ def test_tf32_other_geometries_use_fp32_prefill(nv, oracle):
 
 
 def test_tf32_prefill_tile_boundaries(nv, oracle):
-    """Prefills whose row counts straddle the tensor-core kernels' query tiles
-    (128 rows per CTA, 256 per CTA pair) and their 32 / 64-key tiles, fresh
-    and chunked (rows starting mid-context), with decodes beside them; every
-    row against the oracle at the TF32 tolerance."""
+    """Prefills whose row counts straddle the tensor-core kernel's 128-row
+    query tiles and 32-key tiles (and twice those), fresh and chunked (rows
+    starting mid-context), with decodes beside them; every row against the
+    oracle at the TF32 tolerance."""
     ctx = np.array([255, 256, 257, 511, 513, 100, 640, 300, 1000, 77, 3000], np.int32)
     ql = np.array([255, 256, 257, 511, 513, 100, 260, 44, 129, 1, 1], np.int32)
     b = build_batch(nv, seed=42, num_blocks=2048, block_size=16, num_heads=8, head_dim=128,
