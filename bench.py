@@ -699,7 +699,7 @@ def nvllm_main(args, spec):
 def mixed_leg(args, nvllm, lay, ka, va, dev, stream, ranks: Ranks, sampler, rank: int) -> dict:
     """The mixed prefill + decode super-batch (8 causal prefills U[512, 2048] +
     120 decodes with contexts U[256, 8192]) on the same arenas: the whole step
-    with tensor-core (3xTF32) and with fp32 prefill tiles, and its two parts
+    with tensor-core and with fp32 prefill tiles, and its two parts
     alone (prefills; decodes), each timed like the main leg. Per part: the
     prefill's QK^T + PV FLOPs per second, the decode's algorithmic bytes per
     second. A sample of the step's rows is checked against the oracle."""
@@ -1669,7 +1669,7 @@ def main() -> int:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", choices=["fp32", "tf32"], default=None,
                     help="prefill tile arithmetic (decode is always fp32): fp32 FFMA, or tcgen05 "
-                         "3xTF32 (fp32 quality); default tf32 for a serving workload whose "
+                         "with two-term bf16 products (1e-3); default tf32 for a serving workload whose "
                          "projections run on the tcgen05 GEMMs, else fp32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",

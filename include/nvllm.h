@@ -41,9 +41,11 @@ enum nvllm_status {
 
 enum nvllm_precision {
     NVLLM_PRECISION_FP32 = 0,  /* fp32 FFMA everywhere (max-abs 2e-5 vs the reference) */
-    NVLLM_PRECISION_TF32 = 1   /* prefill QK^T / PV tiles on tcgen05 kind::tf32 (1e-3) when
-                                  head_dim is 128 and block_size 16; other geometries keep
-                                  the fp32 prefill */
+    NVLLM_PRECISION_TF32 = 1   /* prefill QK^T / PV tiles on the tcgen05 tensor cores (1e-3):
+                                  each fp32 operand split into two bf16 terms, three bf16
+                                  products per product, fp32 accumulation; when head_dim is
+                                  128 and block_size 16 (other geometries keep the fp32
+                                  prefill) */
 };
 
 typedef struct nvllm_kv_layout {

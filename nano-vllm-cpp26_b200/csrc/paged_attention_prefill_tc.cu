@@ -1,46 +1,51 @@
-// K3 (TF32 tensor cores): causal paged prefill attention on tcgen05.
+// K3 (tensor cores): causal paged prefill attention on tcgen05.
 //
 // Same mathematics as src/model.cpp:204-260 for sequences with more than one
 // query row, with the two dense products QK^T and PV on the 5th-generation
-// tensor cores (kind::tf32, fp32 accumulation in TMEM); softmax in fp32.
+// tensor cores (fp32 accumulation in TMEM) and the softmax in fp32.
 // Geometry: head_dim 128, block size 16 (one TMA box = the 16 rows of one
 // physical block and 32 columns of one head).
 //
-// One CTA per SM (persistent), 13 warps:
+// Operand precision: every fp32 operand x is split into two bf16 terms,
+// x0 = bf16(x) and x1 = bf16(x - x0) (16 significant bits together, against
+// 11 for one tf32 operand), and each product is taken as three bf16 MMAs
+// (kind::f16) with fp32 accumulation: A0 B0 + A0 B1 + A1 B0; the dropped A1 B1
+// is ~2^-16 of the product. Against tf32 hi / lo parts, bf16 terms take half
+// the bytes in TMEM and shared memory and an MMA covers 16 of the reduction
+// instead of 8, so the S tile is 64 keys wide: a 64-key tile takes 24 S MMAs
+// (N = 64) and 12 O MMAs (N = 128).
+//
+// One CTA per SM (persistent), 9 warps:
 //   warps 0-3  softmax / epilogue: thread t owns query row t of a 128-row tile
-//              and TMEM lane t. Per key tile (32 keys) it reads its row of S
-//              from TMEM (tcgen05.ld), applies the causal mask, updates the
-//              online max and sum, rescales its row of the O accumulator in
-//              TMEM by exp(m_old - m_new) (skipped when no row of the warp saw
-//              its maximum grow: the factor is then exactly 1), and stores P as
-//              tf32 hi / lo parts into its own TMEM lane (the A operand of P.V).
-//   warp 4     producer: one thread issues the TMA gathers of the K and V
-//              tiles (2 physical blocks x 4 swizzle atoms per tensor) into a
-//              3-stage ring and all tcgen05.mma: S(t+1) = Q K(t+1)^T is issued
-//              while the softmax warps work on S(t); O(t) = P(t) V(t) once P(t)
-//              is in TMEM, accumulating into O in TMEM.
-//   warps 5-12 converters, working ahead of the MMAs: write the lo parts of the
-//              landed K and V tiles next to them, and zero the V rows of keys
-//              past the visible ones.
-// Both products run as 3xTF32 (A_hi B_hi + A_lo B_hi + A_hi B_lo), which keeps
-// them at fp32 accuracy: a single tf32 pass errs by ~1e-3 in the output at
-// these magnitudes (one visible key => the output is that key's V row, carried
-// at tf32 precision). The tensor core reads a tf32 operand as the top 19 bits
-// of its fp32 container, so hi is the value itself and lo = x - (x with its low
-// 13 bits cleared), exact in fp32; the terms left out (lo*lo and lo's own low
-// bits) are ~2^-20 of the product. Q_hi and Q_lo live in TMEM as the A operand
-// of S, P_hi and P_lo in TMEM as the A operand of O.
-// The shared-memory operands are the tiles as TMA lands them and their lo
-// parts in the same layout: K read K-major for S (128-byte swizzle, the 32
-// dims of an atom row contiguous along the reduction), V read MN-major for O
-// (the same rows, the reduction running down the keys; an MN-major tf32
-// operand takes the 128-byte swizzle with 32-byte granules, which V's tensor
-// map asks TMA for), so V needs no transpose on chip. TMEM (512 columns): S twice (2 x 32), P_hi and P_lo (32
-// each), O (128), Q_hi and Q_lo (128 each).
+//              and TMEM lane t. Per key tile it reads its row of S from TMEM,
+//              applies the causal mask, updates the running maximum and sum,
+//              rescales its row of O in TMEM when its reference maximum moved
+//              (rarely: see kRescaleMargin), and stores P as two bf16 terms into
+//              its TMEM lane, in one of two P buffers (the A operand of P.V).
+//   warp 4     producer: the warp waits, lane 0 issues the TMA gathers of the K
+//              and V tiles (4 physical blocks x 4 swizzle atoms per tensor) into
+//              a 3-stage ring and all tcgen05.mma: S(t+1) = Q K(t+1)^T is queued
+//              while the softmax works on S(t); O(t) += P(t) V(t) once P(t) is in
+//              TMEM.
+//   warps 5-8  converters: turn each landed fp32 K tile, then V tile, in place,
+//              into its two bf16 terms, zeroing the V rows of keys past the
+//              visible ones; S waits only for K's terms, O for V's.
+// Shared memory per stage (64 keys): K as landed, fp32 in four 128-byte
+// swizzled atoms of 32 dims, then in the same 32 KiB its terms K0 and K1, each
+// two 128-byte swizzled atoms of 64 bf16 dims (the K-major B operand of S); V
+// likewise, its terms read MN-major as the B operand of O (a 16-bit MN-major
+// operand takes the plain 128-byte swizzle, so V needs no transpose). The fp32
+// atoms land in the order 0, 2, 1, 3, so that the two that hold dims 64 p ..
+// 64 p + 63 occupy exactly the bytes their terms go to (term 0 atom p, term 1
+// atom p): two rows of an atom pair are read and written back by one warp,
+// with no wait on any other.
+// TMEM (512 columns): S x2 (2 x 64), P x2 (2 buffers x 2 terms x 32 columns of
+// bf16 pairs), O (128), Q (2 terms x 64).
 // Every wait is bounded; on a timeout the CTA records NVLLM_ERR_TIMEOUT, lets
 // its outstanding copies and MMAs finish and frees its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_bf16.h>
 
 #include <algorithm>
 #include <mutex>
@@ -54,42 +59,67 @@ namespace nvllm {
 namespace {
 
 constexpr int kQT = 128;  // query rows per tile (= TMEM lanes)
-constexpr int kKT = 32;   // keys per tile
+constexpr int kKT = 64;   // keys per tile
 constexpr int kHD = 128;
 constexpr int kStages = 3;
 constexpr int kSoftmaxThreads = 128;  // warps 0-3
 constexpr int kProducerWarp = 4;
-constexpr int kConvThreads = 256;     // warps 5-12
+constexpr int kConvThreads = 128;     // warps 5-8
 constexpr int kThreads = kSoftmaxThreads + 32 + kConvThreads;
-// TMEM columns: S[0] 0..31, S[1] 32..63, P_hi 64..95, P_lo 96..127, O 128..255,
-// Q_hi 256..383, Q_lo 384..511
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColPhi = 64;
-constexpr uint32_t kColPlo = 96;
-constexpr uint32_t kColO = 128;
-constexpr uint32_t kColQhi = 256;
-constexpr uint32_t kColQlo = 384;
 
-constexpr uint32_t kKVAtom = kKT * 128;         // 32 rows x 32 fp32
-constexpr uint32_t kKBytes = 4 * kKVAtom;       // 16 KiB per tensor tile
-constexpr uint32_t kStageBytes = 4 * kKBytes;   // K (= K_hi), K_lo, V (= V_hi), V_lo
+// TMEM columns: S[0] 0..63, S[1] 64..127, P[b] at 128 + 64 b (term 0 then
+// term 1, 32 columns each), O 256..383, Q term 0 384..447, term 1 448..511
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColP = 128;
+constexpr uint32_t kColO = 256;
+constexpr uint32_t kColQ = 384;
+
+// Shared memory: a stage holds the fp32 K tile (4 atoms of 64 keys x 32 dims)
+// then the V tile; after conversion each tile's 32 KiB hold its term 0 (2
+// atoms of 64 keys x 64 bf16 dims) then its term 1.
+constexpr uint32_t kF32Atom = kKT * 128;      // 64 rows x 32 fp32
+constexpr uint32_t kB16Atom = kKT * 128;      // 64 rows x 64 bf16
+constexpr uint32_t kTileBytes = 4 * kF32Atom; // one fp32 tile, or its two terms
+constexpr uint32_t kTermBytes = 2 * kB16Atom; // one bf16 term of a tile
+constexpr uint32_t kStageBytes = 2 * kTileBytes;
 constexpr uint32_t kOffKV = 0;
 constexpr uint32_t kOffBar = kOffKV + kStages * kStageBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + control block + alignment slack
 static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
+// Byte offset of fp32 atom a (dims 32 a .. 32 a + 31) in a landed tile: atoms
+// 2 p and 2 p + 1 at p * 8 KiB and 16 KiB + p * 8 KiB, where term 0 and term 1
+// of atom p go.
+__host__ __device__ constexpr uint32_t f32_atom_offset(int a) {
+    return uint32_t((a & 1) * 2 + (a >> 1)) * kF32Atom;
+}
+static_assert(kF32Atom == kB16Atom && kTermBytes == 2 * kF32Atom, "atom pairs hold their terms");
+constexpr int kConvUnits = (kKT / 2) * (kHD / 64);  // per tensor: row pairs x atom pairs
+static_assert(kConvUnits % (kConvThreads / 32) == 0, "converter split");
 
-constexpr uint32_t kIdescS = tc::tf32_idesc(kQT, kKT, false, false);
-// O's B operand is V as TMA lands it: MN-major (the 32 dims of an atom row
-// contiguous, keys down the rows)
-constexpr uint32_t kIdescO = tc::tf32_idesc(kQT, kHD, false, true);
+// Instruction descriptor for kind::f16 with bf16 A and B and fp32
+// accumulation; b_mn: B is MN-major (else K-major).
+constexpr uint32_t bf16_idesc(int M, int N, bool b_mn) {
+    return (1u << 4)                    // D format: f32
+           | (1u << 7)                  // A format: bf16
+           | (1u << 10)                 // B format: bf16
+           | (uint32_t(b_mn) << 16)     // B major
+           | (uint32_t(N >> 3) << 17)   // N / 8
+           | (uint32_t(M >> 4) << 24);  // M / 16
+}
+constexpr uint32_t kIdescS = bf16_idesc(kQT, kKT, false);
+constexpr uint32_t kIdescO = bf16_idesc(kQT, kHD, true);
 
 struct Control {
-    uint64_t kv_full[kStages];   // TMA landed (transaction count)
-    uint64_t cv_full[kStages];   // converters wrote the stage's K_lo and V_lo (256 arrivals)
-    uint64_t st_free[kStages];   // O of the stage's tile complete: its K and V read
+    uint64_t kv_full[kStages];  // TMA landed (transaction count)
+    uint64_t kc_full[kStages];  // converters wrote K's bf16 terms (128 arrivals)
+    uint64_t vc_full[kStages];  // converters wrote V's bf16 terms (128 arrivals)
+    uint64_t st_free[kStages];  // O of the stage's tile complete: its K and V read
     uint64_t s_full[2];
-    uint64_t p_full;             // P in TMEM, previous O folded (128 arrivals)
-    uint64_t o_full;
+    // Per P buffer b (the tiles n with n % 2 == b), so that neither side can
+    // run two phases ahead of a waiter: p_full[b] P(n) in TMEM and O rescaled
+    // when needed (128 arrivals); p_free[b] O(n) complete (P(n) and O(n) read)
+    uint64_t p_full[2];
+    uint64_t p_free[2];
     uint64_t drain;
     uint32_t tmem_base;
     int32_t item;
@@ -112,12 +142,21 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Co
     }
 }
 
-// x = x_hi + lo exactly, with x_hi = x with its low 13 bits cleared (what the
-// tensor core reads of a tf32 operand)
-__device__ __forceinline__ float tf32_lo(float x) {
-    return x - __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+// Two-term bf16 split of a and b: x = x0 + x1 + r with x0 = bf16(x),
+// x1 = bf16(x - x0), |r| <= 2^-17 |x|. t0 packs a0 (low half) and b0, t1 a1 and b1.
+__device__ __forceinline__ void split2(float a, float b, uint32_t& t0, uint32_t& t1) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    t0 = *reinterpret_cast<const uint32_t*>(&h);
+    t1 = *reinterpret_cast<const uint32_t*>(&l);
 }
 
+// The row's reference maximum moves only when a score exceeds it by more than
+// this (log2 units): until then the weights exp2(s - m) stay <= 2^margin, O
+// and l keep their scale, and the rescale of O (a TMEM round trip between one
+// tile's P.V and the next tile's P) is skipped. The reference cancels in O / l,
+// so only rounding differs.
 #ifndef NVLLM_RESCALE_MARGIN
 #define NVLLM_RESCALE_MARGIN 8.0f
 #endif
@@ -125,6 +164,41 @@ constexpr float kRescaleMargin = NVLLM_RESCALE_MARGIN;
 
 __device__ __forceinline__ uint32_t stage_of(uint32_t n) { return n % kStages; }
 __device__ __forceinline__ uint32_t stage_parity(uint32_t n) { return (n / kStages) & 1u; }
+
+// Stores 32 columns of raw 32-bit words into this warp's TMEM lanes.
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+    float f[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+    tc::tmem_st32(taddr, f);
+}
+
+// In-place conversion of one landed fp32 tile (64 keys x 128 dims) into its
+// two bf16 terms by one converter warp: unit u = (row pair u / 2, atom pair
+// u % 2); lane l reads 16 bytes of atom 2 p + l / 16, row 2 (u / 2) + (l / 8) % 2,
+// swizzle position l % 8 -- together the 512 bytes the unit's terms then
+// occupy -- and, after the warp has read, writes 8 bytes of each term (each
+// row's 128 bytes of a term written whole: no bank conflicts). Rows >=
+// zero_from become 0.
+__device__ __forceinline__ void convert_unit(unsigned char* tile, int u, int lane, int zero_from) {
+    const int ap = u & 1;
+    const int a = 2 * ap + ((lane >> 4) & 1);
+    const int row = 2 * (u >> 1) + ((lane >> 3) & 1);
+    const int phys = lane & 7;
+    float4 x = *reinterpret_cast<const float4*>(tile + f32_atom_offset(a) + row * 128 + phys * 16);
+    __syncwarp();
+    if (row >= zero_from) x = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int dim = 32 * a + ((phys ^ (row & 7)) << 2);  // the first of the 4 dims
+    uint32_t a0, a1, b0, b1;
+    split2(x.x, x.y, a0, a1);
+    split2(x.z, x.w, b0, b1);
+    // term atom ap, the row, 16-byte chunk (dim % 64) / 8 swizzled by the row,
+    // 8 bytes in when dim % 8 == 4
+    const uint32_t off = uint32_t(ap) * kB16Atom + uint32_t(row) * 128u +
+                         uint32_t(((dim & 63) >> 3) ^ (row & 7)) * 16u + uint32_t(dim & 4) * 2u;
+    *reinterpret_cast<uint2*>(tile + off) = make_uint2(a0, b0);
+    *reinterpret_cast<uint2*>(tile + kTermBytes + off) = make_uint2(a1, b1);
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
 prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
@@ -144,14 +218,15 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&ctl->kv_full[i], 1);
-            mbar_init(&ctl->cv_full[i], kConvThreads);
+            mbar_init(&ctl->kc_full[i], kConvThreads);
+            mbar_init(&ctl->vc_full[i], kConvThreads);
             mbar_init(&ctl->st_free[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&ctl->s_full[i], 1);
+            mbar_init(&ctl->p_full[i], kSoftmaxThreads);
+            mbar_init(&ctl->p_free[i], 1);
         }
-        mbar_init(&ctl->p_full, kSoftmaxThreads);
-        mbar_init(&ctl->o_full, 1);
         mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
     }
@@ -169,9 +244,9 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     const ArenaGeom& g = p.g;
     const int H = g.num_heads;
     const int total = p.counters->prefill_items * H;
-    uint32_t tile_seq = 0;   // key tiles processed by this CTA (ring position)
-    uint32_t next_load = 0;  // producer: ring index of the next K/V load to issue
-    uint32_t next_wait = 0;  // producer: ring index of the next load not known to have landed
+    uint32_t tile_seq = 0;    // key tiles processed by this CTA (ring position)
+    uint32_t next_load = 0;   // producer: ring index of the next K/V load to issue
+    uint32_t next_wait = 0;   // producer: ring index of the next load not known to have landed
     bool issued_mma = false;
 
     for (;;) {
@@ -195,28 +270,24 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
         const uint32_t n0 = tile_seq;
 
         if (tid < kSoftmaxThreads) {
-            // Q tile -> TMEM as the A operand of S = Q K^T, split for 3xTF32
-            // (q_hi = q as read by the tensor core, q_lo = the rest).
+            // Q tile -> TMEM as the A operand of S = Q K^T: term 0 in columns
+            // 384.., term 1 in 448.., one pair of consecutive dims per column
             const int row = tid;
             const uint32_t lane_off = uint32_t(warp * 32) << 16;
             const float4* qrow = reinterpret_cast<const float4*>(
                 p.q + int64_t(q0 + r0 + row) * g.row + int64_t(h) * kHD);
 #pragma unroll 1
-            for (int c = 0; c < kHD / 32; ++c) {
-                float hi[32], lo[32];
+            for (int c = 0; c < 2; ++c) {  // 64 dims -> 32 columns of each term
+                uint32_t t0[32], t1[32];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
+                for (int i = 0; i < 16; ++i) {
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (row < nrows) v = __ldg(qrow + c * 8 + i);
-                    const float x[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        hi[4 * i + e] = x[e];
-                        lo[4 * i + e] = tf32_lo(x[e]);
-                    }
+                    if (row < nrows) v = __ldg(qrow + c * 16 + i);
+                    split2(v.x, v.y, t0[2 * i], t1[2 * i]);
+                    split2(v.z, v.w, t0[2 * i + 1], t1[2 * i + 1]);
                 }
-                tc::tmem_st32(tmem + kColQhi + c * 32u + lane_off, hi);
-                tc::tmem_st32(tmem + kColQlo + c * 32u + lane_off, lo);
+                tmem_st32u(tmem + kColQ + c * 32u + lane_off, t0);
+                tmem_st32u(tmem + kColQ + 64u + c * 32u + lane_off, t1);
             }
             tc::tmem_st_wait();
             tc::fence_before_sync();
@@ -225,8 +296,6 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
 
         if (warp == kProducerWarp) {
             // ---------------------------------------------------------------- producer
-            // Lane 0 issues the TMA copies, the MMAs and their commits; the whole
-            // warp takes part in the waits.
             const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
             auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
                 const bool got = wait_or_abort(bar, parity, ctl);
@@ -242,7 +311,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 }
                 if (lane == 0) {
                     unsigned char* sK = sKV + st * kStageBytes;
-                    unsigned char* sV = sK + 2 * kKBytes;
+                    unsigned char* sV = sK + kTileBytes;
                     const int kbase = t * kKT;
                     const int nvalid = min(kKT, nk - kbase);
                     const int nblk = (nvalid + 15) / 16;
@@ -262,8 +331,9 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
 #pragma unroll
                         for (int a = 0; a < 4; ++a) {
                             const int x = h * kHD + a * 32;
-                            tc::tma_load_2d(sK + a * kKVAtom + j * 2048, &kmap, x, y, &ctl->kv_full[st]);
-                            tc::tma_load_2d(sV + a * kKVAtom + j * 2048, &vmap, x, y, &ctl->kv_full[st]);
+                            const uint32_t off = f32_atom_offset(a) + uint32_t(j) * 2048u;
+                            tc::tma_load_2d(sK + off, &kmap, x, y, &ctl->kv_full[st]);
+                            tc::tma_load_2d(sV + off, &vmap, x, y, &ctl->kv_full[st]);
                         }
                     }
                 }
@@ -271,24 +341,28 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 next_load = n + 1;
                 return true;
             };
-            // once the converters have split tile n's K and V:
-            // S(n) = Q_hi K_hi^T + Q_lo K_hi^T + Q_hi K_lo^T
+            // once the converters have split K of tile n:
+            // S(n) = Q1 K0^T + Q0 K1^T + Q0 K0^T, 16 dims per MMA; dims 16k..
+            // start 32 k bytes into the rows of atom k / 4 (K-major, 8-row
+            // groups 1 KiB apart)
             auto issue_s = [&](uint32_t n) -> bool {
-                if (!wait_all(&ctl->cv_full[stage_of(n)], stage_parity(n))) return false;
+                if (!wait_all(&ctl->kc_full[stage_of(n)], stage_parity(n))) return false;
                 next_wait = n + 1;
                 if (lane == 0) {
                     tc::fence_after_sync();
-                    const uint32_t ka = smem_addr(sKV + stage_of(n) * kStageBytes);
-                    const uint32_t kla = ka + kKBytes;
+                    const uint32_t k0 = smem_addr(sKV + stage_of(n) * kStageBytes);
+                    const uint32_t k1 = k0 + kTermBytes;
                     const uint32_t ts = tmem + (n & 1u) * kKT;
 #pragma unroll
-                    for (int k = 0; k < kHD / 8; ++k) {
-                        const uint32_t off = (k >> 2) * kKVAtom + (k & 3) * 32u;  // 8 tf32 = 32 B
-                        const uint64_t bhi = tc::sw128_desc(ka + off, 16, 1024);
-                        const uint64_t blo = tc::sw128_desc(kla + off, 16, 1024);
-                        tc::mma_tf32_ts(ts, tmem + kColQlo + 8u * k, bhi, kIdescS, k > 0);
-                        tc::mma_tf32_ts(ts, tmem + kColQhi + 8u * k, blo, kIdescS, true);
-                        tc::mma_tf32_ts(ts, tmem + kColQhi + 8u * k, bhi, kIdescS, true);
+                    for (int k = 0; k < kHD / 16; ++k) {
+                        const uint32_t off = (k >> 2) * kB16Atom + (k & 3) * 32u;
+                        const uint64_t d0 = tc::sw128_desc(k0 + off, 16, 1024);
+                        const uint64_t d1 = tc::sw128_desc(k1 + off, 16, 1024);
+                        const uint32_t q0c = tmem + kColQ + 8u * k;
+                        const uint32_t q1c = q0c + 64u;
+                        tc::mma_f16_ts(ts, q1c, d0, kIdescS, k > 0);
+                        tc::mma_f16_ts(ts, q0c, d1, kIdescS, true);
+                        tc::mma_f16_ts(ts, q0c, d0, kIdescS, true);
                     }
                     tc::commit(&ctl->s_full[n & 1u]);
                     issued_mma = true;
@@ -296,34 +370,34 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 __syncwarp();
                 return true;
             };
-            // O(n) = P_hi V_hi + P_lo V_hi + P_hi V_lo, P from TMEM, V and V_lo
-            // from the stage, read MN-major (V lands in the 128-byte swizzle
-            // with 32-byte granules): keys 8k..8k+7 start 1 KiB into each
-            // 32-dim atom, the atoms of the 128 dims lie 4 KiB apart (leading
-            // byte offset), rows go in fours 512 bytes apart (stride byte offset)
-            auto issue_o = [&](uint32_t n, bool first) {
+            // O(n) += P1 V0 + P0 V1 + P0 V0, P from its TMEM buffer, V's terms
+            // MN-major: keys 16k.. start 2 KiB into each 64-dim atom, the two
+            // atoms of the 128 dims 8 KiB apart (leading byte offset), 8-key
+            // groups 1 KiB apart (stride byte offset)
+            auto issue_o = [&](uint32_t n, bool first) -> bool {
+                if (!wait_all(&ctl->vc_full[stage_of(n)], stage_parity(n))) return false;
                 if (lane == 0) {
                     tc::fence_after_sync();
-                    const uint32_t va = smem_addr(sKV + stage_of(n) * kStageBytes + 2 * kKBytes);
-                    const uint32_t vla = va + kKBytes;
+                    const uint32_t v0 = smem_addr(sKV + stage_of(n) * kStageBytes + kTileBytes);
+                    const uint32_t v1 = v0 + kTermBytes;
+                    const uint32_t pb = tmem + kColP + (n & 1u) * 64u;
 #pragma unroll
-                    for (int k = 0; k < kKT / 8; ++k) {
-                        const uint64_t vhi = tc::sw128_32b_desc(va + k * 1024u, kKVAtom, 512);
-                        const uint64_t vlo = tc::sw128_32b_desc(vla + k * 1024u, kKVAtom, 512);
-                        tc::mma_tf32_ts(tO, tmem + kColPlo + 8u * k, vhi, kIdescO, k > 0 || !first);
-                        tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vlo, kIdescO, true);
-                        tc::mma_tf32_ts(tO, tmem + kColPhi + 8u * k, vhi, kIdescO, true);
+                    for (int k = 0; k < kKT / 16; ++k) {
+                        const uint64_t d0 = tc::sw128_desc(v0 + k * 2048u, kB16Atom, 1024);
+                        const uint64_t d1 = tc::sw128_desc(v1 + k * 2048u, kB16Atom, 1024);
+                        tc::mma_f16_ts(tO, pb + 32u + 8u * k, d0, kIdescO, k > 0 || !first);
+                        tc::mma_f16_ts(tO, pb + 8u * k, d1, kIdescO, true);
+                        tc::mma_f16_ts(tO, pb + 8u * k, d0, kIdescO, true);
                     }
-                    tc::commit(&ctl->o_full);
+                    tc::commit(&ctl->p_free[n & 1u]);
                     tc::commit(&ctl->st_free[stage_of(n)]);
                 }
                 __syncwarp();
+                return true;
             };
 
             // S(n+1) is queued while the softmax works on S(n); the stage of
-            // tile n-1 is refilled (with tile n+2) once O(n-1) has completed,
-            // which it has by then or soon, so that the wait never holds back
-            // an MMA that could be queued.
+            // tile n-1 is refilled (with tile n+2) once O(n-1) has completed.
             bool ok = true;
             for (int t = 0; ok && t < min(ntiles, kStages); ++t) ok = load(n0 + t, t);
             if (ok) ok = issue_s(n0);
@@ -337,16 +411,11 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     ok = load(n - 1 + kStages, t - 1 + kStages);
                     if (!ok) break;
                 }
-                ok = wait_all(&ctl->p_full, n & 1u);
-                if (!ok) break;
-                issue_o(n, t == 0);
+                ok = wait_all(&ctl->p_full[n & 1u], (n >> 1) & 1u) && issue_o(n, t == 0);
             }
         } else if (warp > kProducerWarp) {
             // -------------------------------------------------------------- converters
-            // thread c: 4 float4 of K_lo, then 4 float4 of V_lo; V rows of keys
-            // past the visible ones (stale rows of the last block, or blocks
-            // not loaded) are zeroed in V and V_lo
-            const int c = tid - (kSoftmaxThreads + 32);
+            const int cw = warp - (kProducerWarp + 1);  // converter warp 0..7
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
                 // wait outcomes are made warp-uniform, so that no lane is left
@@ -356,28 +425,19 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     break;
                 }
                 unsigned char* stage = sKV + stage_of(n) * kStageBytes;
+                // K rows past the visible keys are masked by the softmax; V's
+                // are zeroed, for their zero weights to cancel
                 const int nvk = nk - t * kKT;
-                const float4* kp = reinterpret_cast<const float4*>(stage);
-                float4* klp = reinterpret_cast<float4*>(stage + kKBytes);
-                float4* vp = reinterpret_cast<float4*>(stage + 2 * kKBytes);
-                float4* vlp = reinterpret_cast<float4*>(stage + 3 * kKBytes);
-#pragma unroll
-                for (int i = 0; i < int(kKBytes / 16) / kConvThreads; ++i) {
-                    const int j = c + i * kConvThreads;
-                    const float4 k4 = kp[j];
-                    klp[j] = make_float4(tf32_lo(k4.x), tf32_lo(k4.y), tf32_lo(k4.z), tf32_lo(k4.w));
-                    // float4 j of the V tile: atom j / 256, key row (j % 256) / 8
-                    const int key = (j & 255) >> 3;
-                    if (key < nvk) {
-                        const float4 v4 = vp[j];
-                        vlp[j] = make_float4(tf32_lo(v4.x), tf32_lo(v4.y), tf32_lo(v4.z), tf32_lo(v4.w));
-                    } else {
-                        vp[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        vlp[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+                for (int part = 0; part < 2; ++part) {  // K, then V
+                    unsigned char* tile = stage + part * kTileBytes;
+#pragma unroll 4
+                    for (int u = cw; u < kConvUnits; u += kConvThreads / 32) {
+                        convert_unit(tile, u, lane, part == 0 ? kKT : nvk);
                     }
+                    tc::fence_async_smem();
+                    mbar_arrive(part == 0 ? &ctl->kc_full[stage_of(n)] : &ctl->vc_full[stage_of(n)]);
                 }
-                tc::fence_async_smem();
-                mbar_arrive(&ctl->cv_full[stage_of(n)]);
             }
         } else {
             // ------------------------------------------------------------ softmax warps
@@ -388,13 +448,15 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             bool ok = true;
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
-                if (!__all_sync(0xffffffffu, wait_or_abort(&ctl->s_full[n & 1u], (n >> 1) & 1u, ctl))) {
+                if (!__all_sync(0xffffffffu,
+                                wait_or_abort(&ctl->s_full[n & 1u], (n >> 1) & 1u, ctl))) {
                     ok = false;
                     break;
                 }
                 tc::fence_after_sync();
                 float sc[kKT];
                 tc::tmem_ld32(tmem + (n & 1u) * kKT + lane_off, sc);
+                tc::tmem_ld32(tmem + (n & 1u) * kKT + 32u + lane_off, sc + 32);
                 tc::tmem_ld_wait();
                 const int kbase = t * kKT;
                 float cm = -INFINITY;
@@ -404,61 +466,66 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                     sc[j] = (kp <= qpos && kp < nk) ? sc[j] * p.qk_scale_log2 : -INFINITY;
                     cm = fmaxf(cm, sc[j]);
                 }
-                // The row's reference maximum moves only when a score exceeds it
-                // by more than kRescaleMargin (log2 units): until then the
-                // weights exp2(s - m) stay <= 2^margin, O and l keep their
-                // scale, and the rescale of O (a TMEM round trip between one
-                // tile's P.V and the next tile's P) is skipped. The reference
-                // cancels in O / l, so only rounding differs.
                 const float m_new = cm > m_run + kRescaleMargin ? cm : m_run;
                 const float alpha = exp2f(m_run - m_new);
-                float ps = 0.f;
-#pragma unroll
-                for (int j = 0; j < kKT; ++j) {
-                    sc[j] = exp2f(sc[j] - m_new);
-                    ps += sc[j];
-                }
-                l_run = fmaf(l_run, alpha, ps);
+                l_run *= alpha;
                 m_run = m_new;
-                if (t > 0) {
-                    // previous tile's P.V is in O: P's TMEM columns are free, and O
-                    // can be rescaled to the new maximum before this tile's P.V
-                    if (!__all_sync(0xffffffffu, wait_or_abort(&ctl->o_full, (n - 1) & 1u, ctl))) {
+                // the P buffer is free once O of the tile two back completed
+                if (n >= 2 && !__all_sync(0xffffffffu,
+                                          wait_or_abort(&ctl->p_free[n & 1u],
+                                                        ((n >> 1) - 1) & 1u, ctl))) {
+                    ok = false;
+                    break;
+                }
+                if (t > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                    // O must hold the previous tile's P.V before it is rescaled
+                    if (!__all_sync(0xffffffffu,
+                                    wait_or_abort(&ctl->p_free[(n - 1) & 1u],
+                                                  ((n - 1) >> 1) & 1u, ctl))) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
-                        for (int c = 0; c < kHD / 32; ++c) {
-                            float ov[32];
-                            tc::tmem_ld32(tO + c * 32u + lane_off, ov);
-                            tc::tmem_ld_wait();
+                    for (int c = 0; c < kHD / 32; ++c) {
+                        float ov[32];
+                        tc::tmem_ld32(tO + c * 32u + lane_off, ov);
+                        tc::tmem_ld_wait();
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) ov[j] *= alpha;
-                            tc::tmem_st32(tO + c * 32u + lane_off, ov);
-                        }
+                        for (int j = 0; j < 32; ++j) ov[j] *= alpha;
+                        tc::tmem_st32(tO + c * 32u + lane_off, ov);
                     }
+                } else if (n >= 2) {
+                    tc::fence_after_sync();
                 }
-                // P -> this row's TMEM lane as tf32 hi / lo parts (A operand of O)
-                {
-                    float lo[kKT];
+                // P = exp2(s - m) as two bf16 terms, 32 keys (16 columns of each
+                // term) at a time
+                const uint32_t pb = tmem + kColP + (n & 1u) * 64u + lane_off;
 #pragma unroll
-                    for (int j = 0; j < kKT; ++j) lo[j] = tf32_lo(sc[j]);
-                    tc::tmem_st32(tmem + kColPhi + lane_off, sc);
-                    tc::tmem_st32(tmem + kColPlo + lane_off, lo);
-                    tc::tmem_st_wait();
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t p0[16], p1[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float a = exp2f(sc[32 * half + 2 * j] - m_new);
+                        const float b = exp2f(sc[32 * half + 2 * j + 1] - m_new);
+                        l_run += a + b;
+                        split2(a, b, p0[j], p1[j]);
+                    }
+                    tc::tmem_st16(pb + 16u * half, p0);
+                    tc::tmem_st16(pb + 32u + 16u * half, p1);
                 }
+                tc::tmem_st_wait();
                 tc::fence_before_sync();
-                mbar_arrive(&ctl->p_full);
+                mbar_arrive(&ctl->p_full[n & 1u]);
             }
             if (ok && ntiles > 0) {
                 const uint32_t n = n0 + ntiles - 1;
-                if (__all_sync(0xffffffffu, wait_or_abort(&ctl->o_full, n & 1u, ctl))) {
+                if (__all_sync(0xffffffffu,
+                               wait_or_abort(&ctl->p_free[n & 1u], (n >> 1) & 1u, ctl))) {
                     tc::fence_after_sync();
                     const float inv = 1.0f / fmaxf(l_run, 1e-12f);
-                    float4* op = reinterpret_cast<float4*>(p.out + int64_t(q0 + r0 + row) * g.row +
-                                                           int64_t(h) * kHD);
+                    float4* op = reinterpret_cast<float4*>(
+                        p.out + int64_t(q0 + r0 + row) * g.row + int64_t(h) * kHD);
 #pragma unroll 1
                     for (int c = 0; c < kHD / 32; ++c) {
                         float ov[32];
@@ -514,10 +581,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2D view of an arena: rows (block, layer, slot) x columns H*hd, box = one
-// block's 16 rows x 32 columns, 128-byte swizzle (16-byte granules for K, the
-// K-major operand; 32-byte granules for V, the MN-major one).
-bool make_arena_map(CUtensorMap* map, const float* arena, const ArenaGeom& g,
-                    CUtensorMapSwizzle swizzle) {
+// block's 16 rows x 32 columns, 128-byte swizzle.
+bool make_arena_map(CUtensorMap* map, const float* arena, const ArenaGeom& g) {
     auto fn = encode_fn();
     if (fn == nullptr) return false;
     const cuuint64_t dims[2] = {cuuint64_t(g.row),
@@ -526,7 +591,7 @@ bool make_arena_map(CUtensorMap* map, const float* arena, const ArenaGeom& g,
     const cuuint32_t box[2] = {32, 16};
     const cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(arena), dims, strides,
-              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -538,8 +603,7 @@ int32_t prefill_tc_tile_rows() { return kQT; }
 
 cudaError_t launch_prefill_tc(const AttnParams& p, cudaStream_t stream, int max_sms) {
     CUtensorMap kmap, vmap;
-    if (!make_arena_map(&kmap, p.k_arena, p.g, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_arena_map(&vmap, p.v_arena, p.g, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) {
+    if (!make_arena_map(&kmap, p.k_arena, p.g) || !make_arena_map(&vmap, p.v_arena, p.g)) {
         return cudaErrorInvalidValue;
     }
     static int grid_per_device[64] = {0};

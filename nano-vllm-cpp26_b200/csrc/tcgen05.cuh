@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a tensor-core path: TMEM allocation,
-// tcgen05.mma (kind::tf32) with shared-memory operand descriptors,
+// tcgen05.mma (kind::tf32 and kind::f16) with shared-memory operand descriptors,
 // tcgen05.commit to an mbarrier, tcgen05.ld of fp32 accumulators, and 2D
 // tiled TMA loads (cp.async.bulk.tensor, no multicast).
 #pragma once
@@ -106,6 +106,19 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         : "memory");
 }
 
+// kind::f16 (bf16 or f16 operands, idesc says which): D[tmem] (+)= A[tmem] *
+// B[smem]; A K-major in TMEM, two 16-bit elements per 32-bit column (the
+// lower K index in the low half); issued by one thread.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+
 // The mbarrier receives one arrival once every tcgen05.mma this thread issued
 // before has completed.
 __device__ __forceinline__ void commit(uint64_t* bar) {
@@ -155,6 +168,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
         "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
         "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
         "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+// Stores 16 consecutive 32-bit columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+    __syncwarp();
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15])
         : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() {

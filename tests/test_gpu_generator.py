@@ -43,7 +43,8 @@ def test_generator_reproduces_reference_run(name, graphs, gemm, precision, tmp_p
     power-of-two bucket and replayed as that bucket's CUDA graph; gemm 2: every
     projection on this library's GEMMs (tcgen05 above 32 rows, the decode-size
     kernels below); precision 1: the prefill attention tiles on the tcgen05
-    3xTF32 kernel where the geometry has it (the FFMA kernel elsewhere)."""
+    kernel (two-term bf16 products) where the geometry has it (the FFMA kernel
+    elsewhere)."""
     from nvllm.host import metrics_json
     from oracle.oracle import read_trace
     cfg, z, steps, objs, prompts = build(name, precision=precision, graph_max_tokens=graphs,

@@ -275,7 +275,7 @@ def test_mixed_benchmark_full_size(nv, oracle):
     U[512, 2048] rows + 120 decodes with contexts U[256, 8192], 32 heads x hd 128,
     block size 16, block tables from the seeded permutation of the 65536-block
     arena. All 128 sequences (8376 query rows) against the oracle, with fp32
-    prefill tiles (TOL_FP32) and with tensor-core 3xTF32 tiles (TOL_TF32)."""
+    prefill tiles (TOL_FP32) and with tensor-core tiles (TOL_TF32)."""
     from nvllm.workload import make_batch
     torch = _torch()
     spec = make_batch("mixed", seed=0)
@@ -477,11 +477,11 @@ def test_tf32_other_geometries_use_fp32_prefill(nv, oracle):
 
 def test_tf32_prefill_tile_boundaries(nv, oracle):
     """Prefills whose row counts straddle the tensor-core kernel's 128-row
-    query tiles and 32-key tiles (and twice those), fresh and chunked (rows
-    starting mid-context), with decodes beside them; every row against the
-    oracle at the TF32 tolerance."""
-    ctx = np.array([255, 256, 257, 511, 513, 100, 640, 300, 1000, 77, 3000], np.int32)
-    ql = np.array([255, 256, 257, 511, 513, 100, 260, 44, 129, 1, 1], np.int32)
+    query tiles and 64-key tiles (and multiples of those), fresh and chunked
+    (rows starting mid-context), with decodes beside them; every row against
+    the oracle at the TF32 tolerance."""
+    ctx = np.array([255, 256, 257, 511, 513, 100, 640, 300, 1000, 77, 3000, 191, 193], np.int32)
+    ql = np.array([255, 256, 257, 511, 513, 100, 260, 44, 129, 1, 1, 63, 129], np.int32)
     b = build_batch(nv, seed=42, num_blocks=2048, block_size=16, num_heads=8, head_dim=128,
                     ctx_lens=ctx, q_lens=ql)
     out = run_attention(nv, b, precision=nv.PRECISION_TF32)

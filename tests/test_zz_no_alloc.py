@@ -8,7 +8,7 @@ mid-step): the workspace is a 64 MiB array owned by the library on each GPU.
 The test calls it through the C ABI twice in a row on the same mixed prefill +
 decode batch and compares both outputs with those of the workspace entry point
 (nvllm_paged_attention) at the same precision: fp32 prefill tiles within the
-fp32 tolerance of the other parity tests, tensor-core (3xTF32) prefill tiles,
+fp32 tolerance of the other parity tests, tensor-core prefill tiles,
 which lay the shared array out for their 128-row query tiles, within the TF32
 tolerance.
 It also checks that a batch needing more than 64 MiB of workspace is refused.
