@@ -6,31 +6,36 @@
 //
 // At m <= 32 the product is a stream of W (8 KB of weights per 128 x 32 x 32
 // block of MACs), so W crosses HBM once, unsplit, and everything else happens
-// on chip. The MMA computes D[128 columns of W, 32 token rows] = W^T_tile .
-// X_tile^T (M = 128 output features in TMEM lanes, N = 32 tokens, K = 8 per
-// instruction), every product in 3xTF32: hi = x rounded to tf32 (nearest),
-// lo = x - hi, and W_hi X_hi + W_lo X_hi + W_hi X_lo (the tensor core reads a
-// tf32 operand as the top 19 bits of its fp32 container). X_lo is stored right
-// after X_hi, so W_hi [X_hi | X_lo] is a single N = 64 MMA into a 64-column
-// accumulator whose halves are added when it is folded.
+// on chip. The MMA computes D[128 lanes, 128 columns of W] = A . W_tile with W
+// read straight from the TMA-landed tile as an MN-major operand (the layout W
+// has in memory: a row of W is 128 contiguous output features), so W is never
+// transposed or moved on chip. Every product is fp32-quality through tf32
+// parts: the tensor core reads a tf32 operand as the top 19 bits of its fp32
+// container, so hi = x as stored and lo = x - (x with its low 13 bits
+// cleared), exact. A lives in TMEM: lanes 0-31 hold the token rows' X_hi,
+// lanes 32-63 their X_lo, so one MMA gives X_hi W and X_lo W in the two lane
+// halves, and W_lo, written beside W by the converters, gives X_hi W_lo and
+// X_lo W_lo: two N = 128 MMAs per 8 of K. Lane t and lane 32 + t are summed
+// in fp32 at the end.
 //
-// Per stage (32 rows of K), with 11 warps per CTA (one CTA per SM, all 512
+// Per stage (32 rows of K), with 14 warps per CTA (one CTA per SM, all 512
 // TMEM columns):
-//   warp 8, lane 0: the TMA copies into an 8-stage ring (W tile 32 x 128 fp32,
-//     no swizzle; X tile 32 rows x 32 fp32, 128-byte swizzle; no multicast);
-//   warps 9-10, lane 0: the 8 MMAs of a stage, alternate stages each into its
-//     own accumulators (a single issuing thread leaves the tensor core idle
-//     around each of its mbarrier waits and commits), never waiting on an MMA;
-//   warps 0-7: converters in two groups of four that take alternate stages.
-//     Lane r of warp w owns output feature 32 (w % 4) + r: it reads column r
-//     of the W tile (32 conflict-free scalar loads: the transpose happens
-//     here), splits it and stores hi and lo into its own TMEM lane
-//     (tcgen05.st) in one of four A buffers, so the MMA takes A from TMEM
-//     (.ts form); it also splits a share of the X tile in shared memory (hi
-//     in place, lo beside). Group 0 also folds every finished accumulation
-//     chunk (an issuer's 4 stages = 128 of K: the tensor core's fp32
-//     accumulation truncates, so long sums stay in fp32 registers) into
-//     registers, two stages behind, and writes the result.
+//   warp 10, lane 0: the TMA copies into a 5-stage ring (W tile 32 x 128 fp32
+//     as four 32-column boxes in the 128-byte swizzle with 32-byte granules,
+//     the layout of an MN-major tf32 operand; X tile 32 rows x 32 fp32,
+//     128-byte swizzle; no multicast);
+//   warp 11, lane 0: the 8 MMAs of a stage into one of two accumulators, and
+//     their commits;
+//   warps 0-7: converters in two groups of four that take alternate stages:
+//     all four write W_lo; warp 4g (TMEM lanes 0-31) stores row `lane` of the
+//     X tile into its lane of the stage's A buffer, warp 4g + 1 (lanes 32-63)
+//     that row's lo part;
+//   warps 8, 9, 12, 13: fold each finished accumulation chunk (4 stages = 128
+//     of K: the tensor core's fp32 accumulation truncates, so long sums stay in
+//     fp32 registers) into registers, 64 columns each of the X_hi rows (8, 12)
+//     or the X_lo rows (9, 13); at the end of a tile's segment the X_lo warps
+//     hand their sums to the X_hi warps through shared memory, which add them
+//     and write the result.
 // Work is split stream-K: the (tile, stage) units of all output tiles are
 // dealt to the persistent CTAs in equal contiguous ranges; a tile that one CTA
 // covers whole is written directly with the epilogue op, the pieces of a
@@ -54,38 +59,36 @@
 namespace nvllm {
 namespace {
 
-constexpr int kTileN = 128;    // output features per tile (MMA M, TMEM lanes)
-constexpr int kBT = 32;        // token rows (MMA N)
+constexpr int kTileN = 128;    // output features per tile (MMA N)
+constexpr int kBT = 32;        // token rows: TMEM lanes 0-31 (X_hi), 32-63 (X_lo)
 constexpr int kStageK = 32;    // K rows per stage
-constexpr int kStages = 8;
-constexpr int kChunk = 4;      // an issuer's stages per TMEM accumulation chunk
-constexpr int kABufs = 4;      // A operand buffers in TMEM (units converted ahead)
-constexpr int kGroupThreads = 128;  // one converter group: a warp per TMEM lane quarter
-constexpr int kProducerWarp = 8;
-constexpr int kIssuers = 2;    // MMA-issuing warps: the CTA's unit g to issuer g % 2
-constexpr int kMmaWarp0 = 9;   // warps 9-10
-constexpr int kThreads = 32 * (kMmaWarp0 + kIssuers);  // converters, producer, issuers
+constexpr int kStages = 5;
+constexpr int kChunk = 4;      // stages per TMEM accumulation chunk
+constexpr int kGroupThreads = 128;  // one converter group
+constexpr int kProducerWarp = 10;
+constexpr int kIssuerWarp = 11;
+constexpr int kThreads = 14 * 32;   // converters 0-7, folders 8, 9, 12, 13, producer, issuer
+constexpr int kFoldThreads = 128;
 constexpr int kMaxBatch = 3;
 constexpr int kMinUnits = 8;   // stages a CTA handles at least
-constexpr uint32_t kWBytes = kStageK * kTileN * 4;  // 16 KB
-constexpr uint32_t kXBytes = kBT * kStageK * 4;     // 4 KB
-constexpr uint32_t kStageBytes = kWBytes + 2 * kXBytes;  // W, X (hi in place), X lo
-// TMEM: four A buffers (hi 32 + lo 32 columns each) and two accumulators (64
-// columns each: W_hi X_hi + W_lo X_hi in 0-31, W_hi X_lo in 32-63) for each MMA issuer
+constexpr uint32_t kWAtom = kStageK * 128;           // 32 K rows x 32 features: 4 KB
+constexpr uint32_t kWBytes = 4 * kWAtom;             // 16 KB
+constexpr uint32_t kXBytes = kBT * kStageK * 4;      // 4 KB
+constexpr uint32_t kStageBytes = 2 * kWBytes + kXBytes;  // W, W_lo, X
+constexpr uint32_t kScratchStride = 65;              // floats per row (no bank conflicts)
+constexpr uint32_t kScratchBytes = kBT * kScratchStride * 4;
+constexpr uint32_t kOffScratch = kStages * kStageBytes;
+constexpr uint32_t kOffCtl = kOffScratch + 2 * kScratchBytes;
+constexpr uint32_t kSmem = kOffCtl + 512 + 1024;
+static_assert(kSmem <= 227u * 1024u, "shared memory");
+static_assert(kStageBytes % 1024 == 0 && kWBytes % 1024 == 0, "swizzle atoms stay aligned");
+// TMEM: an A buffer per ring slot (32 columns, one tf32 element of K each) and
+// two accumulators of 128 columns
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColA = 0;
-constexpr uint32_t kColD = kABufs * 64;
-constexpr uint32_t kDCols = 2 * kBT;
-// X lo lies directly after X hi in the stage (same swizzle, 1024-byte row groups),
-// so W_hi [X_hi | X_lo] is one N = 64 MMA
-constexpr uint32_t kIdescHi = tc::tf32_idesc(kTileN, 2 * kBT, false, false);
-constexpr uint32_t kIdescLo = tc::tf32_idesc(kTileN, kBT, false, false);
-constexpr uint32_t kSmem = kStages * kStageBytes + 512 + 1024;
-static_assert(kSmem <= 227u * 1024u, "shared memory");
-// every ring slot (and every A buffer) belongs to one issuer: units g and g + kStages
-// (g + kABufs) go to the same issuer
-static_assert(kStages % kIssuers == 0 && kABufs % kIssuers == 0, "issuer assignment");
-static_assert(kABufs * 64 + kIssuers * 2 * kDCols <= kTmemCols, "TMEM columns");
+constexpr uint32_t kColD = 256;
+static_assert(kStages * kStageK <= int(kColD) && kColD + 2 * kTileN <= kTmemCols, "TMEM columns");
+constexpr uint32_t kIdesc = tc::tf32_idesc(128, kTileN, false, true);
 
 struct DecodeParams {
     int64_t m, n, k, ldc;
@@ -100,11 +103,13 @@ struct DecodeParams {
 
 struct Control {
     uint64_t full[kStages];    // TMA landed (transaction bytes)
-    uint64_t conv[kStages];    // A in TMEM, X split (kGroupThreads arrivals)
+    uint64_t conv[kStages];    // W_lo written, A in TMEM (kGroupThreads arrivals)
     uint64_t empty[kStages];   // the stage's MMAs completed
-    uint64_t d_full[kIssuers][2];  // [issuer][buffer] accumulation chunk complete
-    uint64_t d_free[kIssuers][2];  // chunk folded into registers (kGroupThreads arrivals)
-    uint64_t drain[kIssuers];
+    uint64_t d_full[2];        // accumulation chunk complete
+    uint64_t d_free[2];        // chunk folded into registers (kFoldThreads arrivals)
+    uint64_t comb_full[2];     // [column half] X_lo sums in scratch (32 arrivals)
+    uint64_t comb_free[2];     // [column half] scratch read (32 arrivals)
+    uint64_t drain;
     uint32_t tmem_base;
     int32_t abort;
 };
@@ -140,9 +145,17 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Co
         }
     }
 }
+// The same, its outcome the same on every lane of the warp (a warp whose lanes
+// left a spin at different iterations must not split around a collective step).
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, Control* ctl,
+                                          uint32_t where = 0) {
+    return __all_sync(0xffffffffu, wait_or_abort(bar, parity, ctl, where));
+}
 // roles and barriers of the where code
-enum : uint32_t { kWhoProducer = 1, kWhoIssuer = 2, kWhoConverter = 4 };
-enum : uint32_t { kBarFull = 1, kBarConv = 2, kBarEmpty = 3, kBarDFull = 4, kBarDFree = 5 };
+enum : uint32_t { kWhoProducer = 1, kWhoIssuer = 2, kWhoConverter = 4, kWhoFolder = 6 };
+enum : uint32_t {
+    kBarFull = 1, kBarConv = 2, kBarEmpty = 3, kBarDFull = 4, kBarDFree = 5, kBarComb = 6
+};
 __device__ __forceinline__ uint32_t where_code(uint32_t who, uint32_t bar, uint32_t g) {
     return (who << 24) | (bar << 16) | (g & 0x7fffu);
 }
@@ -176,13 +189,34 @@ __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
     return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// hi = x rounded to tf32 (nearest), lo = x - hi (exact), elementwise
-__device__ __forceinline__ void split4(float4& v, float4& lo) {
-    const float4 hi = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z),
-                                  tc::to_tf32(v.w));
-    lo = make_float4(v.x - hi.x, v.y - hi.y, v.z - hi.z, v.w - hi.w);
-    v = hi;
+// x minus the part of it the tensor core reads as tf32 (its top 19 bits): exact
+__device__ __forceinline__ float lo_part(float x) {
+    return x - __uint_as_float(__float_as_uint(x) & 0xffffe000u);
 }
+
+// Walks a CTA's units in order: the tile and stage of each, its position in
+// the tile's segment (the tile's units in this CTA), and the chunk rule shared
+// by the issuer and the folders.
+struct UnitWalk {
+    int64_t tile;
+    int stage, j, len;
+    __device__ UnitWalk(int64_t u0, int spt) : tile(u0 / spt), stage(int(u0 % spt) - 1), j(0), len(0) {}
+    // advances to unit g (called with g = 0, 1, ...); returns its position in the segment
+    __device__ int next(uint32_t g, uint32_t nu, int spt) {
+        if (++stage == spt) {
+            stage = 0;
+            ++tile;
+        }
+        if (g == 0 || stage == 0) {
+            j = 0;
+            len = min(spt - stage, int(nu - g));
+        }
+        return j++;
+    }
+    __device__ bool chunk_first(int jj) const { return jj % kChunk == 0; }
+    __device__ bool chunk_last(int jj) const { return jj % kChunk == kChunk - 1 || jj + 1 == len; }
+    __device__ bool seg_end(int jj) const { return jj + 1 == len; }
+};
 
 // grid: p.ctas persistent CTAs, CTA c owning units [first_unit(c), first_unit(c + 1))
 __global__ void __launch_bounds__(kThreads, 1)
@@ -190,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap xmap) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = align1024(smem_raw);
-    Control* ctl = reinterpret_cast<Control*>(smem + kStages * kStageBytes);
+    Control* ctl = reinterpret_cast<Control*>(smem + kOffCtl);
     const int tid = int(threadIdx.x), warp = tid / 32, lane = tid % 32;
     const int64_t u0 = first_unit(blockIdx.x, p.units, p.ctas);
     const uint32_t nu = uint32_t(first_unit(int64_t(blockIdx.x) + 1, p.units, p.ctas) - u0);
@@ -201,13 +235,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&ctl->conv[i], kGroupThreads);
             mbar_init(&ctl->empty[i], 1);
         }
-        for (int i = 0; i < kIssuers; ++i) {
-            for (int b = 0; b < 2; ++b) {
-                mbar_init(&ctl->d_full[i][b], 1);
-                mbar_init(&ctl->d_free[i][b], kGroupThreads);
-            }
-            mbar_init(&ctl->drain[i], 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->d_full[b], 1);
+            mbar_init(&ctl->d_free[b], kFoldThreads);
+            mbar_init(&ctl->comb_full[b], 32);
+            mbar_init(&ctl->comb_free[b], 32);
         }
+        mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
     }
     fence_barrier_init();
@@ -234,9 +268,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 unsigned char* st = smem + s * kStageBytes;
                 mbar_arrive_expect_tx(&ctl->full[s], kWBytes + kXBytes);
-                tma_load_3d(st, &wmap, (tile % p.n_tiles) * kTileN, stage * kStageK,
-                            tile / p.n_tiles, &ctl->full[s]);
-                tc::tma_load_2d(st + kWBytes, &xmap, stage * kStageK, 0, &ctl->full[s]);
+                const int x0 = (tile % p.n_tiles) * kTileN, y = stage * kStageK;
+#pragma unroll
+                for (int a = 0; a < kTileN / 32; ++a) {
+                    tma_load_3d(st + a * kWAtom, &wmap, x0 + a * 32, y, tile / p.n_tiles,
+                                &ctl->full[s]);
+                }
+                tc::tma_load_2d(st + 2 * kWBytes, &xmap, y, 0, &ctl->full[s]);
                 loaded = g + 1;
                 if (++stage == p.spt) {
                     stage = 0;
@@ -248,200 +286,184 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait(&ctl->full[h % kStages], (h / kStages) & 1u, kStatusInGemmDecodeTc);
             }
         }
-    } else if (warp >= kMmaWarp0 && warp < kMmaWarp0 + kIssuers) {
+    } else if (warp == kIssuerWarp) {
         // ------------------------------------------------------------------ MMAs
-        // issuer i takes the CTA's units g with g % kIssuers == i, into its own
-        // accumulators: the threads keep the tensor core busy between the waits
-        // and commits that each of them makes. Assigning by g (not by the position
-        // within a tile's segment) gives every ring slot one issuer, which waits on
-        // that slot's barrier phases in order; an issuer waiting on a slot another
-        // issuer still has to consume could see the phase before its own as done.
-        const int me = warp - kMmaWarp0;
         if (lane == 0) {
-            uint32_t q = 0;  // this issuer's accumulation chunks
+            uint32_t q = 0;  // accumulation chunks started
             bool issued_mma = false;
-            int j = 0, len = 0;  // stage within its segment, segment length
-            int stage = int(u0 % p.spt);
-            for (uint32_t g = 0; g < nu; ++g, stage = stage + 1 == p.spt ? 0 : stage + 1) {
-                if (g == 0 || stage == 0) {
-                    j = 0;
-                    len = min(p.spt - stage, int(nu - g));
-                }
-                const int jj = j++;
-                if (int(g % kIssuers) != me) continue;
-                // chunks: windows of kIssuers * kChunk units of the segment, kChunk
-                // of them this issuer's
-                const int w = jj % (kIssuers * kChunk);
-                const bool chunk_first = w < kIssuers;
-                const bool chunk_last = w >= kIssuers * (kChunk - 1) || jj + kIssuers >= len;
-                const uint32_t s = g % kStages, ab = g % kABufs, buf = q & 1u;
+            UnitWalk walk(u0, p.spt);
+            for (uint32_t g = 0; g < nu; ++g) {
+                const int jj = walk.next(g, nu, p.spt);
+                const bool first = walk.chunk_first(jj), last = walk.chunk_last(jj);
+                const uint32_t s = g % kStages, buf = q & 1u;
                 if (!wait_or_abort(&ctl->conv[s], (g / kStages) & 1u, ctl,
-                                   where_code(kWhoIssuer + uint32_t(me), kBarConv, g))) {
+                                   where_code(kWhoIssuer, kBarConv, g))) {
                     break;
                 }
-                if (chunk_first && q >= 2 &&
-                    !wait_or_abort(&ctl->d_free[me][buf], ((q >> 1) - 1) & 1u, ctl,
-                                   where_code(kWhoIssuer + uint32_t(me), kBarDFree, g))) {
+                if (first && q >= 2 &&
+                    !wait_or_abort(&ctl->d_free[buf], ((q >> 1) - 1) & 1u, ctl,
+                                   where_code(kWhoIssuer, kBarDFree, g))) {
                     break;
                 }
                 tc::fence_after_sync();
-                const uint32_t xhi = smem_addr(smem + s * kStageBytes + kWBytes);
-                const uint32_t a_hi = tmem + kColA + ab * 64u;
-                const uint32_t a_lo = a_hi + 32u;
-                const uint32_t d = tmem + kColD + uint32_t(me * 2 + int(buf)) * kDCols;
+                const uint32_t w_hi = smem_addr(smem + s * kStageBytes);
+                const uint32_t w_lo = w_hi + kWBytes;
+                const uint32_t a = tmem + kColA + s * uint32_t(kStageK);
+                const uint32_t d = tmem + kColD + buf * uint32_t(kTileN);
 #pragma unroll
                 for (int kk = 0; kk < kStageK / 8; ++kk) {
-                    // B = rows 0-31 X_hi, rows 32-63 X_lo (N = 64) / X_hi alone (N = 32)
-                    const uint64_t dh = tc::sw128_desc(xhi + uint32_t(kk) * 32u, 16, 1024);
-                    tc::mma_tf32_ts(d, a_hi + uint32_t(kk) * 8u, dh, kIdescHi,
-                                    !chunk_first || kk > 0);
-                    tc::mma_tf32_ts(d, a_lo + uint32_t(kk) * 8u, dh, kIdescLo, true);
+                    // 8 rows of K start 1 KB into each 32-feature atom; the atoms
+                    // of the 128 features are kWAtom apart (leading byte offset),
+                    // groups of 4 rows 512 bytes (stride byte offset)
+                    const uint32_t off = uint32_t(kk) * 1024u;
+                    tc::mma_tf32_ts(d, a + uint32_t(kk) * 8u, tc::sw128_32b_desc(w_hi + off, kWAtom, 512),
+                                    kIdesc, !first || kk > 0);
+                    tc::mma_tf32_ts(d, a + uint32_t(kk) * 8u, tc::sw128_32b_desc(w_lo + off, kWAtom, 512),
+                                    kIdesc, true);
                 }
                 tc::commit(&ctl->empty[s]);
-                if (chunk_last) {
-                    tc::commit(&ctl->d_full[me][buf]);
+                if (last) {
+                    tc::commit(&ctl->d_full[buf]);
                     ++q;
                 }
                 issued_mma = true;
             }
             // issued MMAs complete before the TMEM is freed (bounded wait)
             if (issued_mma) {
-                tc::commit(&ctl->drain[me]);
-                mbar_wait(&ctl->drain[me], 0, kStatusInGemmDecodeTc);
+                tc::commit(&ctl->drain);
+                mbar_wait(&ctl->drain, 0, kStatusInGemmDecodeTc);
             }
         }
-    } else {
-        // -------------------------- converters (two groups), accumulation, epilogue
-        const int grp = warp / 4;          // converts the units g with g % 2 == grp
-        const int r = tid % kGroupThreads;  // output feature within the tile = TMEM lane
-        const uint32_t lane_off = uint32_t((warp % 4) * 32) << 16;
-        float acc[kBT];
-#pragma unroll
-        for (int t = 0; t < kBT; ++t) acc[t] = 0.f;
-        uint32_t qf[kIssuers] = {};  // chunks folded, per issuer (group 0)
-        // folds issuer i's next chunk into acc (chunks are folded in the order in
-        // which they end, a fixed order)
-        auto fold = [&](int i) -> bool {
-            const uint32_t q = qf[i], buf = q & 1u;
-            if (!wait_or_abort(&ctl->d_full[i][buf], (q >> 1) & 1u, ctl,
-                               where_code(kWhoConverter, kBarDFull, (uint32_t(i) << 14) | q))) {
-                return false;
-            }
-            tc::fence_after_sync();
-            const uint32_t dcol = tmem + kColD + uint32_t(i * 2 + int(buf)) * kDCols + lane_off;
-            float v[kBT], w[kBT];
-            tc::tmem_ld32(dcol, v);
-            tc::tmem_ld32(dcol + uint32_t(kBT), w);
-            tc::tmem_ld_wait();
-#pragma unroll
-            for (int t = 0; t < kBT; ++t) acc[t] += v[t] + w[t];
-            tc::fence_before_sync();
-            mbar_arrive(&ctl->d_free[i][buf]);
-            qf[i] = q + 1;
-            return true;
-        };
-        // the segment of `tile` is complete: the whole tile (epilogue op) or a piece
-        auto finish = [&](int64_t tile) {
-            const int64_t c_first = owner(tile * p.spt, p.units, p.ctas);
-            const int64_t c_last = owner((tile + 1) * p.spt - 1, p.units, p.ctas);
-            const int64_t col = (tile % p.n_tiles) * kTileN + r;
-            if (c_first == c_last) {
-                if (col < p.n) {
-                    float* o = out_of(p, int(tile / p.n_tiles)) + col;
-                    for (int t = 0; t < kBT; ++t) {
-                        if (t < p.m) apply(o + int64_t(t) * p.ldc, acc[t], p.epilogue);
-                    }
-                }
-            } else {
-                float* part = p.partial +
-                              ((tile * p.max_seg + (int64_t(blockIdx.x) - c_first)) * kBT) * kTileN + r;
-#pragma unroll
-                for (int t = 0; t < kBT; ++t) part[t * kTileN] = acc[t];
-            }
-#pragma unroll
-            for (int t = 0; t < kBT; ++t) acc[t] = 0.f;
-        };
-        // Chunks waiting to be folded, in the order they end: a chunk that ends at
-        // unit e is folded when unit e + 2 has been converted, so that folding (a
-        // wait on the chunk's MMAs) never delays the conversion of the next units.
-        // At most two are pending (one chunk ends per unit at most).
-        struct Pending {
-            int64_t tile;
-            uint32_t unit;
-            int issuer;
-            bool seg_end;
-        };
-        Pending pend[2];
-        int n_pend = 0;
-        auto fold_pending = [&](uint32_t upto) -> bool {
-            while (n_pend > 0 && pend[0].unit + 2 <= upto) {
-                if (!fold(pend[0].issuer)) return false;
-                if (pend[0].seg_end) finish(pend[0].tile);
-                pend[0] = pend[1];
-                --n_pend;
-            }
-            return true;
-        };
-        bool ok = true;
-        int j = 0, len = 0;
-        int64_t tile = u0 / p.spt;
-        int stage = int(u0 % p.spt) - 1;
-        for (uint32_t g = 0; ok && g < nu; ++g) {
-            if (++stage == p.spt) {
-                stage = 0;
-                ++tile;
-            }
-            if (g == 0 || stage == 0) {
-                j = 0;
-                len = min(p.spt - stage, int(nu - g));
-            }
-            const int jj = j++;
-            const bool seg_end = jj + 1 == len;
-            // the same chunk rule as the issuers (issuer g % kIssuers)
-            const bool chunk_last =
-                jj % (kIssuers * kChunk) >= kIssuers * (kChunk - 1) || jj + kIssuers >= len;
-            if (int(g % 2) == grp) {
-                const uint32_t s = g % kStages, ab = g % kABufs;
-                // A buffer ab was last read by the MMAs of unit g - kABufs, whose
-                // completion is that of its stage
-                const uint32_t h = g - uint32_t(kABufs);
-                if (!wait_or_abort(&ctl->full[s], (g / kStages) & 1u, ctl,
-                                   where_code(kWhoConverter + uint32_t(grp), kBarFull, g)) ||
-                    (g >= uint32_t(kABufs) &&
-                     !wait_or_abort(&ctl->empty[h % kStages], (h / kStages) & 1u, ctl,
-                                    where_code(kWhoConverter + uint32_t(grp), kBarEmpty, g)))) {
-                    ok = false;
-                    break;
-                }
-                unsigned char* st = smem + s * kStageBytes;
-                const float* wt = reinterpret_cast<const float*>(st);
-                float hi[kStageK], lo[kStageK];
-#pragma unroll
-                for (int kk = 0; kk < kStageK; ++kk) {
-                    const float x = wt[kk * kTileN + r];
-                    hi[kk] = tc::to_tf32(x);
-                    lo[kk] = x - hi[kk];
-                }
-                tc::fence_after_sync();
-                tc::tmem_st32(tmem + kColA + ab * 64u + lane_off, hi);
-                tc::tmem_st32(tmem + kColA + ab * 64u + 32u + lane_off, lo);
-                float4* xs = reinterpret_cast<float4*>(st + kWBytes);
-                float4* xl = reinterpret_cast<float4*>(st + kWBytes + kXBytes);
-#pragma unroll
-                for (int i = r; i < int(kXBytes / 16); i += kGroupThreads) split4(xs[i], xl[i]);
-                tc::tmem_st_wait();
-                tc::fence_async_smem();
-                tc::fence_before_sync();
-                mbar_arrive(&ctl->conv[s]);
-            }
-            if (grp != 0) continue;
-            if (!fold_pending(g)) {
-                ok = false;
+    } else if (warp < 8) {
+        // ------------------------------------------------------------ converters
+        const int grp = warp / 4, quarter = warp % 4;
+        const int r = tid % kGroupThreads;
+        for (uint32_t g = uint32_t(grp); g < nu; g += 2) {
+            const uint32_t s = g % kStages;
+            // the stage's previous MMAs (which read this A buffer) completed
+            // before its copies were issued; the wait on `empty` states it
+            if (!wait_warp(&ctl->full[s], (g / kStages) & 1u, ctl,
+                           where_code(kWhoConverter + uint32_t(grp), kBarFull, g)) ||
+                (g >= uint32_t(kStages) &&
+                 !wait_warp(&ctl->empty[s], ((g / kStages) - 1) & 1u, ctl,
+                            where_code(kWhoConverter + uint32_t(grp), kBarEmpty, g)))) {
                 break;
             }
-            if (chunk_last) pend[n_pend++] = Pending{tile, g, int(g % kIssuers), seg_end};
+            unsigned char* st = smem + s * kStageBytes;
+            const float4* w = reinterpret_cast<const float4*>(st);
+            float4* wl = reinterpret_cast<float4*>(st + kWBytes);
+#pragma unroll
+            for (int i = 0; i < int(kWBytes / 16) / kGroupThreads; ++i) {
+                const float4 v = w[r + i * kGroupThreads];
+                wl[r + i * kGroupThreads] =
+                    make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
+            }
+            if (quarter < 2) {
+                // row `lane` of the X tile (128-byte swizzle: chunk c of row t at
+                // position c ^ (t % 8)) into TMEM lane 32 quarter + lane
+                const float4* xr = reinterpret_cast<const float4*>(st + 2 * kWBytes) + lane * 8;
+                float v[kStageK];
+#pragma unroll
+                for (int c = 0; c < kStageK / 4; ++c) {
+                    float4 x = xr[c ^ (lane & 7)];
+                    if (quarter == 1) {
+                        x = make_float4(lo_part(x.x), lo_part(x.y), lo_part(x.z), lo_part(x.w));
+                    }
+                    v[4 * c] = x.x;
+                    v[4 * c + 1] = x.y;
+                    v[4 * c + 2] = x.z;
+                    v[4 * c + 3] = x.w;
+                }
+                tc::fence_after_sync();
+                tc::tmem_st32(tmem + kColA + s * uint32_t(kStageK) + (uint32_t(quarter * 32) << 16), v);
+                tc::tmem_st_wait();
+            }
+            tc::fence_async_smem();
+            tc::fence_before_sync();
+            mbar_arrive(&ctl->conv[s]);
         }
-        if (grp == 0 && ok) fold_pending(nu + 2);
+    } else {
+        // ------------------------------------------------- accumulation, epilogue
+        // warps 8, 12: X_hi rows (TMEM lanes 0-31); 9, 13: X_lo rows (32-63);
+        // 8, 9 columns 0-63 of the tile, 12, 13 columns 64-127
+        const bool lo_rows = (warp % 4) == 1;
+        const int half = warp >= 12 ? 1 : 0;
+        const uint32_t lane_off = uint32_t((warp % 4) * 32) << 16;
+        float* scratch = reinterpret_cast<float*>(smem + kOffScratch + half * kScratchBytes);
+        float acc[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+        uint32_t q = 0, e = 0;  // chunks folded, segments finished
+        UnitWalk walk(u0, p.spt);
+        for (uint32_t g = 0; g < nu; ++g) {
+            const int jj = walk.next(g, nu, p.spt);
+            if (!walk.chunk_last(jj)) continue;
+            const uint32_t buf = q & 1u;
+            if (!wait_warp(&ctl->d_full[buf], (q >> 1) & 1u, ctl,
+                           where_code(kWhoFolder, kBarDFull, q))) {
+                break;
+            }
+            tc::fence_after_sync();
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float v[32];
+                tc::tmem_ld32(tmem + kColD + buf * uint32_t(kTileN) + uint32_t(half * 64 + c * 32) +
+                                  lane_off,
+                              v);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[c * 32 + i] += v[i];
+            }
+            tc::fence_before_sync();
+            mbar_arrive(&ctl->d_free[buf]);
+            ++q;
+            if (!walk.seg_end(jj)) continue;
+            // the tile's segment is complete: the X_lo rows' sums join the X_hi rows'
+            if (lo_rows) {
+                if (e >= 1 && !wait_warp(&ctl->comb_free[half], (e - 1) & 1u, ctl,
+                                         where_code(kWhoFolder, kBarComb, e))) {
+                    break;
+                }
+#pragma unroll
+                for (int i = 0; i < 64; ++i) scratch[lane * kScratchStride + i] = acc[i];
+                mbar_arrive(&ctl->comb_full[half]);
+            } else {
+                if (!wait_warp(&ctl->comb_full[half], e & 1u, ctl,
+                               where_code(kWhoFolder, kBarComb, e))) {
+                    break;
+                }
+#pragma unroll
+                for (int i = 0; i < 64; ++i) acc[i] += scratch[lane * kScratchStride + i];
+                mbar_arrive(&ctl->comb_free[half]);
+                const int64_t tile = walk.tile;
+                const int64_t c_first = owner(tile * p.spt, p.units, p.ctas);
+                const int64_t c_last = owner((tile + 1) * p.spt - 1, p.units, p.ctas);
+                const int64_t col0 = (tile % p.n_tiles) * kTileN + half * 64;
+                if (lane < p.m) {
+                    if (c_first == c_last) {
+                        float* o = out_of(p, int(tile / p.n_tiles)) + int64_t(lane) * p.ldc + col0;
+#pragma unroll
+                        for (int i = 0; i < 64; ++i) {
+                            if (col0 + i < p.n) apply(o + i, acc[i], p.epilogue);
+                        }
+                    } else {
+                        float4* part = reinterpret_cast<float4*>(
+                            p.partial +
+                            ((tile * p.max_seg + (int64_t(blockIdx.x) - c_first)) * kBT + lane) *
+                                kTileN +
+                            half * 64);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            part[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2],
+                                                  acc[4 * i + 3]);
+                        }
+                    }
+                }
+            }
+            ++e;
+#pragma unroll
+            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -489,19 +511,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // W_b [k, n] (row stride ldw, matrix stride wbs floats) as {n, k, batch} in
-// boxes of 128 columns x 32 rows, no swizzle; X [m, k] (row stride lda) as
-// {k, m} in boxes of 32 columns x 32 rows, 128-byte swizzle. Reads past the
-// ends are zero.
+// boxes of 32 columns x 32 rows, 128-byte swizzle with 32-byte granules (the
+// shared-memory layout of an MN-major tf32 operand); X [m, k] (row stride
+// lda) as {k, m} in boxes of 32 columns x 32 rows, 128-byte swizzle. Reads
+// past the ends are zero.
 bool make_maps(CUtensorMap* wmap, CUtensorMap* xmap, const float* w, int64_t ldw, int64_t wbs,
                int64_t n, int64_t k, int32_t batch, const float* x, int64_t lda, int64_t m) {
     auto fn = encode_fn();
     if (fn == nullptr) return false;
     const cuuint64_t wdims[3] = {cuuint64_t(n), cuuint64_t(k), cuuint64_t(batch)};
     const cuuint64_t wstr[2] = {cuuint64_t(ldw) * 4, cuuint64_t(wbs) * 4};
-    const cuuint32_t wbox[3] = {uint32_t(kTileN), uint32_t(kStageK), 1};
+    const cuuint32_t wbox[3] = {32u, uint32_t(kStageK), 1};
     const cuuint32_t e3[3] = {1, 1, 1};
     if (fn(wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(w), wdims, wstr, wbox, e3,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
         return false;
     }

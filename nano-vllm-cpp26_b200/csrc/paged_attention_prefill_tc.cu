@@ -15,19 +15,20 @@
 // instead of 8, so the S tile is 64 keys wide: a 64-key tile takes 24 S MMAs
 // (N = 64) and 12 O MMAs (N = 128).
 //
-// One CTA per SM (persistent), 9 warps:
+// One CTA per SM (persistent), 12 warps:
 //   warps 0-3  softmax / epilogue: thread t owns query row t of a 128-row tile
 //              and TMEM lane t. Per key tile it reads its row of S from TMEM,
 //              applies the causal mask, updates the running maximum and sum,
 //              rescales its row of O in TMEM when its reference maximum moved
 //              (rarely: see kRescaleMargin), and stores P as two bf16 terms into
 //              its TMEM lane, in one of two P buffers (the A operand of P.V).
-//   warp 4     producer: the warp waits, lane 0 issues the TMA gathers of the K
-//              and V tiles (4 physical blocks x 4 swizzle atoms per tensor) into
-//              a 3-stage ring and all tcgen05.mma: S(t+1) = Q K(t+1)^T is queued
-//              while the softmax works on S(t); O(t) += P(t) V(t) once P(t) is in
-//              TMEM.
-//   warps 5-8  converters: turn each landed fp32 K tile, then V tile, in place,
+//   warp 4     MMAs: lane 0 issues every tcgen05.mma and commit: S(t+1) = Q K(t+1)^T
+//              is queued while the softmax works on S(t); O(t) += P(t) V(t) once
+//              P(t) is in TMEM.
+//   warp 5     loader: the TMA gathers of the K and V tiles into a 3-stage ring,
+//              lanes 0-3 one physical block each (4 swizzle atoms per tensor),
+//              up to three tiles ahead of the MMAs.
+//   warps 6-11 converters: turn each landed fp32 K tile, then V tile, in place,
 //              into its two bf16 terms, zeroing the V rows of keys past the
 //              visible ones; S waits only for K's terms, O for V's.
 // Shared memory per stage (64 keys): K as landed, fp32 in four 128-byte
@@ -63,9 +64,11 @@ constexpr int kKT = 64;   // keys per tile
 constexpr int kHD = 128;
 constexpr int kStages = 3;
 constexpr int kSoftmaxThreads = 128;  // warps 0-3
-constexpr int kProducerWarp = 4;
-constexpr int kConvThreads = 128;     // warps 5-8
-constexpr int kThreads = kSoftmaxThreads + 32 + kConvThreads;
+constexpr int kMmaWarp = 4;
+constexpr int kLoaderWarp = 5;
+constexpr int kConvWarp0 = 6;
+constexpr int kConvThreads = 192;     // warps 6-11
+constexpr int kThreads = kSoftmaxThreads + 64 + kConvThreads;
 
 // TMEM columns: S[0] 0..63, S[1] 64..127, P[b] at 128 + 64 b (term 0 then
 // term 1, 32 columns each), O 256..383, Q term 0 384..447, term 1 448..511
@@ -94,7 +97,6 @@ __host__ __device__ constexpr uint32_t f32_atom_offset(int a) {
 }
 static_assert(kF32Atom == kB16Atom && kTermBytes == 2 * kF32Atom, "atom pairs hold their terms");
 constexpr int kConvUnits = (kKT / 2) * (kHD / 64);  // per tensor: row pairs x atom pairs
-static_assert(kConvUnits % (kConvThreads / 32) == 0, "converter split");
 
 // Instruction descriptor for kind::f16 with bf16 A and B and fp32
 // accumulation; b_mn: B is MN-major (else K-major).
@@ -111,8 +113,8 @@ constexpr uint32_t kIdescO = bf16_idesc(kQT, kHD, true);
 
 struct Control {
     uint64_t kv_full[kStages];  // TMA landed (transaction count)
-    uint64_t kc_full[kStages];  // converters wrote K's bf16 terms (128 arrivals)
-    uint64_t vc_full[kStages];  // converters wrote V's bf16 terms (128 arrivals)
+    uint64_t kc_full[kStages];  // converters wrote K's bf16 terms (one per converter)
+    uint64_t vc_full[kStages];  // converters wrote V's bf16 terms (one per converter)
     uint64_t st_free[kStages];  // O of the stage's tile complete: its K and V read
     uint64_t s_full[2];
     // Per P buffer b (the tiles n with n % 2 == b), so that neither side can
@@ -231,7 +233,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
         ctl->abort = 0;
     }
     fence_barrier_init();
-    if (warp == kProducerWarp) {
+    if (warp == kMmaWarp) {
         tc::tmem_alloc(&ctl->tmem_base, kTmemCols);
         tc::tmem_relinquish();
     }
@@ -245,9 +247,8 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     const int H = g.num_heads;
     const int total = p.counters->prefill_items * H;
     uint32_t tile_seq = 0;    // key tiles processed by this CTA (ring position)
-    uint32_t next_load = 0;   // producer: ring index of the next K/V load to issue
-    uint32_t next_wait = 0;   // producer: ring index of the next load not known to have landed
-    bool issued_mma = false;
+    uint32_t next_load = 0;   // loader: ring index of the next K/V load to issue
+    bool issued_mma = false;  // MMA warp
 
     for (;;) {
         if (tid == 0) ctl->item = atomicAdd(&p.counters->prefill_next, 1);
@@ -294,60 +295,54 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
         }
         __syncthreads();
 
-        if (warp == kProducerWarp) {
-            // ---------------------------------------------------------------- producer
+        auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+            const bool got = wait_or_abort(bar, parity, ctl);
+            return __all_sync(0xffffffffu, got);
+        };
+        if (warp == kLoaderWarp) {
+            // ------------------------------------------------------------------ loader
+            // Tile t's four blocks go to lanes 0-3, each issuing its block's eight
+            // boxes; the stage is free once O of its earlier tile completed (S
+            // read its K before).
             const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
-            auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-                const bool got = wait_or_abort(bar, parity, ctl);
-                return __all_sync(0xffffffffu, got);
-            };
-            // the stage is free once O of its earlier tile completed (S read
-            // its K before)
-            auto load = [&](uint32_t n, int t) -> bool {
+            for (int t = 0; t < ntiles; ++t) {
+                const uint32_t n = n0 + t;
                 const uint32_t st = stage_of(n);
-                if (n >= uint32_t(kStages) &&
-                    !wait_all(&ctl->st_free[st], stage_parity(n - kStages))) {
-                    return false;
+                if (n >= uint32_t(kStages) && !wait_all(&ctl->st_free[st], stage_parity(n - kStages))) {
+                    break;
                 }
-                if (lane == 0) {
+                const int kbase = t * kKT;
+                const int nblk = (min(kKT, nk - kbase) + 15) / 16;
+                int64_t blk = -1;
+                if (lane < nblk) blk = table[kbase / 16 + lane];
+                const bool valid = lane < nblk && blk >= 0 && blk < g.num_blocks;
+                const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
+                if (lane == 0) mbar_arrive_expect_tx(&ctl->kv_full[st], uint32_t(__popc(vmask)) * 16384u);
+                __syncwarp();
+                if (lane < nblk && !valid) raise_status(kStatusBounds);
+                if (valid) {
                     unsigned char* sK = sKV + st * kStageBytes;
                     unsigned char* sV = sK + kTileBytes;
-                    const int kbase = t * kKT;
-                    const int nvalid = min(kKT, nk - kbase);
-                    const int nblk = (nvalid + 15) / 16;
-                    uint32_t bytes = 0;
-                    for (int j = 0; j < nblk; ++j) {
-                        const int64_t blk = table[kbase / 16 + j];
-                        if (blk >= 0 && blk < g.num_blocks) bytes += 2u * 4u * 2048u;
-                    }
-                    mbar_arrive_expect_tx(&ctl->kv_full[st], bytes);
-                    for (int j = 0; j < nblk; ++j) {
-                        const int64_t blk = table[kbase / 16 + j];
-                        if (blk < 0 || blk >= g.num_blocks) {
-                            raise_status(kStatusBounds);
-                            continue;
-                        }
-                        const int y = int((blk * g.num_layers + p.layer) * 16);
+                    const int y = int((blk * g.num_layers + p.layer) * 16);
 #pragma unroll
-                        for (int a = 0; a < 4; ++a) {
-                            const int x = h * kHD + a * 32;
-                            const uint32_t off = f32_atom_offset(a) + uint32_t(j) * 2048u;
-                            tc::tma_load_2d(sK + off, &kmap, x, y, &ctl->kv_full[st]);
-                            tc::tma_load_2d(sV + off, &vmap, x, y, &ctl->kv_full[st]);
-                        }
+                    for (int a = 0; a < 4; ++a) {
+                        const int x = h * kHD + a * 32;
+                        const uint32_t off = f32_atom_offset(a) + uint32_t(lane) * 2048u;
+                        tc::tma_load_2d(sK + off, &kmap, x, y, &ctl->kv_full[st]);
+                        tc::tma_load_2d(sV + off, &vmap, x, y, &ctl->kv_full[st]);
                     }
                 }
                 __syncwarp();
                 next_load = n + 1;
-                return true;
-            };
+            }
+        } else if (warp == kMmaWarp) {
+            // -------------------------------------------------------------------- MMAs
             // once the converters have split K of tile n:
             // S(n) = Q1 K0^T + Q0 K1^T + Q0 K0^T, 16 dims per MMA; dims 16k..
             // start 32 k bytes into the rows of atom k / 4 (K-major, 8-row
             // groups 1 KiB apart)
             auto issue_s = [&](uint32_t n) -> bool {
                 if (!wait_all(&ctl->kc_full[stage_of(n)], stage_parity(n))) return false;
-                next_wait = n + 1;
                 if (lane == 0) {
                     tc::fence_after_sync();
                     const uint32_t k0 = smem_addr(sKV + stage_of(n) * kStageBytes);
@@ -395,27 +390,16 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 __syncwarp();
                 return true;
             };
-
-            // S(n+1) is queued while the softmax works on S(n); the stage of
-            // tile n-1 is refilled (with tile n+2) once O(n-1) has completed.
-            bool ok = true;
-            for (int t = 0; ok && t < min(ntiles, kStages); ++t) ok = load(n0 + t, t);
-            if (ok) ok = issue_s(n0);
+            // S(n+1) is queued while the softmax works on S(n)
+            bool ok = issue_s(n0);
             for (int t = 0; ok && t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
-                if (t + 1 < ntiles) {
-                    ok = issue_s(n + 1);
-                    if (!ok) break;
-                }
-                if (t >= 1 && t - 1 + kStages < ntiles) {
-                    ok = load(n - 1 + kStages, t - 1 + kStages);
-                    if (!ok) break;
-                }
+                if (t + 1 < ntiles && !issue_s(n + 1)) break;
                 ok = wait_all(&ctl->p_full[n & 1u], (n >> 1) & 1u) && issue_o(n, t == 0);
             }
-        } else if (warp > kProducerWarp) {
+        } else if (warp >= kConvWarp0) {
             // -------------------------------------------------------------- converters
-            const int cw = warp - (kProducerWarp + 1);  // converter warp 0..7
+            const int cw = warp - kConvWarp0;
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
                 // wait outcomes are made warp-uniform, so that no lane is left
@@ -548,10 +532,14 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
 
     // Teardown: on an abort, let this CTA's copies and MMAs finish (bounded)
     // before its shared memory and TMEM are released.
-    if (warp == kProducerWarp && lane == 0) {
-        for (uint32_t n = next_wait; n < next_load; ++n) {
+    // (only the last load of each stage can still be in flight: a stage is
+    // reloaded only after the MMAs that read its previous load completed)
+    if (warp == kLoaderWarp && lane == 0) {
+        for (uint32_t n = next_load > uint32_t(kStages) ? next_load - kStages : 0; n < next_load; ++n) {
             mbar_wait(&ctl->kv_full[stage_of(n)], stage_parity(n), kStatusInPrefillTc);
         }
+    }
+    if (warp == kMmaWarp && lane == 0) {
         if (issued_mma) {
             tc::commit(&ctl->drain);
             mbar_wait(&ctl->drain, 0, kStatusInPrefillTc);
@@ -559,7 +547,7 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == kProducerWarp) {
+    if (warp == kMmaWarp) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, kTmemCols);
     }
