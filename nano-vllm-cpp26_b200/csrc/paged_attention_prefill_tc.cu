@@ -175,31 +175,80 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
     tc::tmem_st32(taddr, f);
 }
 
-// In-place conversion of one landed fp32 tile (64 keys x 128 dims) into its
-// two bf16 terms by one converter warp: unit u = (row pair u / 2, atom pair
-// u % 2); lane l reads 16 bytes of atom 2 p + l / 16, row 2 (u / 2) + (l / 8) % 2,
-// swizzle position l % 8 -- together the 512 bytes the unit's terms then
-// occupy -- and, after the warp has read, writes 8 bytes of each term (each
-// row's 128 bytes of a term written whole: no bank conflicts). Rows >=
-// zero_from become 0.
-__device__ __forceinline__ void convert_unit(unsigned char* tile, int u, int lane, int zero_from) {
-    const int ap = u & 1;
-    const int a = 2 * ap + ((lane >> 4) & 1);
-    const int row = 2 * (u >> 1) + ((lane >> 3) & 1);
-    const int phys = lane & 7;
-    float4 x = *reinterpret_cast<const float4*>(tile + f32_atom_offset(a) + row * 128 + phys * 16);
-    __syncwarp();
-    if (row >= zero_from) x = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int dim = 32 * a + ((phys ^ (row & 7)) << 2);  // the first of the 4 dims
-    uint32_t a0, a1, b0, b1;
-    split2(x.x, x.y, a0, a1);
-    split2(x.z, x.w, b0, b1);
-    // term atom ap, the row, 16-byte chunk (dim % 64) / 8 swizzled by the row,
-    // 8 bytes in when dim % 8 == 4
-    const uint32_t off = uint32_t(ap) * kB16Atom + uint32_t(row) * 128u +
-                         uint32_t(((dim & 63) >> 3) ^ (row & 7)) * 16u + uint32_t(dim & 4) * 2u;
-    *reinterpret_cast<uint2*>(tile + off) = make_uint2(a0, b0);
-    *reinterpret_cast<uint2*>(tile + kTermBytes + off) = make_uint2(a1, b1);
+// 2^x on the MUFU unit (flush-to-zero: weights below 2^-126 of the row's
+// reference maximum become 0, far below the tolerance of this path).
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// In-place conversion of a landed fp32 tile (64 keys x 128 dims) into its two
+// bf16 terms. Unit u = (row pair u / 2, atom pair p = u % 2) is the 512 bytes
+// that rows 2 (u / 2) and 2 (u / 2) + 1 of fp32 atoms 2 p and 2 p + 1 occupy,
+// which are exactly the bytes those rows of term 0 atom p and term 1 atom p
+// go to. Converter warp cw takes the units u = cw + 6 i; lane l reads 16
+// bytes of atom 2 p + (l / 8) % 2, row 2 (u / 2) + l / 16, swizzle position
+// l % 8 (a quarter-warp reads one 128-byte row of one atom), and writes 8
+// bytes of each term (a half-warp writes one term row whole: no bank
+// conflicts). The offsets depend only on the warp, the lane and i, so they
+// are computed once per work item.
+constexpr int kConvWarps = kConvThreads / 32;
+constexpr int kConvMax = (kConvUnits + kConvWarps - 1) / kConvWarps;  // units per warp, at most
+constexpr int kConvBatch = 4;  // units read before the warp writes
+
+struct ConvPlan {
+    uint32_t rd[kConvMax];   // read offset in the landed tile
+    uint32_t wr[kConvMax];   // term-0 write offset (term 1: + kTermBytes)
+    int32_t row[kConvMax];   // key row of the lane's data
+    int32_t n;               // units of this warp
+};
+
+__device__ __forceinline__ void make_conv_plan(ConvPlan& cp, int cw, int lane) {
+    cp.n = (kConvUnits - cw + kConvWarps - 1) / kConvWarps;
+#pragma unroll
+    for (int i = 0; i < kConvMax; ++i) {
+        const int u = cw + kConvWarps * i;
+        const int ap = u & 1;
+        const int a = 2 * ap + ((lane >> 3) & 1);
+        const int row = 2 * (u >> 1) + (lane >> 4);
+        const int phys = lane & 7;
+        const int dim = 32 * a + ((phys ^ (row & 7)) << 2);  // the first of the lane's 4 dims
+        cp.rd[i] = f32_atom_offset(a) + uint32_t(row) * 128u + uint32_t(phys) * 16u;
+        // term atom ap, the row, 16-byte chunk (dim % 64) / 8 swizzled by the
+        // row, 8 bytes in when dim % 8 == 4
+        cp.wr[i] = uint32_t(ap) * kB16Atom + uint32_t(row) * 128u +
+                   uint32_t(((dim & 63) >> 3) ^ (row & 7)) * 16u + uint32_t(dim & 4) * 2u;
+        cp.row[i] = row;
+    }
+}
+
+// Converts this warp's units of one tile; rows >= zero_from become 0 (V).
+template <bool kZero>
+__device__ __forceinline__ void convert_tile(unsigned char* tile, const ConvPlan& cp, int zero_from) {
+#pragma unroll
+    for (int i0 = 0; i0 < kConvMax; i0 += kConvBatch) {
+        float4 x[kConvBatch];
+#pragma unroll
+        for (int b = 0; b < kConvBatch; ++b) {
+            if (i0 + b < kConvMax && i0 + b < cp.n) {
+                x[b] = *reinterpret_cast<const float4*>(tile + cp.rd[i0 + b]);
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int b = 0; b < kConvBatch; ++b) {
+            const int i = i0 + b;
+            if (i < kConvMax && i < cp.n) {
+                if (kZero && cp.row[i] >= zero_from) x[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+                uint32_t a0, a1, b0, b1;
+                split2(x[b].x, x[b].y, a0, a1);
+                split2(x[b].z, x[b].w, b0, b1);
+                *reinterpret_cast<uint2*>(tile + cp.wr[i]) = make_uint2(a0, b0);
+                *reinterpret_cast<uint2*>(tile + kTermBytes + cp.wr[i]) = make_uint2(a1, b1);
+            }
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -271,8 +320,9 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
         const uint32_t n0 = tile_seq;
 
         if (tid < kSoftmaxThreads) {
-            // Q tile -> TMEM as the A operand of S = Q K^T: term 0 in columns
-            // 384.., term 1 in 448.., one pair of consecutive dims per column
+            // Q tile, times scale * log2 e (so that S holds log2-domain scores),
+            // -> TMEM as the A operand of S = Q K^T: term 0 in columns 384..,
+            // term 1 in 448.., one pair of consecutive dims per column
             const int row = tid;
             const uint32_t lane_off = uint32_t(warp * 32) << 16;
             const float4* qrow = reinterpret_cast<const float4*>(
@@ -284,6 +334,8 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 for (int i = 0; i < 16; ++i) {
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (row < nrows) v = __ldg(qrow + c * 16 + i);
+                    const float qs = p.qk_scale_log2;
+                    v = make_float4(v.x * qs, v.y * qs, v.z * qs, v.w * qs);
                     split2(v.x, v.y, t0[2 * i], t1[2 * i]);
                     split2(v.z, v.w, t0[2 * i + 1], t1[2 * i + 1]);
                 }
@@ -399,7 +451,10 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             }
         } else if (warp >= kConvWarp0) {
             // -------------------------------------------------------------- converters
-            const int cw = warp - kConvWarp0;
+            // (the plan is rebuilt per item so that its registers are not live
+            // in the other roles' code)
+            ConvPlan cp;
+            make_conv_plan(cp, warp - kConvWarp0, lane);
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
                 // wait outcomes are made warp-uniform, so that no lane is left
@@ -411,17 +466,12 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 unsigned char* stage = sKV + stage_of(n) * kStageBytes;
                 // K rows past the visible keys are masked by the softmax; V's
                 // are zeroed, for their zero weights to cancel
-                const int nvk = nk - t * kKT;
-#pragma unroll 1
-                for (int part = 0; part < 2; ++part) {  // K, then V
-                    unsigned char* tile = stage + part * kTileBytes;
-#pragma unroll 4
-                    for (int u = cw; u < kConvUnits; u += kConvThreads / 32) {
-                        convert_unit(tile, u, lane, part == 0 ? kKT : nvk);
-                    }
-                    tc::fence_async_smem();
-                    mbar_arrive(part == 0 ? &ctl->kc_full[stage_of(n)] : &ctl->vc_full[stage_of(n)]);
-                }
+                convert_tile<false>(stage, cp, kKT);
+                tc::fence_async_smem();
+                mbar_arrive(&ctl->kc_full[stage_of(n)]);
+                convert_tile<true>(stage + kTileBytes, cp, nk - t * kKT);
+                tc::fence_async_smem();
+                mbar_arrive(&ctl->vc_full[stage_of(n)]);
             }
         } else {
             // ------------------------------------------------------------ softmax warps
@@ -443,15 +493,21 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 tc::tmem_ld32(tmem + (n & 1u) * kKT + 32u + lane_off, sc + 32);
                 tc::tmem_ld_wait();
                 const int kbase = t * kKT;
-                float cm = -INFINITY;
+                // only tiles that reach past the tile's first query position
+                // need the causal mask (keys past nk are past every row's too)
+                if (kbase + kKT - 1 > first_pos + r0) {
 #pragma unroll
-                for (int j = 0; j < kKT; ++j) {
-                    const int kp = kbase + j;
-                    sc[j] = (kp <= qpos && kp < nk) ? sc[j] * p.qk_scale_log2 : -INFINITY;
-                    cm = fmaxf(cm, sc[j]);
+                    for (int j = 0; j < kKT; ++j) {
+                        const int kp = kbase + j;
+                        sc[j] = (kp <= qpos && kp < nk) ? sc[j] : -INFINITY;
+                    }
                 }
+                float mx[4] = {sc[0], sc[1], sc[2], sc[3]};
+#pragma unroll
+                for (int j = 4; j < kKT; ++j) mx[j & 3] = fmaxf(mx[j & 3], sc[j]);
+                const float cm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
                 const float m_new = cm > m_run + kRescaleMargin ? cm : m_run;
-                const float alpha = exp2f(m_run - m_new);
+                const float alpha = ex2_ftz(m_run - m_new);
                 l_run *= alpha;
                 m_run = m_new;
                 // the P buffer is free once O of the tile two back completed
@@ -485,19 +541,21 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 // P = exp2(s - m) as two bf16 terms, 32 keys (16 columns of each
                 // term) at a time
                 const uint32_t pb = tmem + kColP + (n & 1u) * 64u + lane_off;
+                float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     uint32_t p0[16], p1[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const float a = exp2f(sc[32 * half + 2 * j] - m_new);
-                        const float b = exp2f(sc[32 * half + 2 * j + 1] - m_new);
-                        l_run += a + b;
+                        const float a = ex2_ftz(sc[32 * half + 2 * j] - m_new);
+                        const float b = ex2_ftz(sc[32 * half + 2 * j + 1] - m_new);
+                        ls[j & 3] += a + b;
                         split2(a, b, p0[j], p1[j]);
                     }
                     tc::tmem_st16(pb + 16u * half, p0);
                     tc::tmem_st16(pb + 32u + 16u * half, p1);
                 }
+                l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
                 tc::tmem_st_wait();
                 tc::fence_before_sync();
                 mbar_arrive(&ctl->p_full[n & 1u]);
