@@ -54,6 +54,7 @@ struct AttnParams {
     int32_t max_splits;
     int32_t split_tokens;     // P: positions per decode item
     int32_t prefill_tile;     // QT: query rows per prefill item
+    int32_t beside_prefill;   // decode launched beside a prefill (no wait for it)
     // Head split (num_outs > 0): every decode row leaves through the merge
     // kernel, which stores it at column out_col of row token in each of the
     // num_outs output buffers (this rank's and its peers', row stride

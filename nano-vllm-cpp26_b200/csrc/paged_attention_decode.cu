@@ -140,6 +140,11 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const AttnParams p) 
     }
     fence_barrier_init();
     __syncwarp();
+    pdl_release();
+    // the work list, the arena rows and the queries come from the kernels
+    // before (beside a prefill, which writes none of them, the plan completed
+    // before the prefill started)
+    if (!p.beside_prefill) pdl_wait();
 
     const uint64_t pol = l2_evict_first();
     const ArenaGeom& g = p.g;
@@ -428,6 +433,8 @@ __global__ void __launch_bounds__(256) merge_kernel(const AttnParams p, int wpr)
     constexpr int PER_LANE = HD / 32;
     __shared__ float sm_m[8], sm_l[8];
     __shared__ float sm_o[8][HD];
+    pdl_release();
+    pdl_wait();  // the partials of the decode kernel
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int H = p.g.num_heads;
@@ -551,20 +558,24 @@ __global__ void signal_kernel(AttnParams p) {
 }
 
 // Head split: the call completes once every rank has signalled this rank.
+// It may start while this rank's merge still runs (the flag only reaches the
+// target once that merge has signalled too), and completes after it.
 __global__ void flag_wait_kernel(const uint32_t* flag, uint32_t target) {
-    if (threadIdx.x != 0) return;
-    const uint64_t t0 = global_ns();
-    for (;;) {
-        uint32_t v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-        if (int32_t(v - target) >= 0) return;
-        if (global_ns() - t0 > kWaitLimitNs) {
-            record_flag_timeout(kStatusInHeadSplit, target, v);
-            raise_status(kStatusTimeout | kStatusInHeadSplit);
-            return;
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = global_ns();
+        for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+            if (int32_t(v - target) >= 0) break;
+            if (global_ns() - t0 > kWaitLimitNs) {
+                record_flag_timeout(kStatusInHeadSplit, target, v);
+                raise_status(kStatusTimeout | kStatusInHeadSplit);
+                break;
+            }
+            __nanosleep(200);
         }
-        __nanosleep(200);
     }
+    pdl_wait();
 }
 
 // Builds the decode and prefill work lists from the batch metadata (one CTA).
@@ -599,6 +610,8 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int& t
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const AttnParams p) {
     __shared__ int warp_tot[32];
+    pdl_release();
+    pdl_wait();  // the metadata may come from the kernel before
     int run_d = 0, run_p = 0, run_s = 0;
     const int B = p.g.block_size;
     for (int base = 0; base < p.num_seqs; base += kPlanThreads) {
@@ -678,28 +691,16 @@ cudaError_t launch_decode_t(const AttnParams& p, cudaStream_t stream, bool overl
         const int64_t warps = (units + rounds - 1) / rounds;
         grid = int(std::clamp<int64_t>((warps + NW - 1) / NW, 1, grid));
     }
-    if (overlap_previous) {
-        cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(unsigned(grid));
-        cfg.blockDim = dim3(NW * 32);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, decode_kernel<HD, NW, NS, kB16>, p);
-    } else {
-        decode_kernel<HD, NW, NS, kB16><<<grid, NW * 32, smem, stream>>>(p);
-        e = cudaGetLastError();
-    }
+    AttnParams q = p;
+    q.beside_prefill = overlap_previous ? 1 : 0;
+    e = launch_programmatic(decode_kernel<HD, NW, NS, kB16>, dim3(unsigned(grid)), dim3(NW * 32),
+                            smem, stream, q);
     if (e != cudaSuccess) return e;
     const int rows = p.num_seqs * p.g.num_heads;
     const int wpr = merge_warps_per_row(p.max_splits);
     const int rows_per_cta = 8 / wpr;
-    merge_kernel<HD><<<(rows + rows_per_cta - 1) / rows_per_cta, 256, 0, stream>>>(p, wpr);
-    return cudaGetLastError();
+    return launch_programmatic(merge_kernel<HD>, dim3(unsigned((rows + rows_per_cta - 1) / rows_per_cta)),
+                               dim3(256), 0, stream, q, wpr);
 }
 
 }  // namespace
@@ -720,13 +721,11 @@ cudaError_t launch_signal(uint32_t* const* flags, int n, cudaStream_t stream) {
 }
 
 cudaError_t launch_flag_wait(const uint32_t* flag, uint32_t target, cudaStream_t stream) {
-    flag_wait_kernel<<<1, 32, 0, stream>>>(flag, target);
-    return cudaGetLastError();
+    return launch_programmatic(flag_wait_kernel, dim3(1), dim3(32), 0, stream, flag, target);
 }
 
 cudaError_t launch_plan(const AttnParams& p, cudaStream_t stream) {
-    plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
-    return cudaGetLastError();
+    return launch_programmatic(plan_kernel, dim3(1), dim3(kPlanThreads), 0, stream, p);
 }
 
 // Warps per CTA and stages per warp of the decode kernel (build-time tunables).

@@ -18,6 +18,8 @@ reshape_and_cache_kernel(const float* __restrict__ key, const float* __restrict_
                          float* __restrict__ k_arena, float* __restrict__ v_arena,
                          const int32_t* __restrict__ slot_mapping, int32_t layer,
                          ArenaGeom g) {
+    pdl_release();
+    pdl_wait();  // the rows and the slot mapping may come from the kernel before
     const int64_t t = blockIdx.x;
     const int32_t slot = slot_mapping[t];
     if (slot < 0) return;
@@ -57,14 +59,9 @@ cudaError_t launch_reshape_and_cache(const float* key, const float* value, float
     if (num_tokens <= 0) return cudaSuccess;
     const dim3 grid(static_cast<unsigned>(num_tokens));
     const int threads = g.row >= 1024 ? 256 : 128;
-    if (vec4) {
-        reshape_and_cache_kernel<true><<<grid, threads, 0, stream>>>(key, value, k_arena, v_arena,
-                                                                     slot_mapping, layer, g);
-    } else {
-        reshape_and_cache_kernel<false><<<grid, threads, 0, stream>>>(key, value, k_arena, v_arena,
-                                                                      slot_mapping, layer, g);
-    }
-    return cudaGetLastError();
+    return launch_programmatic(vec4 ? reshape_and_cache_kernel<true> : reshape_and_cache_kernel<false>,
+                               grid, dim3(threads), 0, stream, key, value, k_arena, v_arena,
+                               slot_mapping, layer, g);
 }
 
 }  // namespace nvllm
