@@ -69,6 +69,7 @@ constexpr int kLoaderWarp = 5;
 constexpr int kConvWarp0 = 6;
 constexpr int kConvThreads = 192;     // warps 6-11
 constexpr int kThreads = kSoftmaxThreads + 64 + kConvThreads;
+constexpr int kItemReaders = kThreads / 32 - 1;  // every warp but the loader
 
 // TMEM columns: S[0] 0..63, S[1] 64..127, P[b] at 128 + 64 b (term 0 then
 // term 1, 32 columns each), O 256..383, Q term 0 384..447, term 1 448..511
@@ -123,8 +124,14 @@ struct Control {
     uint64_t p_full[2];
     uint64_t p_free[2];
     uint64_t drain;
+    // work items pass through a two-slot queue: item_full[i] the loader wrote
+    // items[i]; item_free[i] every other warp read it (kItemReaders arrivals);
+    // q_full the query tile of the current item in TMEM (128 arrivals)
+    uint64_t item_full[2];
+    uint64_t item_free[2];
+    uint64_t q_full;
     uint32_t tmem_base;
-    int32_t item;
+    int32_t items[2];
     int32_t abort;
 };
 static_assert(sizeof(Control) <= 256, "control block");
@@ -279,6 +286,11 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             mbar_init(&ctl->p_free[i], 1);
         }
         mbar_init(&ctl->drain, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&ctl->item_full[i], 1);
+            mbar_init(&ctl->item_free[i], kItemReaders);
+        }
+        mbar_init(&ctl->q_full, kSoftmaxThreads);
         ctl->abort = 0;
     }
     fence_barrier_init();
@@ -299,13 +311,48 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
     uint32_t next_load = 0;   // loader: ring index of the next K/V load to issue
     bool issued_mma = false;  // MMA warp
 
-    for (;;) {
-        if (tid == 0) ctl->item = atomicAdd(&p.counters->prefill_next, 1);
-        __syncthreads();
-        const int it = ctl->item;
-        const bool stop = it >= total || *reinterpret_cast<volatile int32_t*>(&ctl->abort);
-        __syncthreads();
-        if (stop) break;
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+        const bool got = wait_or_abort(bar, parity, ctl);
+        return __all_sync(0xffffffffu, got);
+    };
+    // Work items: the loader's lane 0 takes each from the global cursor (the
+    // loader needs an item first and runs ahead of the rest by up to the
+    // ring's depth) and publishes it in the queue slot j % 2; every other warp
+    // reads the items in the same order and frees the slot. -1 ends the loop.
+    // No role waits for the others at an item boundary: the loader and the
+    // converters go on into the next item's tiles while the softmax warps
+    // finish the last one.
+    auto publish = [&](uint32_t j, int it) -> bool {
+        const uint32_t slot = j & 1u;
+        if (j >= 2 && !wait_or_abort(&ctl->item_free[slot], ((j >> 1) - 1) & 1u, ctl)) return false;
+        ctl->items[slot] = it;
+        mbar_arrive(&ctl->item_full[slot]);
+        return true;
+    };
+    auto take = [&](uint32_t j) -> int {
+        const uint32_t slot = j & 1u;
+        if (!wait_all(&ctl->item_full[slot], (j >> 1) & 1u)) return -1;
+        const int it = *reinterpret_cast<volatile int32_t*>(&ctl->items[slot]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->item_free[slot]);
+        return it;
+    };
+
+    for (uint32_t j = 0;; ++j) {
+        int it = -1;
+        if (warp == kLoaderWarp) {
+            if (lane == 0) {
+                if (!*reinterpret_cast<volatile int32_t*>(&ctl->abort)) {
+                    it = atomicAdd(&p.counters->prefill_next, 1);
+                    if (it >= total) it = -1;
+                }
+                if (!publish(j, it)) it = -1;
+            }
+            it = __shfl_sync(0xffffffffu, it, 0);
+        } else {
+            it = take(j);
+        }
+        if (it < 0 || *reinterpret_cast<volatile int32_t*>(&ctl->abort)) break;
 
         const WorkItem wi = p.prefill_items[it / H];
         const int h = it % H;
@@ -319,38 +366,6 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
         const int ntiles = (nk + kKT - 1) / kKT;
         const uint32_t n0 = tile_seq;
 
-        if (tid < kSoftmaxThreads) {
-            // Q tile, times scale * log2 e (so that S holds log2-domain scores),
-            // -> TMEM as the A operand of S = Q K^T: term 0 in columns 384..,
-            // term 1 in 448.., one pair of consecutive dims per column
-            const int row = tid;
-            const uint32_t lane_off = uint32_t(warp * 32) << 16;
-            const float4* qrow = reinterpret_cast<const float4*>(
-                p.q + int64_t(q0 + r0 + row) * g.row + int64_t(h) * kHD);
-#pragma unroll 1
-            for (int c = 0; c < 2; ++c) {  // 64 dims -> 32 columns of each term
-                uint32_t t0[32], t1[32];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (row < nrows) v = __ldg(qrow + c * 16 + i);
-                    const float qs = p.qk_scale_log2;
-                    v = make_float4(v.x * qs, v.y * qs, v.z * qs, v.w * qs);
-                    split2(v.x, v.y, t0[2 * i], t1[2 * i]);
-                    split2(v.z, v.w, t0[2 * i + 1], t1[2 * i + 1]);
-                }
-                tmem_st32u(tmem + kColQ + c * 32u + lane_off, t0);
-                tmem_st32u(tmem + kColQ + 64u + c * 32u + lane_off, t1);
-            }
-            tc::tmem_st_wait();
-            tc::fence_before_sync();
-        }
-        __syncthreads();
-
-        auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-            const bool got = wait_or_abort(bar, parity, ctl);
-            return __all_sync(0xffffffffu, got);
-        };
         if (warp == kLoaderWarp) {
             // ------------------------------------------------------------------ loader
             // Tile t's four blocks go to lanes 0-3, each issuing its block's eight
@@ -442,8 +457,9 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
                 __syncwarp();
                 return true;
             };
-            // S(n+1) is queued while the softmax works on S(n)
-            bool ok = issue_s(n0);
+            // S(n+1) is queued while the softmax works on S(n); the first S of
+            // an item waits for its Q tile in TMEM
+            bool ok = wait_all(&ctl->q_full, j & 1u) && issue_s(n0);
             for (int t = 0; ok && t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
                 if (t + 1 < ntiles && !issue_s(n + 1)) break;
@@ -478,6 +494,33 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
             const int row = tid;  // query row and TMEM lane
             const int qpos = first_pos + r0 + row;
             const uint32_t lane_off = uint32_t(warp * 32) << 16;
+            {
+                // Q tile, times scale * log2 e (so that S holds log2-domain
+                // scores), -> TMEM as the A operand of S = Q K^T: term 0 in
+                // columns 384.., term 1 in 448.., one pair of consecutive dims
+                // per column. The previous item's S MMAs all completed (this
+                // warp waited for its last S).
+                const float4* qrow = reinterpret_cast<const float4*>(
+                    p.q + int64_t(q0 + r0 + row) * g.row + int64_t(h) * kHD);
+#pragma unroll 1
+                for (int c = 0; c < 2; ++c) {  // 64 dims -> 32 columns of each term
+                    uint32_t t0[32], t1[32];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (row < nrows) v = __ldg(qrow + c * 16 + i);
+                        const float qs = p.qk_scale_log2;
+                        v = make_float4(v.x * qs, v.y * qs, v.z * qs, v.w * qs);
+                        split2(v.x, v.y, t0[2 * i], t1[2 * i]);
+                        split2(v.z, v.w, t0[2 * i + 1], t1[2 * i + 1]);
+                    }
+                    tmem_st32u(tmem + kColQ + c * 32u + lane_off, t0);
+                    tmem_st32u(tmem + kColQ + 64u + c * 32u + lane_off, t1);
+                }
+                tc::tmem_st_wait();
+                tc::fence_before_sync();
+                mbar_arrive(&ctl->q_full);
+            }
             float m_run = -INFINITY, l_run = 0.f;
             bool ok = true;
             for (int t = 0; t < ntiles; ++t) {
