@@ -6,36 +6,34 @@
 //
 // At m <= 32 the product is a stream of W (8 KB of weights per 128 x 32 x 32
 // block of MACs), so W crosses HBM once, unsplit, and everything else happens
-// on chip. The MMA computes D[128 lanes, 128 columns of W] = A . W_tile with W
-// read straight from the TMA-landed tile as an MN-major operand (the layout W
-// has in memory: a row of W is 128 contiguous output features), so W is never
-// transposed or moved on chip. Every product is fp32-quality through tf32
-// parts: the tensor core reads a tf32 operand as the top 19 bits of its fp32
-// container, so hi = x as stored and lo = x - (x with its low 13 bits
-// cleared), exact. A lives in TMEM: lanes 0-31 hold the token rows' X_hi,
-// lanes 32-63 their X_lo, so one MMA gives X_hi W and X_lo W in the two lane
-// halves, and W_lo, written beside W by the converters, gives X_hi W_lo and
-// X_lo W_lo: two N = 128 MMAs per 8 of K. Lane t and lane 32 + t are summed
-// in fp32 at the end.
+// on chip. The MMA computes D[128 output features (TMEM lanes), 64 columns] =
+// W_tile^T . [X_hi | X_lo]^T with W read straight from its TMA tile as an
+// MN-major A operand (a row of W is 128 contiguous output features: the
+// layout it has in memory, so W is never transposed or moved on chip), and
+// X's 32 token rows followed by their lo parts as one K-major B operand of 64
+// rows. Every product is fp32-quality through tf32 parts: the tensor core
+// reads a tf32 operand as the top 19 bits of its fp32 container, so hi = x as
+// stored and lo = x - (x with its low 13 bits cleared), exact. Per 8 of K:
+// W [X_hi | X_lo] (N = 64) and W_lo X_hi (N = 32, into the first 32 columns),
+// where W_lo, written beside W by the converters, is an MN-major A operand in
+// the same layout. Column t + 32 (W X_lo) is added to column t at the fold.
 //
-// Per stage (32 rows of K), with 14 warps per CTA (one CTA per SM, all 512
-// TMEM columns):
-//   warp 10, lane 0: the TMA copies into a 5-stage ring (W tile 32 x 128 fp32
+// Per stage (32 rows of K), with 15 warps per CTA (one CTA per SM):
+//   warp 12, lane 0: the TMA copies into a 5-stage ring (W tile 32 x 128 fp32
 //     as four 32-column boxes in the 128-byte swizzle with 32-byte granules,
 //     the layout of an MN-major tf32 operand; X tile 32 rows x 32 fp32,
 //     128-byte swizzle; no multicast);
-//   warp 11, lane 0: the 8 MMAs of a stage into one of two accumulators, and
-//     their commits;
+//   warps 13 and 14, lane 0: the 8 MMAs of a stage and their commits, the
+//     two warps taking alternate accumulation chunks (2 stages each) into
+//     their own pairs of accumulators: a tcgen05.mma takes about as long to
+//     issue as one of these small ones takes to run;
 //   warps 0-7: converters in two groups of four that take alternate stages:
-//     all four write W_lo; warp 4g (TMEM lanes 0-31) stores row `lane` of the
-//     X tile into its lane of the stage's A buffer, warp 4g + 1 (lanes 32-63)
-//     that row's lo part;
-//   warps 8, 9, 12, 13: fold each finished accumulation chunk (4 stages = 128
-//     of K: the tensor core's fp32 accumulation truncates, so long sums stay in
-//     fp32 registers) into registers, 64 columns each of the X_hi rows (8, 12)
-//     or the X_lo rows (9, 13); at the end of a tile's segment the X_lo warps
-//     hand their sums to the X_hi warps through shared memory, which add them
-//     and write the result.
+//     W_lo beside W and X_lo beside X, elementwise in the landed layouts;
+//   warps 8-11: fold each finished accumulation chunk (2 stages = 64 of K:
+//     the tensor core's fp32 accumulation truncates, so long sums stay in
+//     fp32 registers) into registers, thread = output feature (TMEM lane),
+//     32 token sums each, and write the tile's columns at the end of its
+//     segment.
 // Work is split stream-K: the (tile, stage) units of all output tiles are
 // dealt to the persistent CTAs in equal contiguous ranges; a tile that one CTA
 // covers whole is written directly with the epilogue op, the pieces of a
@@ -59,36 +57,34 @@
 namespace nvllm {
 namespace {
 
-constexpr int kTileN = 128;    // output features per tile (MMA N)
-constexpr int kBT = 32;        // token rows: TMEM lanes 0-31 (X_hi), 32-63 (X_lo)
+constexpr int kTileN = 128;    // output features per tile (MMA M, TMEM lanes)
+constexpr int kBT = 32;        // token rows (X_hi: B rows 0-31, X_lo: 32-63)
 constexpr int kStageK = 32;    // K rows per stage
 constexpr int kStages = 5;
-constexpr int kChunk = 4;      // stages per TMEM accumulation chunk
+constexpr int kChunk = 2;      // stages per TMEM accumulation chunk
 constexpr int kGroupThreads = 128;  // one converter group
-constexpr int kProducerWarp = 10;
-constexpr int kIssuerWarp = 11;
-constexpr int kThreads = 14 * 32;   // converters 0-7, folders 8, 9, 12, 13, producer, issuer
+constexpr int kFoldWarp0 = 8;
+constexpr int kProducerWarp = 12;
+constexpr int kIssuerWarp = 13;     // and 14: the two MMA issuers
+constexpr int kIssuers = 2;
+constexpr int kThreads = 15 * 32;   // converters 0-7, folders 8-11, producer, 2 issuers
 constexpr int kFoldThreads = 128;
 constexpr int kMaxBatch = 3;
 constexpr int kMinUnits = 8;   // stages a CTA handles at least
 constexpr uint32_t kWAtom = kStageK * 128;           // 32 K rows x 32 features: 4 KB
 constexpr uint32_t kWBytes = 4 * kWAtom;             // 16 KB
 constexpr uint32_t kXBytes = kBT * kStageK * 4;      // 4 KB
-constexpr uint32_t kStageBytes = 2 * kWBytes + kXBytes;  // W, W_lo, X
-constexpr uint32_t kScratchStride = 65;              // floats per row (no bank conflicts)
-constexpr uint32_t kScratchBytes = kBT * kScratchStride * 4;
-constexpr uint32_t kOffScratch = kStages * kStageBytes;
-constexpr uint32_t kOffCtl = kOffScratch + 2 * kScratchBytes;
+constexpr uint32_t kStageBytes = 2 * kWBytes + 2 * kXBytes;  // W, W_lo, X, X_lo
+constexpr uint32_t kOffCtl = kStages * kStageBytes;
 constexpr uint32_t kSmem = kOffCtl + 512 + 1024;
 static_assert(kSmem <= 227u * 1024u, "shared memory");
-static_assert(kStageBytes % 1024 == 0 && kWBytes % 1024 == 0, "swizzle atoms stay aligned");
-// TMEM: an A buffer per ring slot (32 columns, one tf32 element of K each) and
-// two accumulators of 128 columns
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColA = 0;
-constexpr uint32_t kColD = 256;
-static_assert(kStages * kStageK <= int(kColD) && kColD + 2 * kTileN <= kTmemCols, "TMEM columns");
-constexpr uint32_t kIdesc = tc::tf32_idesc(128, kTileN, false, true);
+static_assert(kStageBytes % 1024 == 0 && kWBytes % 1024 == 0 && kXBytes % 1024 == 0,
+              "swizzle atoms stay aligned");
+// TMEM: two accumulators of 64 columns per issuer
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColsD = 2 * kBT;
+constexpr uint32_t kIdescBoth = tc::tf32_idesc(kTileN, 2 * kBT, true, false);  // W [X_hi | X_lo]
+constexpr uint32_t kIdescHi = tc::tf32_idesc(kTileN, kBT, true, false);        // W_lo X_hi
 
 struct DecodeParams {
     int64_t m, n, k, ldc;
@@ -103,13 +99,11 @@ struct DecodeParams {
 
 struct Control {
     uint64_t full[kStages];    // TMA landed (transaction bytes)
-    uint64_t conv[kStages];    // W_lo written, A in TMEM (kGroupThreads arrivals)
+    uint64_t conv[kStages];    // W_lo and X_lo written (kGroupThreads arrivals)
     uint64_t empty[kStages];   // the stage's MMAs completed
-    uint64_t d_full[2];        // accumulation chunk complete
-    uint64_t d_free[2];        // chunk folded into registers (kFoldThreads arrivals)
-    uint64_t comb_full[2];     // [column half] X_lo sums in scratch (32 arrivals)
-    uint64_t comb_free[2];     // [column half] scratch read (32 arrivals)
-    uint64_t drain;
+    uint64_t d_full[2 * kIssuers];  // [issuer, buffer] accumulation chunk complete
+    uint64_t d_free[2 * kIssuers];  // [issuer, buffer] chunk folded (kFoldThreads arrivals)
+    uint64_t drain[kIssuers];
     uint32_t tmem_base;
     int32_t abort;
 };
@@ -153,9 +147,7 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, Contro
 }
 // roles and barriers of the where code
 enum : uint32_t { kWhoProducer = 1, kWhoIssuer = 2, kWhoConverter = 4, kWhoFolder = 6 };
-enum : uint32_t {
-    kBarFull = 1, kBarConv = 2, kBarEmpty = 3, kBarDFull = 4, kBarDFree = 5, kBarComb = 6
-};
+enum : uint32_t { kBarFull = 1, kBarConv = 2, kBarEmpty = 3, kBarDFull = 4, kBarDFree = 5 };
 __device__ __forceinline__ uint32_t where_code(uint32_t who, uint32_t bar, uint32_t g) {
     return (who << 24) | (bar << 16) | (g & 0x7fffu);
 }
@@ -235,13 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&ctl->conv[i], kGroupThreads);
             mbar_init(&ctl->empty[i], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < 2 * kIssuers; ++b) {
             mbar_init(&ctl->d_full[b], 1);
             mbar_init(&ctl->d_free[b], kFoldThreads);
-            mbar_init(&ctl->comb_full[b], 32);
-            mbar_init(&ctl->comb_free[b], 32);
         }
-        mbar_init(&ctl->drain, 1);
+        for (int i = 0; i < kIssuers; ++i) mbar_init(&ctl->drain[i], 1);
         ctl->abort = 0;
     }
     fence_barrier_init();
@@ -286,183 +276,162 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait(&ctl->full[h % kStages], (h / kStages) & 1u, kStatusInGemmDecodeTc);
             }
         }
-    } else if (warp == kIssuerWarp) {
+    } else if (warp >= kIssuerWarp) {
         // ------------------------------------------------------------------ MMAs
+        // The CTA's units fall into accumulation chunks (kChunk stages, or
+        // fewer at a tile's end); chunk q is issued by issuer q % 2 into its
+        // own pair of accumulators, so that two threads issue: a tcgen05.mma
+        // takes about as long to issue as one of these small ones takes to run.
+        const uint32_t me = uint32_t(warp - kIssuerWarp);
         if (lane == 0) {
-            uint32_t q = 0;  // accumulation chunks started
+            // The operands' descriptors, built once: a descriptor's start
+            // address is its low 14 bits in 16-byte units and shared-memory
+            // addresses stay below 2^18, so a slot's or a K step's operand is
+            // the base descriptor plus its byte offset / 16 (no carry out of
+            // the field). A: 8 rows of K start 1 KB into each 32-feature atom;
+            // the atoms of the 128 features are kWAtom apart (leading byte
+            // offset), groups of 4 rows 512 bytes (stride byte offset). B: 8 of
+            // K are 32 bytes into each 128-byte row, 8-row groups 1 KB apart.
+            const uint32_t base = smem_addr(smem);
+            const uint64_t a_hi = tc::sw128_32b_desc(base, kWAtom, 512);
+            const uint64_t a_lo = tc::sw128_32b_desc(base + kWBytes, kWAtom, 512);
+            const uint64_t b_x = tc::sw128_desc(base + 2 * kWBytes, 16, 1024);
+            uint32_t q = 0;  // chunks of the CTA started (both issuers)
+            uint32_t s = 0, phase = 0;  // ring slot of unit g and its phase
             bool issued_mma = false;
             UnitWalk walk(u0, p.spt);
             for (uint32_t g = 0; g < nu; ++g) {
                 const int jj = walk.next(g, nu, p.spt);
                 const bool first = walk.chunk_first(jj), last = walk.chunk_last(jj);
-                const uint32_t s = g % kStages, buf = q & 1u;
-                if (!wait_or_abort(&ctl->conv[s], (g / kStages) & 1u, ctl,
-                                   where_code(kWhoIssuer, kBarConv, g))) {
-                    break;
-                }
-                if (first && q >= 2 &&
-                    !wait_or_abort(&ctl->d_free[buf], ((q >> 1) - 1) & 1u, ctl,
-                                   where_code(kWhoIssuer, kBarDFree, g))) {
-                    break;
-                }
-                tc::fence_after_sync();
-                const uint32_t w_hi = smem_addr(smem + s * kStageBytes);
-                const uint32_t w_lo = w_hi + kWBytes;
-                const uint32_t a = tmem + kColA + s * uint32_t(kStageK);
-                const uint32_t d = tmem + kColD + buf * uint32_t(kTileN);
+                if ((q % kIssuers) == me) {
+                    const uint32_t lq = q / kIssuers;  // this issuer's chunk count
+                    const uint32_t ib = me * 2u + (lq & 1u);
+                    if (!wait_or_abort(&ctl->conv[s], phase, ctl,
+                                       where_code(kWhoIssuer, kBarConv, g))) {
+                        break;
+                    }
+                    if (first && lq >= 2 &&
+                        !wait_or_abort(&ctl->d_free[ib], ((lq >> 1) - 1) & 1u, ctl,
+                                       where_code(kWhoIssuer, kBarDFree, g))) {
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint64_t so = uint64_t(s * (kStageBytes >> 4));
+                    const uint32_t d = tmem + ib * kColsD;
 #pragma unroll
-                for (int kk = 0; kk < kStageK / 8; ++kk) {
-                    // 8 rows of K start 1 KB into each 32-feature atom; the atoms
-                    // of the 128 features are kWAtom apart (leading byte offset),
-                    // groups of 4 rows 512 bytes (stride byte offset)
-                    const uint32_t off = uint32_t(kk) * 1024u;
-                    tc::mma_tf32_ts(d, a + uint32_t(kk) * 8u, tc::sw128_32b_desc(w_hi + off, kWAtom, 512),
-                                    kIdesc, !first || kk > 0);
-                    tc::mma_tf32_ts(d, a + uint32_t(kk) * 8u, tc::sw128_32b_desc(w_lo + off, kWAtom, 512),
-                                    kIdesc, true);
+                    for (int kk = 0; kk < kStageK / 8; ++kk) {
+                        const uint64_t b = b_x + so + uint64_t(kk * (32 >> 4));
+                        const uint64_t ka = so + uint64_t(kk * (1024 >> 4));
+                        tc::mma_tf32(d, a_hi + ka, b, kIdescBoth, !first || kk > 0);
+                        tc::mma_tf32(d, a_lo + ka, b, kIdescHi, true);
+                    }
+                    tc::commit(&ctl->empty[s]);
+                    if (last) tc::commit(&ctl->d_full[ib]);
+                    issued_mma = true;
                 }
-                tc::commit(&ctl->empty[s]);
-                if (last) {
-                    tc::commit(&ctl->d_full[buf]);
-                    ++q;
+                if (last) ++q;
+                if (++s == uint32_t(kStages)) {
+                    s = 0;
+                    phase ^= 1u;
                 }
-                issued_mma = true;
             }
             // issued MMAs complete before the TMEM is freed (bounded wait)
             if (issued_mma) {
-                tc::commit(&ctl->drain);
-                mbar_wait(&ctl->drain, 0, kStatusInGemmDecodeTc);
+                tc::commit(&ctl->drain[me]);
+                mbar_wait(&ctl->drain[me], 0, kStatusInGemmDecodeTc);
             }
         }
-    } else if (warp < 8) {
+    } else if (warp < kFoldWarp0) {
         // ------------------------------------------------------------ converters
-        const int grp = warp / 4, quarter = warp % 4;
+        const int grp = warp / 4;
         const int r = tid % kGroupThreads;
         for (uint32_t g = uint32_t(grp); g < nu; g += 2) {
             const uint32_t s = g % kStages;
-            // the stage's previous MMAs (which read this A buffer) completed
-            // before its copies were issued; the wait on `empty` states it
+            // a slot is reloaded only after the MMAs that read its previous
+            // contents completed (the producer waits on `empty`)
             if (!wait_warp(&ctl->full[s], (g / kStages) & 1u, ctl,
-                           where_code(kWhoConverter + uint32_t(grp), kBarFull, g)) ||
-                (g >= uint32_t(kStages) &&
-                 !wait_warp(&ctl->empty[s], ((g / kStages) - 1) & 1u, ctl,
-                            where_code(kWhoConverter + uint32_t(grp), kBarEmpty, g)))) {
+                           where_code(kWhoConverter + uint32_t(grp), kBarFull, g))) {
                 break;
             }
             unsigned char* st = smem + s * kStageBytes;
+            // W then X (4 KB after W_lo) -> their lo parts, all loads first
             const float4* w = reinterpret_cast<const float4*>(st);
             float4* wl = reinterpret_cast<float4*>(st + kWBytes);
+            const float4* x = reinterpret_cast<const float4*>(st + 2 * kWBytes);
+            float4* xl = reinterpret_cast<float4*>(st + 2 * kWBytes + kXBytes);
+            constexpr int kW4 = int(kWBytes / 16) / kGroupThreads;  // float4 of W per thread
+            constexpr int kX4 = int(kXBytes / 16) / kGroupThreads;  // and of X
+            float4 v[kW4 + kX4];
 #pragma unroll
-            for (int i = 0; i < int(kWBytes / 16) / kGroupThreads; ++i) {
-                const float4 v = w[r + i * kGroupThreads];
-                wl[r + i * kGroupThreads] =
-                    make_float4(lo_part(v.x), lo_part(v.y), lo_part(v.z), lo_part(v.w));
-            }
-            if (quarter < 2) {
-                // row `lane` of the X tile (128-byte swizzle: chunk c of row t at
-                // position c ^ (t % 8)) into TMEM lane 32 quarter + lane
-                const float4* xr = reinterpret_cast<const float4*>(st + 2 * kWBytes) + lane * 8;
-                float v[kStageK];
+            for (int i = 0; i < kW4; ++i) v[i] = w[r + i * kGroupThreads];
 #pragma unroll
-                for (int c = 0; c < kStageK / 4; ++c) {
-                    float4 x = xr[c ^ (lane & 7)];
-                    if (quarter == 1) {
-                        x = make_float4(lo_part(x.x), lo_part(x.y), lo_part(x.z), lo_part(x.w));
-                    }
-                    v[4 * c] = x.x;
-                    v[4 * c + 1] = x.y;
-                    v[4 * c + 2] = x.z;
-                    v[4 * c + 3] = x.w;
+            for (int i = 0; i < kX4; ++i) v[kW4 + i] = x[r + i * kGroupThreads];
+#pragma unroll
+            for (int i = 0; i < kW4 + kX4; ++i) {
+                const float4 lo =
+                    make_float4(lo_part(v[i].x), lo_part(v[i].y), lo_part(v[i].z), lo_part(v[i].w));
+                if (i < kW4) {
+                    wl[r + i * kGroupThreads] = lo;
+                } else {
+                    xl[r + (i - kW4) * kGroupThreads] = lo;
                 }
-                tc::fence_after_sync();
-                tc::tmem_st32(tmem + kColA + s * uint32_t(kStageK) + (uint32_t(quarter * 32) << 16), v);
-                tc::tmem_st_wait();
             }
             tc::fence_async_smem();
-            tc::fence_before_sync();
             mbar_arrive(&ctl->conv[s]);
         }
-    } else {
+    } else if (warp < kFoldWarp0 + 4) {
         // ------------------------------------------------- accumulation, epilogue
-        // warps 8, 12: X_hi rows (TMEM lanes 0-31); 9, 13: X_lo rows (32-63);
-        // 8, 9 columns 0-63 of the tile, 12, 13 columns 64-127
-        const bool lo_rows = (warp % 4) == 1;
-        const int half = warp >= 12 ? 1 : 0;
+        // thread = output feature 32 (warp % 4) + lane of the tile (its TMEM lane)
+        const int f = (warp % 4) * 32 + lane;
         const uint32_t lane_off = uint32_t((warp % 4) * 32) << 16;
-        float* scratch = reinterpret_cast<float*>(smem + kOffScratch + half * kScratchBytes);
-        float acc[64];
+        float acc[kBT];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) acc[i] = 0.f;
-        uint32_t q = 0, e = 0;  // chunks folded, segments finished
+        for (int i = 0; i < kBT; ++i) acc[i] = 0.f;
+        uint32_t q = 0;  // chunks folded, in the CTA's order (issuer q % 2)
         UnitWalk walk(u0, p.spt);
         for (uint32_t g = 0; g < nu; ++g) {
             const int jj = walk.next(g, nu, p.spt);
             if (!walk.chunk_last(jj)) continue;
-            const uint32_t buf = q & 1u;
-            if (!wait_warp(&ctl->d_full[buf], (q >> 1) & 1u, ctl,
+            const uint32_t lq = q / kIssuers;
+            const uint32_t ib = (q % kIssuers) * 2u + (lq & 1u);
+            if (!wait_warp(&ctl->d_full[ib], (lq >> 1) & 1u, ctl,
                            where_code(kWhoFolder, kBarDFull, q))) {
                 break;
             }
             tc::fence_after_sync();
+            float hi[kBT], lo[kBT];
+            tc::tmem_ld32(tmem + ib * kColsD + lane_off, hi);
+            tc::tmem_ld32(tmem + ib * kColsD + kBT + lane_off, lo);
+            tc::tmem_ld_wait();
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float v[32];
-                tc::tmem_ld32(tmem + kColD + buf * uint32_t(kTileN) + uint32_t(half * 64 + c * 32) +
-                                  lane_off,
-                              v);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) acc[c * 32 + i] += v[i];
-            }
+            for (int i = 0; i < kBT; ++i) acc[i] += hi[i] + lo[i];
             tc::fence_before_sync();
-            mbar_arrive(&ctl->d_free[buf]);
+            mbar_arrive(&ctl->d_free[ib]);
             ++q;
             if (!walk.seg_end(jj)) continue;
-            // the tile's segment is complete: the X_lo rows' sums join the X_hi rows'
-            if (lo_rows) {
-                if (e >= 1 && !wait_warp(&ctl->comb_free[half], (e - 1) & 1u, ctl,
-                                         where_code(kWhoFolder, kBarComb, e))) {
-                    break;
-                }
+            // the tile's segment is complete: write its column f for every row
+            const int64_t tile = walk.tile;
+            const int64_t c_first = owner(tile * p.spt, p.units, p.ctas);
+            const int64_t c_last = owner((tile + 1) * p.spt - 1, p.units, p.ctas);
+            const int64_t col = (tile % p.n_tiles) * kTileN + f;
+            if (c_first == c_last) {
+                if (col < p.n) {
+                    float* o = out_of(p, int(tile / p.n_tiles)) + col;
 #pragma unroll
-                for (int i = 0; i < 64; ++i) scratch[lane * kScratchStride + i] = acc[i];
-                mbar_arrive(&ctl->comb_full[half]);
-            } else {
-                if (!wait_warp(&ctl->comb_full[half], e & 1u, ctl,
-                               where_code(kWhoFolder, kBarComb, e))) {
-                    break;
-                }
-#pragma unroll
-                for (int i = 0; i < 64; ++i) acc[i] += scratch[lane * kScratchStride + i];
-                mbar_arrive(&ctl->comb_free[half]);
-                const int64_t tile = walk.tile;
-                const int64_t c_first = owner(tile * p.spt, p.units, p.ctas);
-                const int64_t c_last = owner((tile + 1) * p.spt - 1, p.units, p.ctas);
-                const int64_t col0 = (tile % p.n_tiles) * kTileN + half * 64;
-                if (lane < p.m) {
-                    if (c_first == c_last) {
-                        float* o = out_of(p, int(tile / p.n_tiles)) + int64_t(lane) * p.ldc + col0;
-#pragma unroll
-                        for (int i = 0; i < 64; ++i) {
-                            if (col0 + i < p.n) apply(o + i, acc[i], p.epilogue);
-                        }
-                    } else {
-                        float4* part = reinterpret_cast<float4*>(
-                            p.partial +
-                            ((tile * p.max_seg + (int64_t(blockIdx.x) - c_first)) * kBT + lane) *
-                                kTileN +
-                            half * 64);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            part[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2],
-                                                  acc[4 * i + 3]);
-                        }
+                    for (int t = 0; t < kBT; ++t) {
+                        if (t < p.m) apply(o + int64_t(t) * p.ldc, acc[t], p.epilogue);
                     }
                 }
-            }
-            ++e;
+            } else {
+                float* part = p.partial +
+                              (tile * p.max_seg + (int64_t(blockIdx.x) - c_first)) * kBT * kTileN + f;
 #pragma unroll
-            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+                for (int t = 0; t < kBT; ++t) {
+                    if (t < p.m) part[int64_t(t) * kTileN] = acc[t];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kBT; ++i) acc[i] = 0.f;
         }
     }
     tc::fence_before_sync();
