@@ -19,7 +19,7 @@
 // the same layout. Column t + 32 (W X_lo) is added to column t at the fold.
 //
 // Per stage (32 rows of K), with 15 warps per CTA (one CTA per SM):
-//   warp 12, lane 0: the TMA copies into a 5-stage ring (W tile 32 x 128 fp32
+//   warp 12: the TMA copies into a 5-stage ring, one per lane (W tile 32 x 128 fp32
 //     as four 32-column boxes in the 128-byte swizzle with 32-byte granules,
 //     the layout of an MN-major tf32 operand; X tile 32 rows x 32 fp32,
 //     128-byte swizzle; no multicast);
@@ -246,32 +246,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------------------ TMA copies
-        if (lane == 0) {
-            uint32_t loaded = 0;
-            int tile = int(u0 / p.spt), stage = int(u0 % p.spt);
-            for (uint32_t g = 0; g < nu; ++g) {
-                const uint32_t s = g % kStages;
-                if (g >= uint32_t(kStages) &&
-                    !wait_or_abort(&ctl->empty[s], ((g / kStages) - 1) & 1u, ctl,
-                                   where_code(kWhoProducer, kBarEmpty, g))) {
-                    break;
-                }
-                unsigned char* st = smem + s * kStageBytes;
-                mbar_arrive_expect_tx(&ctl->full[s], kWBytes + kXBytes);
-                const int x0 = (tile % p.n_tiles) * kTileN, y = stage * kStageK;
-#pragma unroll
-                for (int a = 0; a < kTileN / 32; ++a) {
-                    tma_load_3d(st + a * kWAtom, &wmap, x0 + a * 32, y, tile / p.n_tiles,
-                                &ctl->full[s]);
-                }
-                tc::tma_load_2d(st + 2 * kWBytes, &xmap, y, 0, &ctl->full[s]);
-                loaded = g + 1;
-                if (++stage == p.spt) {
-                    stage = 0;
-                    ++tile;
-                }
+        // a stage's five copies (four W atoms, the X tile) go one to a lane,
+        // so that they leave as one warp instruction
+        uint32_t loaded = 0;
+        int tile = int(u0 / p.spt), stage = int(u0 % p.spt);
+        for (uint32_t g = 0; g < nu; ++g) {
+            const uint32_t s = g % kStages;
+            if (g >= uint32_t(kStages) &&
+                !wait_warp(&ctl->empty[s], ((g / kStages) - 1) & 1u, ctl,
+                           where_code(kWhoProducer, kBarEmpty, g))) {
+                break;
             }
-            // copies in flight land before the CTA ends (bounded waits)
+            unsigned char* st = smem + s * kStageBytes;
+            if (lane == 0) mbar_arrive_expect_tx(&ctl->full[s], kWBytes + kXBytes);
+            __syncwarp();
+            const int x0 = (tile % p.n_tiles) * kTileN, y = stage * kStageK;
+            if (lane < kTileN / 32) {
+                tma_load_3d(st + lane * kWAtom, &wmap, x0 + lane * 32, y, tile / p.n_tiles,
+                            &ctl->full[s]);
+            } else if (lane == kTileN / 32) {
+                tc::tma_load_2d(st + 2 * kWBytes, &xmap, y, 0, &ctl->full[s]);
+            }
+            __syncwarp();
+            loaded = g + 1;
+            if (++stage == p.spt) {
+                stage = 0;
+                ++tile;
+            }
+        }
+        // copies in flight land before the CTA ends (bounded waits)
+        if (lane == 0) {
             for (uint32_t h = loaded > uint32_t(kStages) ? loaded - kStages : 0; h < loaded; ++h) {
                 mbar_wait(&ctl->full[h % kStages], (h / kStages) & 1u, kStatusInGemmDecodeTc);
             }

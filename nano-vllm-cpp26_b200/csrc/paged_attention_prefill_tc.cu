@@ -26,8 +26,8 @@
 //              is queued while the softmax works on S(t); O(t) += P(t) V(t) once
 //              P(t) is in TMEM.
 //   warp 5     loader: the TMA gathers of the K and V tiles into a 3-stage ring,
-//              lanes 0-3 one physical block each (4 swizzle atoms per tensor),
-//              up to three tiles ahead of the MMAs.
+//              one 2 KiB box (a block's 16 rows of one 32-dim atom of K or V)
+//              per lane, up to three tiles ahead of the MMAs.
 //   warps 6-11 converters: turn each landed fp32 K tile, then V tile, in place,
 //              into its two bf16 terms, zeroing the V rows of keys past the
 //              visible ones; S waits only for K's terms, O for V's.
@@ -368,36 +368,41 @@ prefill_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap kmap,
 
         if (warp == kLoaderWarp) {
             // ------------------------------------------------------------------ loader
-            // Tile t's four blocks go to lanes 0-3, each issuing its block's eight
-            // boxes; the stage is free once O of its earlier tile completed (S
-            // read its K before).
+            // A tile's 32 boxes (4 blocks x 4 atoms x K, V) go one to a lane,
+            // so that they leave as one warp instruction (a thread issuing its
+            // copies one after another pays the issue cost of each): lane l
+            // copies block l / 8, tensor (l / 4) % 2, atom l % 4. The block ids
+            // of the item's next tiles are read a tile ahead. The stage is free
+            // once O of its earlier tile completed (S read its K before).
             const int32_t* table = p.block_tables + int64_t(s) * p.max_blocks;
+            const int lb = lane >> 3, lt = (lane >> 2) & 1, la = lane & 3;
+            auto block_of = [&](int t) -> int64_t {
+                const int kb = t * kKT;
+                const int nb = t < ntiles ? (min(kKT, nk - kb) + 15) / 16 : 0;
+                return lb < nb ? int64_t(table[kb / 16 + lb]) : int64_t(-1);
+            };
+            int64_t blk_next = block_of(0);
             for (int t = 0; t < ntiles; ++t) {
                 const uint32_t n = n0 + t;
                 const uint32_t st = stage_of(n);
+                const int64_t blk = blk_next;
+                blk_next = block_of(t + 1);
                 if (n >= uint32_t(kStages) && !wait_all(&ctl->st_free[st], stage_parity(n - kStages))) {
                     break;
                 }
                 const int kbase = t * kKT;
                 const int nblk = (min(kKT, nk - kbase) + 15) / 16;
-                int64_t blk = -1;
-                if (lane < nblk) blk = table[kbase / 16 + lane];
-                const bool valid = lane < nblk && blk >= 0 && blk < g.num_blocks;
+                const bool valid = lb < nblk && blk >= 0 && blk < g.num_blocks;
+                // a block's 8 boxes are 16 KiB; the lanes of one block agree
                 const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
-                if (lane == 0) mbar_arrive_expect_tx(&ctl->kv_full[st], uint32_t(__popc(vmask)) * 16384u);
+                if (lane == 0) mbar_arrive_expect_tx(&ctl->kv_full[st], uint32_t(__popc(vmask)) * 2048u);
                 __syncwarp();
-                if (lane < nblk && !valid) raise_status(kStatusBounds);
+                if (lb < nblk && !valid && (lane & 7) == 0) raise_status(kStatusBounds);
                 if (valid) {
-                    unsigned char* sK = sKV + st * kStageBytes;
-                    unsigned char* sV = sK + kTileBytes;
+                    unsigned char* dst = sKV + st * kStageBytes + lt * kTileBytes +
+                                         f32_atom_offset(la) + uint32_t(lb) * 2048u;
                     const int y = int((blk * g.num_layers + p.layer) * 16);
-#pragma unroll
-                    for (int a = 0; a < 4; ++a) {
-                        const int x = h * kHD + a * 32;
-                        const uint32_t off = f32_atom_offset(a) + uint32_t(lane) * 2048u;
-                        tc::tma_load_2d(sK + off, &kmap, x, y, &ctl->kv_full[st]);
-                        tc::tma_load_2d(sV + off, &vmap, x, y, &ctl->kv_full[st]);
-                    }
+                    tc::tma_load_2d(dst, lt ? &vmap : &kmap, h * kHD + la * 32, y, &ctl->kv_full[st]);
                 }
                 __syncwarp();
                 next_load = n + 1;
