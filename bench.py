@@ -1208,9 +1208,11 @@ def serve_router_main(args):
     samplers = [ClockSampler(smi_device_id(d)).start() for d in range(n_gpu)]
 
     def one_run(run: int):
+        # the stream arrives as one burst: placed in one call, each GPU woken
+        # once with its whole share
         base = (run + 1) * 1_000_000
-        for i, (p_, m_) in enumerate(zip(spec.prompts, spec.max_new)):
-            router.add_request(base + i, p_, m_)
+        router.add_requests([base + i for i in range(len(spec.prompts))], spec.prompts,
+                            spec.max_new)
         router.wait_idle()
 
     for r in range(args.warmup):

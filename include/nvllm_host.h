@@ -283,6 +283,19 @@ int nvllm_router_create(nvllm_generator* const* gens, int32_t n, nvllm_router** 
 void nvllm_router_destroy(nvllm_router* r);
 int nvllm_router_add_request(nvllm_router* r, uint64_t seq_id, const int64_t* prompt,
                              int64_t prompt_len, int64_t max_new_tokens, int32_t* gpu);
+/* A burst of n requests in one call: request k's prompt is
+ * tokens[offsets[k] .. offsets[k + 1]) (offsets has n + 1 entries), its
+ * completion max_new_tokens[k]. Placed in one decision pass, each on the GPU
+ * that is least loaded counting those placed before it in the burst, then each
+ * GPU is woken once, so that its engine thread takes its whole share in its
+ * next iteration (placing a burst one call at a time while the engines run
+ * spreads it over many small iterations). All or nothing: an id in use or
+ * repeated places none (NVLLM_ERR_INVALID). gpus, when not NULL, receives each
+ * request's GPU. No counterpart in the reference, whose engine takes one
+ * request per submit (src/engine.cpp:89-104); this is a batch form of it. */
+int nvllm_router_add_requests(nvllm_router* r, int64_t n, const uint64_t* seq_ids,
+                              const int64_t* tokens, const int64_t* offsets,
+                              const int64_t* max_new_tokens, int32_t* gpus);
 /* Blocks until every GPU is idle with an empty queue; the error of a GPU whose
  * loop failed (its thread stops; the others carry on). */
 int nvllm_router_wait_idle(nvllm_router* r);

@@ -555,6 +555,30 @@ int nvllm_router_add_request(nvllm_router* r, uint64_t seq_id, const int64_t* pr
     return NVLLM_OK;
 }
 
+int nvllm_router_add_requests(nvllm_router* r, int64_t n, const uint64_t* seq_ids,
+                              const int64_t* tokens, const int64_t* offsets,
+                              const int64_t* max_new_tokens, int32_t* gpus) {
+    if (r == nullptr || n < 0 || (n > 0 && (seq_ids == nullptr || tokens == nullptr ||
+                                            offsets == nullptr || max_new_tokens == nullptr))) {
+        return NVLLM_ERR_INVALID;
+    }
+    if (n == 0) return NVLLM_OK;
+    std::vector<nvllm::SeqId> ids(seq_ids, seq_ids + n);
+    std::vector<std::vector<int64_t>> prompts(static_cast<std::size_t>(n));
+    std::vector<std::size_t> mx(static_cast<std::size_t>(n));
+    for (int64_t k = 0; k < n; ++k) {
+        if (offsets[k] < 0 || offsets[k + 1] < offsets[k]) return NVLLM_ERR_INVALID;
+        if (!make_prompt(tokens + offsets[k], offsets[k + 1] - offsets[k], prompts[k])) {
+            return NVLLM_ERR_INVALID;
+        }
+        mx[k] = std::size_t(std::max<int64_t>(max_new_tokens[k], 1));
+    }
+    auto res = r->impl->add_requests(ids, prompts, mx,
+                                     gpus ? std::span<int32_t>(gpus, std::size_t(n))
+                                          : std::span<int32_t>());
+    return res ? NVLLM_OK : engine_status(res.error());
+}
+
 int nvllm_router_wait_idle(nvllm_router* r) {
     if (r == nullptr) return NVLLM_ERR_INVALID;
     auto res = r->impl->wait_idle();

@@ -1,5 +1,8 @@
 #include "router.hpp"
 
+#include <algorithm>
+#include <unordered_set>
+
 #include <cuda_runtime.h>
 
 #include <limits>
@@ -104,6 +107,61 @@ std::expected<int32_t, EngineError> Router::add_request(SeqId id, std::vector<in
         l.cv.notify_one();
     }
     return best;
+}
+
+std::expected<void, EngineError> Router::add_requests(std::span<const SeqId> ids,
+                                                      std::span<std::vector<int64_t>> prompts,
+                                                      std::span<const std::size_t> max_new,
+                                                      std::span<int32_t> gpus) {
+    const std::size_t n = ids.size();
+    if (prompts.size() != n || max_new.size() != n || (!gpus.empty() && gpus.size() != n) ||
+        lanes_.empty()) {
+        return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+    }
+    std::vector<std::vector<Pending>> per_lane(lanes_.size());
+    std::vector<uint64_t> rows_to(lanes_.size(), 0);
+    {
+        std::lock_guard<std::mutex> lk(route_mu_);
+        std::unordered_set<SeqId> fresh;
+        for (SeqId id : ids) {
+            if (owner_.contains(id) || !fresh.insert(id).second) {
+                return std::unexpected(EngineError{EngineError::Kind::Invalid, 0});
+            }
+        }
+        std::vector<uint64_t> load(lanes_.size());
+        for (std::size_t i = 0; i < lanes_.size(); ++i) {
+            load[i] = lanes_[i]->load.load() + lanes_[i]->queued_rows.load();
+        }
+        for (std::size_t k = 0; k < n; ++k) {
+            std::vector<int64_t>& prompt = prompts[k];
+            if (prompt.empty()) prompt.push_back(1);  // as Sequence does (src/scheduler.cpp:8-20)
+            const std::size_t mx = std::max<std::size_t>(max_new[k], 1);
+            const uint64_t rows = prompt.size() + mx;
+            const auto best = std::size_t(std::min_element(load.begin(), load.end()) - load.begin());
+            load[best] += rows;
+            rows_to[best] += rows;
+            owner_[ids[k]] = int32_t(best);
+            if (!gpus.empty()) gpus[k] = int32_t(best);
+            per_lane[best].push_back(Pending{ids[k], std::move(prompt), mx, {}});
+        }
+        // counted before the requests are visible to the threads
+        for (std::size_t i = 0; i < lanes_.size(); ++i) {
+            if (per_lane[i].empty()) continue;
+            lanes_[i]->queued_rows += rows_to[i];
+            lanes_[i]->placed += per_lane[i].size();
+        }
+    }
+    for (std::size_t i = 0; i < lanes_.size(); ++i) {
+        if (per_lane[i].empty()) continue;
+        Lane& l = *lanes_[i];
+        {
+            std::lock_guard<std::mutex> lq(l.mu);
+            for (Pending& p : per_lane[i]) l.ingress.push_back(std::move(p));
+            l.busy = true;
+        }
+        l.cv.notify_one();
+    }
+    return {};
 }
 
 void Router::signal_idle() {

@@ -68,6 +68,16 @@ public:
     std::expected<int32_t, EngineError> add_request(SeqId id, std::vector<int64_t> prompt,
                                                     std::size_t max_new_tokens,
                                                     std::shared_ptr<TokenStream> stream = {});
+    // Places a burst of requests in one decision pass (each on the GPU that is
+    // least loaded counting the ones placed before it in the burst), then
+    // wakes each GPU once: its engine thread finds its whole share queued
+    // instead of ingesting it over many small iterations. All or nothing:
+    // a seq_id already in use, or repeated in the burst, places none. gpus
+    // (when given) receives each request's GPU.
+    std::expected<void, EngineError> add_requests(std::span<const SeqId> ids,
+                                                  std::span<std::vector<int64_t>> prompts,
+                                                  std::span<const std::size_t> max_new,
+                                                  std::span<int32_t> gpus = {});
     // Blocks until every GPU is idle with an empty ingress queue (or one has
     // failed: its error is returned).
     std::expected<void, EngineError> wait_idle();

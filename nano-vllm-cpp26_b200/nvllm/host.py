@@ -131,6 +131,9 @@ def host_lib() -> ctypes.CDLL:
     L.nvllm_router_destroy.argtypes = [_vp]
     L.nvllm_router_add_request.argtypes = [_vp, ctypes.c_uint64, _i64p, ctypes.c_int64,
                                            ctypes.c_int64, ctypes.POINTER(ctypes.c_int32)]
+    L.nvllm_router_add_requests.argtypes = [_vp, ctypes.c_int64,
+                                            ctypes.POINTER(ctypes.c_uint64), _i64p, _i64p,
+                                            _i64p, _i32p]
     L.nvllm_router_wait_idle.argtypes = [_vp]
     L.nvllm_router_output.restype = ctypes.c_int64
     L.nvllm_router_output.argtypes = [_vp, ctypes.c_uint64, _i64p, ctypes.c_int64]
@@ -627,6 +630,26 @@ class Router:
         if rc != OK:
             raise NvllmError(rc, "nvllm_router_add_request")
         return gpu.value
+
+    def add_requests(self, seq_ids, prompts, max_new_tokens) -> np.ndarray:
+        """Places a burst of requests in one call (one decision pass, each GPU
+        woken once); returns each request's GPU index. All or nothing."""
+        n = len(seq_ids)
+        ids = np.ascontiguousarray(seq_ids, np.uint64)
+        lens = np.array([len(p) for p in prompts], np.int64)
+        offsets = np.zeros(n + 1, np.int64)
+        np.cumsum(lens, out=offsets[1:])
+        tokens = (np.concatenate([np.asarray(p, np.int64) for p in prompts]) if n
+                  else np.zeros(1, np.int64))
+        tokens = np.ascontiguousarray(tokens, np.int64)
+        mx = np.ascontiguousarray(max_new_tokens, np.int64)
+        gpus = np.zeros(max(n, 1), np.int32)
+        rc = self.L.nvllm_router_add_requests(
+            self.h, n, ids.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
+            _ptr(tokens, _i64p), _ptr(offsets, _i64p), _ptr(mx, _i64p), _ptr(gpus, _i32p))
+        if rc != OK:
+            raise NvllmError(rc, "nvllm_router_add_requests")
+        return gpus[:n]
 
     def wait_idle(self) -> None:
         rc = self.L.nvllm_router_wait_idle(self.h)

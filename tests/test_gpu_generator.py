@@ -105,14 +105,16 @@ def test_generator_step_by_step_and_preemption_count():
         eng.close()
 
 
+@pytest.mark.parametrize("burst", [False, True])
 @pytest.mark.parametrize("lanes", [2, 3])
-def test_router_serves_every_request_with_the_reference_stream(lanes):
+def test_router_serves_every_request_with_the_reference_stream(lanes, burst):
     """The reference benchmark's 96 requests through nvllm_router over several
     generators, each with its own engine (arena, allocator, scheduler), model
     and engine thread: on distinct GPUs where the box has them, else several on
     cuda:0. Every request finishes on the GPU the router chose with the token
     stream the reference produced for it; the requests spread over the lanes by
-    outstanding work."""
+    outstanding work. Placed one call per request, or as one burst
+    (nvllm_router_add_requests), which is all or nothing."""
     import torch
 
     import nvllm
@@ -138,8 +140,14 @@ def test_router_serves_every_request_with_the_reference_stream(lanes):
             objs.append((eng, model, gen))
         router = Router([g for _, _, g in objs])
         try:
-            placed = [router.add_request(i + 1, p, m)
-                      for i, (p, m) in enumerate(zip(prompts, max_new))]
+            if burst:
+                with pytest.raises(nvllm.NvllmError):  # an id repeated in the burst
+                    router.add_requests([1, 1], prompts[:2], max_new[:2])
+                placed = router.add_requests([i + 1 for i in range(len(prompts))], prompts,
+                                             max_new).tolist()
+            else:
+                placed = [router.add_request(i + 1, p, m)
+                          for i, (p, m) in enumerate(zip(prompts, max_new))]
             router.wait_idle()
             assert sorted(set(placed)) == list(range(lanes))
             for lane in range(lanes):
