@@ -97,6 +97,12 @@ def test_tails_and_strides(impl):
     assert err <= REL, err
     err, _ = run(31, 70, 132, lda_pad=2, ldw_pad=12, impl=impl)
     assert err <= REL, err
+    # n a multiple of 32 but not of 128 (the last tile's atoms past n read as
+    # zero), with and without a padded row stride, one matrix and two
+    err, _ = run(26, 512, 160, impl=impl)
+    assert err <= REL, err
+    err, _ = run(17, 300, 224, ldw_pad=32, batch=2, impl=impl)
+    assert err <= REL, err
 
 
 @pytest.mark.parametrize("impl", IMPLS)
